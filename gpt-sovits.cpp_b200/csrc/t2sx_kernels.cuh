@@ -1,0 +1,79 @@
+// Kernel launchers of the T2S decode path (host-side declarations).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace t2sx {
+
+enum WType : int { W_F32 = 0, W_F16 = 1, W_Q4_0 = 2, W_Q8_0 = 8, W_Q4_K = 12 };
+
+// A linear weight [N rows][K] repacked for the device.
+//   Q8_0: q8 [N][K] int8, d [N][K/32] f32 (the f16 block scales widened)
+//   Q4_0: q4 [N][K/32][16] (ggml nibble order: low nibble j -> element j, high -> j+16), d as Q8_0
+//   Q4_K: q4 [N][K/256][128] (ggml order), d, dmin [N][K/256] f32, scm [N][K/256][16] = the
+//         eight 6-bit sub-block scales then the eight 6-bit mins
+//   F16 : h [N][K];  F32: f [N][K]
+struct DevW {
+    int type = -1, N = 0, K = 0;
+    const int8_t* q8 = nullptr;
+    const uint8_t* q4 = nullptr;
+    const float* d = nullptr;
+    const float* dmin = nullptr;
+    const uint8_t* scm = nullptr;
+    const uint16_t* h = nullptr;
+    const float* f = nullptr;
+};
+
+// Activations converted to a weight type's dot type (ggml vec_dot_type):
+//   Q8_0/Q4_0 weights -> q [M][K] int8 + d [M][K/32] (f16-rounded scales as f32)
+//   Q4_K weights      -> q [M][K] int8 + d [M][K/256] f32 + bs [M][K/32] (sum of each 32 group)
+//   F16 weights       -> h [M][K];  F32 weights -> f [M][K] (the input itself)
+struct ActQ {
+    int8_t* q = nullptr;
+    float* d = nullptr;
+    int32_t* bs = nullptr;
+    uint16_t* h = nullptr;
+    const float* f = nullptr;
+};
+
+// Paged f16 KV cache: page p holds kPage positions of every layer,
+// element (p, layer, kv, head, pos, dim) at
+//   pool[((((p * n_layer + layer) * 2 + kv) * kHeads + head) * kPage + pos) * kHeadDim + dim]
+struct KVView {
+    uint16_t* pool = nullptr;
+    const int32_t* ptab = nullptr;  // [n_slots][max_pages]
+    int max_pages = 0;
+    int n_layer = 0;
+};
+
+// Per-row routing of one forward pass (rows = tokens of this pass).
+struct Rows {
+    const int32_t* slot = nullptr;  // [T] slot of the row
+    int32_t* pos = nullptr;         // [T] KV position written by the row
+    int32_t* L = nullptr;           // [T] attended prefix length
+    const int32_t* cap = nullptr;   // [n_slots] capacity (positions) of the slot
+    int32_t* err = nullptr;         // device error flag (bounds)
+};
+
+void quantize_act(int wtype, const float* x, int M, int K, ActQ& a, cudaStream_t st);
+void matmul(const DevW& W, const ActQ& a, int M, const float* bias, int relu, float* y, cudaStream_t st);
+void embed_decode(int T, const int32_t* row_slot, const int32_t* token_in, const int32_t* n_pos,
+                  const int32_t* audio_off, const uint16_t* emb16, const float* emb32, int emb_rows,
+                  const float* pe, int pe_rows, float alpha, Rows rows, float* x, cudaStream_t st);
+void qkv_post(int T, const float* qkv, Rows rows, KVView kv, int layer, uint16_t* q16, cudaStream_t st);
+void attention_decode(int T, const uint16_t* q16, Rows rows, KVView kv, int layer, float scale, float* out,
+                      cudaStream_t st);
+void attention_prefill(int T, const uint16_t* q16, Rows rows, KVView kv, int layer, float scale, float* out,
+                       cudaStream_t st);
+void residual_layernorm(int T, const float* a, const float* b, const float* g, const float* beta, float eps,
+                        float* y, cudaStream_t st);
+void sample_greedy(int T, const float* logits, int V, const int32_t* row_slot, const uint8_t* seen, float rp,
+                   float inv_rp, int eos_mask, int eos, int32_t* tok_out, cudaStream_t st);
+void advance(int T, const int32_t* row_slot, const int32_t* tok, int32_t* token_in, int32_t* n_pos, uint8_t* seen,
+             int V, int32_t* ring, int ring_len, int32_t* ring_step, cudaStream_t st);
+void gather_rows(int n, const float* src, const int32_t* idx, int ld, float* dst, cudaStream_t st);
+void embed_prefill_rows(int T_text, int T_prompt, const int32_t* phones, const int32_t* sem, const float* bert_proj,
+                        const uint16_t* text16, const float* text32, const uint16_t* audio16, const float* audio32,
+                        const float* pe, float alpha_t, float alpha_a, float* x, cudaStream_t st);
+
+}  // namespace t2sx

@@ -1,0 +1,96 @@
+// Device arithmetic of the T2S decode path.
+//
+// Every reduction in the kernels follows one fixed evaluation order so that results are
+// reproducible bit for bit (the CPU oracle restates the same order).  All code here is
+// compiled with --fmad=false: a fused multiply-add appears only where it is written as
+// __fmaf_rn, everything else rounds after each operation.
+#pragma once
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+namespace t2sx {
+
+constexpr int kD = 512;        // d_model
+constexpr int kHeads = 16;
+constexpr int kHeadDim = 32;
+constexpr int kPage = 64;      // KV positions per page
+constexpr int kAttnLanes = 128;  // decode attention: position lanes per (row, head)
+
+// e^x: Cody-Waite reduction x = k*ln2 + r (ln2 split in a 16-bit head and a tail so k*head
+// is exact), e^r from its Taylor series to degree 7 in Horner form with fused multiply-adds,
+// scaled by 2^k assembled from exponent bits.  Arguments <= -87 (and -inf, NaN) give 0; the
+// kernels only evaluate e^(s - max) <= 1.
+__device__ __forceinline__ float t2s_expf(float x) {
+    if (!(x > -87.0f)) return 0.0f;
+    if (x > 88.0f) return __int_as_float(0x7f800000);
+    const float kf = rintf(__fmul_rn(x, 1.44269502162933349609375f));
+    float r = __fmaf_rn(kf, -0.693145751953125f, x);
+    r = __fmaf_rn(kf, -1.428606765330187045037746429443359375e-06f, r);
+    float p = 1.98412701138295233249664306640625e-04f;
+    p = __fmaf_rn(p, r, 1.3888889225199818611145019531250e-03f);
+    p = __fmaf_rn(p, r, 8.3333337679505348205566406250000e-03f);
+    p = __fmaf_rn(p, r, 4.1666667908430099487304687500000e-02f);
+    p = __fmaf_rn(p, r, 1.6666667163372039794921875000000e-01f);
+    p = __fmaf_rn(p, r, 0.5f);
+    p = __fmaf_rn(p, r, 1.0f);
+    p = __fmaf_rn(p, r, 1.0f);
+    const int k = (int)kf;
+    return __fmul_rn(p, __int_as_float((k + 127) << 23));
+}
+
+__device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
+__device__ __forceinline__ uint16_t f2h(float f) { return __half_as_ushort(__float2half_rn(f)); }
+
+// Online softmax state of one attention lane.
+struct AttnState {
+    float m, l, o[kHeadDim];
+};
+
+__device__ __forceinline__ void st_empty(AttnState& s) {
+    s.m = __int_as_float(0xff800000);
+    s.l = 0.0f;
+#pragma unroll
+    for (int d = 0; d < kHeadDim; ++d) s.o[d] = 0.0f;
+}
+
+// Fold one key position (score s, value row v as f32) into the state.
+__device__ __forceinline__ void st_update(AttnState& st, float s, const float* v) {
+    if (s > st.m) {
+        const float t = t2s_expf(__fsub_rn(st.m, s));
+        st.m = s;
+        st.l = __fmaf_rn(st.l, t, 1.0f);
+#pragma unroll
+        for (int d = 0; d < kHeadDim; ++d) st.o[d] = __fmaf_rn(st.o[d], t, v[d]);
+    } else {
+        const float t = t2s_expf(__fsub_rn(s, st.m));
+        st.l = __fadd_rn(st.l, t);
+#pragma unroll
+        for (int d = 0; d < kHeadDim; ++d) st.o[d] = __fmaf_rn(t, v[d], st.o[d]);
+    }
+}
+
+// Symmetric merge of two states: merge(A,B) == merge(B,A) bit for bit.
+__device__ __forceinline__ void st_merge_scalars(float mA, float lA, float mB, float lB, float& M, float& a,
+                                                 float& b, float& l, bool& empty) {
+    M = fmaxf(mA, mB);
+    empty = (M == __int_as_float(0xff800000));
+    a = empty ? 0.0f : t2s_expf(__fsub_rn(mA, M));
+    b = empty ? 0.0f : t2s_expf(__fsub_rn(mB, M));
+    l = empty ? 0.0f : __fadd_rn(__fmul_rn(lA, a), __fmul_rn(lB, b));
+}
+
+// 32-term dot of an f16-rounded query (as f32) with an f16 key row: four sequential fma
+// chains of 8 terms (the products of two f16 values are exact in f32), summed pairwise.
+__device__ __forceinline__ float dot32(const float* q, const float* k) {
+    float c[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        float s = 0.0f;
+#pragma unroll
+        for (int d = 8 * j; d < 8 * j + 8; ++d) s = __fmaf_rn(q[d], k[d], s);
+        c[j] = s;
+    }
+    return __fadd_rn(__fadd_rn(c[0], c[1]), __fadd_rn(c[2], c[3]));
+}
+
+}  // namespace t2sx

@@ -1,0 +1,147 @@
+/*
+ * t2sx -- C ABI of the B200 T2S decode path (libt2sx.so).
+ *
+ * Drop-in for the model/session layer of GPT-SoVITS.cpp's T2S path (src/t2s) without a ggml
+ * backend: it reads the GGUF files written by python/convert_t2s_to_gguf.py unchanged and runs
+ * the prefill and the autoregressive decode step on one CUDA device.  Plain pointers and sizes
+ * only; every function returns a status (T2SX_OK == 0) and t2sx_last_error() describes the
+ * last failure of the calling thread.  Citations name the reference interface each entry point
+ * replaces (include/gpt_sovits/t2s.h, src/t2s/*.cpp).
+ *
+ * Threading: a session is a single-owner object (as t2s_session is); different sessions may be
+ * driven from different host threads.  All device work of a session runs on its own stream.
+ */
+#ifndef T2SX_H
+#define T2SX_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define T2SX_API __attribute__((visibility("default")))
+#else
+#define T2SX_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define T2SX_OK 0
+#define T2SX_ERR_INVALID 1   /* bad argument / plan (reference: false return or GGML_ASSERT) */
+#define T2SX_ERR_IO 2        /* file missing or unreadable (t2s_model_load returns false) */
+#define T2SX_ERR_FORMAT 3    /* GGUF malformed, tensor missing or unsupported type */
+#define T2SX_ERR_CUDA 4      /* CUDA runtime failure */
+#define T2SX_ERR_OOM 5       /* device memory exhausted */
+#define T2SX_ERR_STATE 6     /* illegal slot transition (reference aborts via GGML_ASSERT) */
+#define T2SX_ERR_BOUNDS 7    /* a slot ran past its capacity (device-side check) */
+
+typedef struct t2sx_model t2sx_model;
+typedef struct t2sx_session t2sx_session;
+
+/* Sampler parameters, bound at session creation (t2s_sampler_config, t2s.h:279-284).
+ * eos_mask != 0 sets logit[eos] = -inf after the repetition penalty (not in the reference
+ * sampler; used to decode fixed-length sequences). */
+typedef struct t2sx_sampler_config {
+    int32_t top_k;
+    float top_p;
+    float temperature;
+    float repetition_penalty;
+    int32_t eos_mask;
+} t2sx_sampler_config;
+
+T2SX_API const char* t2sx_last_error(void);
+T2SX_API int t2sx_version(void);
+T2SX_API int t2sx_device_count(int32_t* n);
+
+/* t2s_model_load / t2s_model_free (t2s.h:269-272, src/t2s/loader.cpp:140-240): parse the GGUF,
+ * read hparams with the reference defaults (loader.cpp:39-50), repack every linear weight into
+ * the device layout and upload it to `device`. */
+T2SX_API int t2sx_model_load(const char* path, int32_t device, t2sx_model** out);
+T2SX_API void t2sx_model_free(t2sx_model* model);
+/* hp[9] = embedding_dim, hidden_dim, n_head, linear_units, n_layer, vocab_size,
+ * phoneme_vocab_size, eos, inter_channels (t2s_hparams, t2s.h:215-225);
+ * wtypes[4] = ggml types of qkv_w, lm_head_w, audio_embedding, bert_proj_w. */
+T2SX_API int t2sx_model_hparams(const t2sx_model* model, uint32_t* hp, int32_t* wtypes);
+/* Device bytes held by the model's weights. */
+T2SX_API int t2sx_model_device_bytes(const t2sx_model* model, uint64_t* bytes);
+
+/* t2s_session_init / t2s_session_free (t2s.h:385-394, session.cpp:55-213).  n_slots concurrent
+ * sequences, slot_size positions each; the KV cache is paged f16 (64 positions per page, all
+ * layers) sized n_slots * ceil(slot_size / 64) pages.  n_slots == 0 or slot_size == 0 ->
+ * T2SX_ERR_INVALID (session.cpp:64-67). */
+T2SX_API int t2sx_session_create(const t2sx_model* model, uint32_t n_slots, uint32_t slot_size,
+                        const t2sx_sampler_config* cfg, t2sx_session** out);
+T2SX_API void t2sx_session_free(t2sx_session* s);
+/* t2s_session_find_free_slot (t2s.h:400, session.cpp:215-222): first slot with n_pos == 0, or -1. */
+T2SX_API int t2sx_session_find_free_slot(const t2sx_session* s);
+/* t2s_session_slot_release (t2s.h:404, session.cpp:224-240). */
+T2SX_API int t2sx_session_slot_release(t2sx_session* s, int32_t slot);
+/* t2s_session_slot_n_pos (t2s.h:418, session.cpp:242-245); -1 for a bad slot. */
+T2SX_API int t2sx_session_slot_n_pos(const t2sx_session* s, int32_t slot);
+T2SX_API int t2sx_session_slot_audio_offset(const t2sx_session* s, int32_t slot);
+/* Device bytes held by the session (KV pages and work buffers). */
+T2SX_API int t2sx_session_device_bytes(const t2sx_session* s, uint64_t* bytes);
+
+/* Prefill input rows for one prompt (t2s_embed_input_forward / t2s_embed_ref_forward text and
+ * audio parts, block.cpp:424-511): text rows [0, T_text) from phoneme ids and BERT features
+ * (f32 [T_text][1024]) with PE from position 0, then audio rows from prompt semantic ids with PE
+ * from position 0.  Inputs are host pointers; x_out (f32 [T_text+T_prompt][d]) is a host
+ * pointer, or a device pointer when x_out_on_device != 0. */
+T2SX_API int t2sx_embed_prefill(t2sx_session* s, const int32_t* phones, const float* bert, int32_t T_text,
+                       const int32_t* sem, int32_t T_prompt, float* x_out, int32_t x_out_on_device);
+
+/* Prefill of n idle slots in one pass (t2s_session_build_flex_graph + t2s_session_flex_advance
+ * with prefill-only plans, session.cpp:461-859): slot[i] receives n_query[i] rows of x (rows of
+ * all slots concatenated in the given order, f32 [sum n_query][d]; host pointer, or device
+ * pointer when x_on_device != 0).  t_prompt[i] is the slot's ref_T_prompt: rows
+ * [0, n_query - t_prompt) are text (bidirectional among text), the rest audio (causal).  Sets
+ * n_pos = n_query and audio_offset = n_query - t_prompt; writes each slot's first token (greedy
+ * on the last row) to tokens_out[i] (host, may be NULL).  A busy slot, n_query < t_prompt or
+ * n_query > slot_size -> T2SX_ERR_STATE / T2SX_ERR_INVALID. */
+T2SX_API int t2sx_prefill(t2sx_session* s, int32_t n, const int32_t* slots, const int32_t* n_query,
+                 const int32_t* t_prompt, const float* x, int32_t x_on_device, int32_t* tokens_out);
+
+/* Decode (t2s_session_decode_advance + the persistent decode graph, session.cpp:247-396):
+ * n_steps steps over every active slot (n_pos > 0); each step embeds the slot's current token,
+ * runs the 24 layers and the sampler and feeds the sampled token back, all on the device (one
+ * CUDA graph per step).  tokens_out (host, may be NULL) receives [n_steps][n_active] tokens in
+ * slot order.  Any active slot reaching slot_size -> T2SX_ERR_BOUNDS before any work. */
+T2SX_API int t2sx_decode(t2sx_session* s, int32_t n_steps, int32_t* tokens_out);
+/* Enqueue n_steps decode steps without waiting (tokens stay on the device). */
+T2SX_API int t2sx_decode_async(t2sx_session* s, int32_t n_steps);
+T2SX_API int t2sx_synchronize(t2sx_session* s);
+/* One step driven from host buffers, the reference's decode loop shape
+ * (test_t2s_infer.cpp:364-421): tokens_in[n_active] are copied to the device, one step runs,
+ * tokens_out[n_active] are copied back.  Either pointer may be NULL (device tokens are used /
+ * nothing is copied back). */
+T2SX_API int t2sx_decode_step_host(t2sx_session* s, const int32_t* tokens_in, int32_t* tokens_out);
+/* Active slots in row order (size >= n_slots); returns their count via *n. */
+T2SX_API int t2sx_active_slots(t2sx_session* s, int32_t* slots, int32_t* n);
+/* Logits f32 [rows][vocab] of the last pass (decode: one row per active slot; prefill: one
+ * row per prefilled slot), before the repetition penalty. */
+T2SX_API int t2sx_read_logits(t2sx_session* s, float* out, int32_t max_rows, int32_t* rows);
+/* Cached f16 K (which=0) or V (which=1) of one slot and layer: out [n_pos][d] (uint16 bits). */
+T2SX_API int t2sx_read_kv(t2sx_session* s, int32_t slot, int32_t layer, int32_t which, uint16_t* out);
+/* Seen-token mask used by the repetition penalty (t2s_session_get_seen_mask, t2s.h:487): set
+ * one slot's mask (uint8 [vocab], nonzero = seen).  The device marks every sampled token. */
+T2SX_API int t2sx_set_seen(t2sx_session* s, int32_t slot, const uint8_t* seen);
+/* Device time of the last t2sx_decode / t2sx_decode_async batch, in ms (CUDA events). */
+T2SX_API int t2sx_last_decode_ms(t2sx_session* s, float* ms);
+
+/* ---- kernels on caller-provided device buffers (isolated measurements) ------------------- */
+
+/* A linear weight [N][K] given as ggml block bytes on the host (Q8_0, Q4_0, Q4_K, F16 or F32),
+ * repacked to the device layout. */
+typedef struct t2sx_weight t2sx_weight;
+T2SX_API int t2sx_weight_create(int32_t device, int32_t ggml_type, const void* host_bytes, int64_t N,
+                       int64_t K, t2sx_weight** out);
+T2SX_API void t2sx_weight_free(t2sx_weight* w);
+/* y[M][N] = x[M][K] . W^T (+ bias[N]) on device pointers, with ggml-CPU semantics (activation
+ * rows converted to the weight's dot type).  `stream` is a cudaStream_t (0 = legacy default). */
+T2SX_API int t2sx_matmul(t2sx_weight* w, const float* x_dev, int64_t M, const float* bias_dev, float* y_dev,
+                void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

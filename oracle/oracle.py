@@ -1,0 +1,175 @@
+"""ctypes binding of the T2S oracle (liborc.so) -- TEST INFRASTRUCTURE ONLY.
+
+Loaded by tests/, the smoke entry and bench.py's cpu_baseline / reference arm; never by the
+product.  `build()` compiles liborc.so with the Makefile beside this file.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "liborc.so")
+_lib = None
+
+F32, F16, Q4_0, Q8_0, Q4_K = 0, 1, 2, 8, 12
+
+
+def build(force: bool = False) -> str:
+    src = os.path.join(HERE, "t2s_oracle.cpp")
+    if force or not os.path.exists(LIB_PATH) or os.path.getmtime(LIB_PATH) < os.path.getmtime(src):
+        subprocess.run(["make", "-C", HERE, "-B" if force else "liborc.so"], check=True,
+                       stdout=subprocess.DEVNULL)
+    return LIB_PATH
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            build()
+        L = C.CDLL(LIB_PATH)
+        P, I, I64, F = C.c_void_p, C.c_int, C.c_int64, C.c_float
+        sig = {
+            "orc_expf": (F, [F]), "orc_f32_to_f16": (C.c_uint16, [F]), "orc_f16_to_f32": (F, [C.c_uint16]),
+            "orc_row_bytes": (I64, [I, I64]),
+            "orc_quantize_q8_0": (None, [P, I64, P]), "orc_quantize_q8_K": (None, [P, I64, P]),
+            "orc_dequantize": (None, [I, P, I64, P]),
+            "orc_matmul": (I, [I, P, I64, I64, P, I64, P]),
+            "orc_attn_decode": (None, [P, P, P, I, P]), "orc_attn_prefill": (None, [P, P, P, I, P]),
+            "orc_layernorm": (None, [P, P, P, I, F, P]), "orc_pe_row": (None, [I, I, P]),
+            "orc_model_load": (P, [C.c_char_p]), "orc_model_free": (None, [P]),
+            "orc_model_info": (I, [P, P, P]),
+            "orc_session_new": (P, [P, I, I]), "orc_session_free": (None, [P]),
+            "orc_set_threads": (None, [I]),
+            "orc_embed_prefill": (I, [P, P, P, I, P, I, P]),
+            "orc_prefill": (I, [P, I, P, I, I, I, P, P, P]),
+            "orc_decode_step": (I, [P, I, P, P, P, F, I, P, P]),
+            "orc_slot_n_pos": (I, [P, I]), "orc_read_kv": (I, [P, I, I, I, P]),
+        }
+        for name, (res, args) in sig.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def ptr(a: np.ndarray | None):
+    return None if a is None else a.ctypes.data_as(C.c_void_p)
+
+
+def expf(x: float) -> float:
+    return lib().orc_expf(x)
+
+
+def matmul(wtype: int, w_bytes: np.ndarray, N: int, K: int, x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1, K)
+    y = np.empty((x.shape[0], N), dtype=np.float32)
+    rc = lib().orc_matmul(wtype, ptr(np.ascontiguousarray(w_bytes)), N, K, ptr(x), x.shape[0], ptr(y))
+    assert rc == 0
+    return y
+
+
+def quantize_q8_0(x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32).ravel()
+    out = np.empty(x.size // 32 * 34, dtype=np.uint8)
+    lib().orc_quantize_q8_0(ptr(x), x.size, ptr(out))
+    return out
+
+
+def dequantize(wtype: int, data: np.ndarray, n: int) -> np.ndarray:
+    out = np.empty(n, dtype=np.float32)
+    lib().orc_dequantize(wtype, ptr(np.ascontiguousarray(data)), n, ptr(out))
+    return out
+
+
+class Model:
+    def __init__(self, path: str):
+        self.h = lib().orc_model_load(path.encode())
+        if not self.h:
+            raise RuntimeError(f"oracle could not load {path}")
+        hp = np.zeros(9, dtype=np.uint32)
+        types = np.zeros(4, dtype=np.int32)
+        lib().orc_model_info(self.h, ptr(hp), ptr(types))
+        self.hp = hp
+        (self.embedding_dim, self.d, self.n_head, self.ff, self.n_layer, self.vocab,
+         self.phone_vocab, self.eos, _) = [int(v) for v in hp]
+        self.types = types
+
+    def embed_prefill(self, phones, bert, sem):
+        phones = np.ascontiguousarray(phones, dtype=np.int32)
+        sem = np.ascontiguousarray(sem, dtype=np.int32)
+        bert = np.ascontiguousarray(bert, dtype=np.float32)
+        x = np.empty((phones.size + sem.size, self.d), dtype=np.float32)
+        rc = lib().orc_embed_prefill(self.h, ptr(phones), ptr(bert), phones.size, ptr(sem), sem.size, ptr(x))
+        assert rc == 0
+        return x
+
+    def close(self):
+        if self.h:
+            lib().orc_model_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class Session:
+    def __init__(self, model: Model, n_slots: int, capacity: int):
+        self.model = model
+        self.h = lib().orc_session_new(model.h, n_slots, capacity)
+        if not self.h:
+            raise RuntimeError("oracle session init failed")
+
+    def prefill(self, slot: int, x: np.ndarray, T_prompt: int, eos_mask=True, want_logits=False, want_y=False):
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        tok = np.zeros(1, dtype=np.int32)
+        logits = np.empty(self.model.vocab, dtype=np.float32) if want_logits else None
+        y = np.empty_like(x) if want_y else None
+        rc = lib().orc_prefill(self.h, slot, ptr(x), x.shape[0], T_prompt, int(eos_mask), ptr(tok), ptr(logits), ptr(y))
+        if rc != 0:
+            raise RuntimeError("oracle prefill rejected")
+        return int(tok[0]), logits, y
+
+    def decode(self, slots, tokens, seen=None, rep_penalty=1.0, eos_mask=True, want_logits=False):
+        slots = np.ascontiguousarray(slots, dtype=np.int32)
+        tokens = np.ascontiguousarray(tokens, dtype=np.int32)
+        out = np.empty(slots.size, dtype=np.int32)
+        logits = np.empty((slots.size, self.model.vocab), dtype=np.float32) if want_logits else None
+        seen_a = None if seen is None else np.ascontiguousarray(seen, dtype=np.float32)
+        rc = lib().orc_decode_step(self.h, slots.size, ptr(slots), ptr(tokens), ptr(seen_a),
+                                   float(rep_penalty), int(eos_mask), ptr(out), ptr(logits))
+        if rc != 0:
+            raise RuntimeError("oracle decode rejected")
+        return out, logits
+
+    def n_pos(self, slot):
+        return lib().orc_slot_n_pos(self.h, slot)
+
+    def read_kv(self, slot, layer, which):
+        n = self.n_pos(slot)
+        out = np.empty((n, self.model.d), dtype=np.uint16)
+        lib().orc_read_kv(self.h, slot, layer, which, ptr(out))
+        return out
+
+    def close(self):
+        if self.h:
+            lib().orc_session_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def set_threads(n: int):
+    lib().orc_set_threads(int(n))

@@ -1,0 +1,35 @@
+"""The C-ABI library loads and exports every entry point include/t2sx.h declares (no GPU)."""
+import os
+import re
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_symbols():
+    src = open(os.path.join(ROOT, "include", "t2sx.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(t2sx_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_library_exports_every_declared_symbol(t2sx_mod):
+    import ctypes
+    lib = ctypes.CDLL(t2sx_mod.LIB_PATH)
+    syms = declared_symbols()
+    assert len(syms) >= 25
+    missing = [s for s in syms if not hasattr(lib, s)]
+    assert not missing, missing
+    # the binding covers the whole header
+    assert set(syms) == set(t2sx_mod.SIGNATURES), set(syms) ^ set(t2sx_mod.SIGNATURES)
+
+
+def test_errors_without_device(t2sx_mod):
+    """Invalid arguments are rejected on the host, before any device work."""
+    import ctypes
+    L = t2sx_mod.lib()
+    h = ctypes.c_void_p()
+    assert L.t2sx_model_load(None, 0, ctypes.byref(h)) == t2sx_mod.ERR_INVALID
+    assert b"null" in L.t2sx_last_error()
+    assert L.t2sx_session_create(None, 1, 1, None, ctypes.byref(h)) == t2sx_mod.ERR_INVALID
+    assert L.t2sx_session_find_free_slot(None) == -1
+    assert L.t2sx_session_slot_n_pos(None, 0) == -1
+    assert L.t2sx_version() == 1

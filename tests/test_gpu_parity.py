@@ -1,0 +1,173 @@
+"""GPU parity: libt2sx (through its C ABI) against the CPU oracle, bit for bit.
+
+Every kernel reproduces the oracle's evaluation order, so the comparisons below are exact
+(array_equal on the raw bits), well inside the north-star tolerance for logits (1e-2 abs /
+1e-3 rel), and greedy token streams must be identical.
+"""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+
+
+def _need_gpu():
+    if not torch.cuda.is_available():
+        pytest.fail("CUDA device required for -m gpu tests")
+
+
+def _weights(fmt, N, K, seed):
+    import gguf
+    import synth
+    rng = np.random.default_rng(seed)
+    w = (rng.standard_normal((N, K), dtype=np.float32) * np.float32(0.02)).astype(np.float32)
+    if fmt == "q8_0":
+        return 8, gguf.quantize(w, gguf.GGMLQuantizationType.Q8_0)
+    if fmt == "q4_0":
+        return 2, gguf.quantize(w, gguf.GGMLQuantizationType.Q4_0)
+    if fmt == "q4_k":
+        return 12, synth.quantize_q4_k(w)
+    if fmt == "f16":
+        return 1, w.astype(np.float16).view(np.uint8)
+    return 0, w.view(np.uint8)
+
+
+def same_bits(a, b):
+    a = np.ascontiguousarray(a, dtype=np.float32)
+    b = np.ascontiguousarray(b, dtype=np.float32)
+    return a.shape == b.shape and np.array_equal(a.view(np.uint32), b.view(np.uint32))
+
+
+@pytest.mark.parametrize("fmt", ["q8_0", "q4_0", "q4_k", "f16", "f32"])
+@pytest.mark.parametrize("NK", [(1536, 512), (512, 2048), (1025, 512)])
+@pytest.mark.parametrize("M", [1, 7, 32, 33, 130])
+def test_matmul_bit_exact(t2sx_mod, orc, fmt, NK, M):
+    _need_gpu()
+    if fmt in ("f16", "f32") and M > 33:
+        M = 40
+    N, K = NK
+    wt, wb = _weights(fmt, N, K, seed=N * 7 + K + M)
+    x = np.random.default_rng(M).standard_normal((M, K), dtype=np.float32)
+    ref = orc.matmul(wt, wb.reshape(-1), N, K, x)
+    w = t2sx_mod.Weight(wt, wb, N, K)
+    xd = torch.from_numpy(x).cuda()
+    yd = torch.empty((M, N), dtype=torch.float32, device="cuda")
+    w.matmul(xd.data_ptr(), M, yd.data_ptr(), stream=torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    got = yd.cpu().numpy()
+    assert np.isfinite(got).all()
+    if not same_bits(got, ref):
+        d = np.abs(got - ref)
+        pytest.fail(f"{fmt} {NK} M={M}: {int((got != ref).sum())} mismatches, max abs {d.max():.3e}")
+
+
+def _run_pair(t2sx_mod, orc, path, lengths, steps, rep_penalty=1.0, eos_mask=True, check_kv=True):
+    """Prefill + `steps` greedy decode steps on both; returns the token arrays."""
+    import synth
+    m_gpu = t2sx_mod.Model(path)
+    m_orc = orc.Model(path)
+    cap = max(tt + tp for tt, tp, _ in lengths) + steps + 1
+    n = len(lengths)
+    s_gpu = t2sx_mod.Session(m_gpu, n, cap, repetition_penalty=rep_penalty, eos_mask=eos_mask)
+    s_orc = orc.Session(m_orc, n, cap)
+    xs, nq, tps = [], [], []
+    first_orc = []
+    for i, (tt, tp, seed) in enumerate(lengths):
+        ph, bert, sem = synth.session_inputs(seed, tt, tp)
+        x_ref = m_orc.embed_prefill(ph, bert, sem)
+        x_gpu = s_gpu.embed_prefill(ph, bert, sem)
+        assert same_bits(x_gpu, x_ref), "prefill embedding differs"
+        xs.append(x_ref); nq.append(tt + tp); tps.append(tp)
+        tok, lg, _ = s_orc.prefill(i, x_ref, tp, eos_mask=eos_mask, want_logits=True)
+        first_orc.append((tok, lg))
+    toks_gpu = s_gpu.prefill(np.arange(n), nq, tps, np.concatenate(xs))
+    lg_gpu = s_gpu.read_logits(n)
+    for i in range(n):
+        assert same_bits(lg_gpu[i], first_orc[i][1]), f"prefill logits of slot {i} differ"
+        assert toks_gpu[i] == first_orc[i][0]
+        assert s_gpu.slot_n_pos(i) == nq[i] and s_gpu.slot_audio_offset(i) == nq[i] - tps[i]
+    if check_kv:
+        for layer in (0, m_orc.n_layer - 1):
+            for which in (0, 1):
+                assert np.array_equal(s_gpu.read_kv(0, layer, which), s_orc.read_kv(0, layer, which))
+    V = m_orc.vocab
+    seen = np.zeros((n, V), dtype=np.float32)
+    cur = np.array([t for t, _ in first_orc], dtype=np.int32)
+    seen[np.arange(n), cur] = 1.0
+    ref_tokens = []
+    ref_last_logits = None
+    for step in range(steps):
+        out, lg = s_orc.decode(np.arange(n), cur, seen=seen if rep_penalty != 1.0 else None,
+                               rep_penalty=rep_penalty, eos_mask=eos_mask, want_logits=(step == steps - 1))
+        ref_tokens.append(out.copy())
+        seen[np.arange(n), out] = 1.0
+        cur = out
+        if lg is not None:
+            ref_last_logits = lg
+    gpu_tokens = s_gpu.decode(steps)
+    ref_tokens = np.stack(ref_tokens)
+    assert np.array_equal(gpu_tokens, ref_tokens), (
+        f"token streams differ at step {int(np.argmax((gpu_tokens != ref_tokens).any(axis=1)))}")
+    assert same_bits(s_gpu.read_logits(n), ref_last_logits), "last-step logits differ"
+    if check_kv:
+        for which in (0, 1):
+            assert np.array_equal(s_gpu.read_kv(n - 1, m_orc.n_layer - 1, which), s_orc.read_kv(n - 1, m_orc.n_layer - 1, which))
+    return gpu_tokens
+
+
+@pytest.mark.parametrize("fmt", ["q8_0", "q4_0", "q4_k", "f16"])
+def test_decode_small_model_bit_exact(t2sx_mod, orc, fmt):
+    _need_gpu()
+    import synth
+    path = synth.ensure_gguf(fmt, 7, n_layer=2)
+    lengths = [(40, 30, 11), (17, 50, 12), (64, 3, 13)]
+    _run_pair(t2sx_mod, orc, path, lengths, steps=70)
+
+
+def test_decode_repetition_penalty_bit_exact(t2sx_mod, orc):
+    _need_gpu()
+    import synth
+    path = synth.ensure_gguf("q8_0", 7, n_layer=2)
+    _run_pair(t2sx_mod, orc, path, [(20, 20, 21), (33, 9, 22)], steps=40, rep_penalty=1.35, eos_mask=False)
+
+
+def test_decode_full_model_bs1_bit_exact(t2sx_mod, orc):
+    """The bs=1 Q8_0 workload shape (128 phonemes + 150 prompt tokens, 24 layers), 64 steps."""
+    _need_gpu()
+    import synth
+    path = synth.ensure_gguf("q8_0", 0, n_layer=24)
+    _run_pair(t2sx_mod, orc, path, [(128, 150, 0)], steps=64)
+
+
+def test_slot_reuse_and_errors(t2sx_mod):
+    _need_gpu()
+    import synth
+    T = t2sx_mod
+    path = synth.ensure_gguf("q8_0", 7, n_layer=2)
+    m = T.Model(path)
+    s = T.Session(m, 2, 64, eos_mask=True)
+    assert s.find_free_slot() == 0
+    x = np.random.default_rng(0).standard_normal((10, 512), dtype=np.float32)
+    s.prefill([0], [10], [4], x)
+    assert s.find_free_slot() == 1
+    with pytest.raises(T.T2SXError) as e:
+        s.prefill([0], [10], [4], x)           # prefill on an active slot
+    assert e.value.code == T.ERR_STATE
+    with pytest.raises(T.T2SXError) as e:
+        s.prefill([1], [3], [4], x[:3])        # n_query < ref_T_prompt
+    assert e.value.code == T.ERR_INVALID
+    s.decode(5)
+    assert s.slot_n_pos(0) == 15
+    with pytest.raises(T.T2SXError) as e:
+        s.decode(60)                           # would run past slot_size
+    assert e.value.code == T.ERR_BOUNDS
+    s.slot_release(0)
+    assert s.slot_n_pos(0) == 0 and s.find_free_slot() == 0
+    with pytest.raises(T.T2SXError):
+        s.decode(1)                            # no active slot
+    s.prefill([0], [10], [4], x)
+    s.decode(3)
+    with pytest.raises(T.T2SXError) as e:
+        T.Model("/nonexistent/path.gguf")
+    assert e.value.code == T.ERR_IO
