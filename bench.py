@@ -1,0 +1,384 @@
+"""T2S decode throughput on B200: the box-scale batched-session workload.
+
+Workload (default): 2048 independent sessions, Q4_K weights (synthetic, seed 3), each a
+200-phoneme + 150-semantic-token prompt, greedy decode with EOS masked, sharded evenly over
+the GPUs (one process per GPU, no collective on the data path).  A step = one decode step of
+every session on the GPU; value = tokens/s over all ranks (max device time over ranks).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                  [--workload bs2048_q4_k|bs32_q4_0|bs1_q8_0]
+
+--impl reference times the reference's CPU arithmetic (the oracle restatement; the reference's
+ggml cannot be built here) on the host cores for a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "gpt-sovits.cpp_b200"))
+sys.path.insert(0, os.path.join(ROOT, "oracle"))
+
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d, "measured"
+    return PEAKS_FALLBACK, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle samples during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 8:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = max(mx, float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[4:8]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_setup(n_gpus):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != n_gpus:
+        raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={world}")
+    return rank, world, local
+
+
+def session_prompts(workload, sessions):
+    import synth
+    return synth.workload_lengths(workload, sessions)
+
+
+# ------------------------------------------------------------------------------------------------
+# our arm
+# ------------------------------------------------------------------------------------------------
+def run_ours(args):
+    import torch
+    import synth
+    import t2sx
+    import build as t2sx_build
+
+    rank, world, local = dist_setup(args.gpus)
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(local)
+    t2sx_build.build()
+    w = synth.WORKLOADS[args.workload]
+    total_sessions = w["sessions"]
+    per = total_sessions // world
+    lo = rank * per
+    lengths_all = session_prompts(args.workload, total_sessions)
+    mine = lengths_all[lo:lo + per]
+    path = synth.ensure_gguf(w["wtype"], w["seed"], n_layer=24)
+
+    W, K = args.warmup, args.steps
+    max_prompt = max(tt + tp for tt, tp, _ in mine)
+    slot_size = max_prompt + W + K + 1
+
+    model = t2sx.Model(path, device=local)
+    sess = t2sx.Session(model, per, slot_size, repetition_penalty=1.0, eos_mask=True)
+
+    # ---- prefill (not timed): GPU embedding of the seeded prompts, then batched prefill ----
+    t0 = time.perf_counter()
+    total_rows = sum(tt + tp for tt, tp, _ in mine)
+    xdev = torch.empty((total_rows, 512), dtype=torch.float32, device="cuda")
+    off = 0
+    for tt, tp, seed in mine:
+        ph, bert, sem = synth.session_inputs(seed, tt, tp)
+        sess.embed_prefill(ph, bert, sem, out_dev_ptr=xdev[off].data_ptr())
+        off += tt + tp
+    torch.cuda.synchronize()
+    first = sess.prefill(np.arange(per), [tt + tp for tt, tp, _ in mine], [tp for _, tp, _ in mine],
+                         x_dev_ptr=xdev.data_ptr())
+    del xdev
+    torch.cuda.synchronize()
+    prefill_s = time.perf_counter() - t0
+
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        import torch.distributed as dist
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        import torch.distributed as dist
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        return float(t.item())
+
+    # ---- warm-up: W host-driven steps (also captures the step graph) ----
+    cur = first.copy()
+    for _ in range(W):
+        cur = sess.decode_step_host(cur, want_tokens=True)
+    n_kernels = sess.graph_kernels()
+    ctx_before = np.array([sess.slot_n_pos(i) for i in range(per)], dtype=np.int64)
+
+    # ---- timed region: K decode steps through the C ABI with host buffers every step ----
+    # (e2e = wall clock of the loop incl. the per-step host<->device token copies;
+    #  value = the same steps' device time of the step graphs, CUDA events on the session stream)
+    barrier()
+    torch.cuda.synchronize()
+    dev_ms = 0.0
+    with ClockSampler(local) as clk:
+        t0 = time.perf_counter()
+        for _ in range(K):
+            cur = sess.decode_step_host(cur, want_tokens=True)
+            dev_ms += sess.last_decode_ms()
+        wall_s = time.perf_counter() - t0
+    barrier()
+    t_max = max_over_ranks(dev_ms / 1e3)
+    e2e_max = max_over_ranks(wall_s)
+    tokens = sum_over_ranks(float(per * K))
+    value = tokens / t_max
+    e2e_value = tokens / e2e_max
+
+    # ---- per-kernel device times on the final state, for the roofline ----
+    prof = sess.profile_step(iters=10)
+    ctx_now = np.array([sess.slot_n_pos(i) for i in range(per)], dtype=np.int64)
+    # attention of one layer at the last step: each session reads K and V of its whole prefix
+    # (ctx_now positions): 2 (K,V) * 16 heads * 32 dims * 2 B = 2048 B per position, plus q/out
+    attn_bytes = float((ctx_now * 2048).sum() + per * (512 * 2 + 512 * 4))
+    attn_gbs = attn_bytes / (prof["attention"] * 1e-3) / 1e9
+
+    # ---- CPU baseline (rank 0, N=1 only): the oracle on the host cores, bounded sample ----
+    cpu = None
+    if world == 1 and not args.no_cpu:
+        cpu = cpu_baseline(args.workload, path, args.cpu_sessions, args.cpu_steps)
+
+    peaks, peak_kind = load_peaks()
+    if rank == 0:
+        clocks = clk.summary()
+        line = {
+            "metric": "T2S decode tokens/s (batched sessions)",
+            "value": round(value, 2),
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": K,
+            "warmup": W,
+            "ms_per_step": round(t_max * 1e3 / K, 4),
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "int8xint8->f32 (Q4_K weights), f16 KV",
+            "data": "synthetic (seeded N(0,0.02) weights, uniform ids, N(0,1) BERT features)",
+            "config": {
+                "workload": args.workload,
+                "model": "T2S GPT-SoVITS v2 shape: 24 post-norm layers, d=512, 16x32 heads, FFN 2048, vocab 1025",
+                "weights": w["wtype"],
+                "sessions_total": total_sessions,
+                "sessions_per_gpu": per,
+                "prompt": "200 phonemes + 150 semantic tokens" if args.workload == "bs2048_q4_k" else "see synth.WORKLOADS",
+                "context_at_start": int(ctx_before.mean()),
+                "context_at_end": int(ctx_now.mean()),
+                "global_batch": total_sessions,
+                "parallelism": f"session-sharded dp{world}, no collective",
+                "l2": "inputs larger than L2: KV cache %.1f GB per GPU" % (sess.device_bytes() / 1e9),
+                "prefill_s": round(prefill_s, 2),
+            },
+            "e2e": {"value": round(e2e_value, 2), "unit": "tokens/s", "h2d_bytes_per_step": 4 * per,
+                    "d2h_bytes_per_step": 4 * per,
+                    "how": "t2sx_decode_step_host per step: host tokens -> device, one step graph, tokens -> host; wall clock"},
+            "gpu_launches": int(n_kernels * K),
+            "roofline": {
+                "kernel": "k_attn_decode (paged f16 KV attention, one layer)",
+                "bound": "hbm",
+                "achieved": round(attn_gbs, 1),
+                "peak": peaks["hbm_gbs"],
+                "unit": "GB/s",
+                "frac": round(attn_gbs / peaks["hbm_gbs"], 4),
+                "traffic": None,
+                "peak_kind": peak_kind,
+                "algorithmic_bytes_per_launch": int(attn_bytes),
+                "launch_ms": round(prof["attention"], 4),
+            },
+            "kernel_ms": {k: round(v, 4) for k, v in prof.items()},
+            "clocks": clocks,
+            "first_tokens": [int(t) for t in first[:4]],
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line))
+    sess.close()
+    model.close()
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def cpu_baseline(workload, path, n_sessions, n_steps, warm=2):
+    """The oracle (CPU restatement of the reference arithmetic) on the host cores: prefill of
+    `n_sessions` prompts of the workload (untimed), then `n_steps` timed decode steps."""
+    import oracle
+    import synth
+    cores = os.cpu_count() or 1
+    oracle.set_threads(cores)
+    m = oracle.Model(path)
+    lengths = synth.workload_lengths(workload)[:n_sessions]
+    cap = max(tt + tp for tt, tp, _ in lengths) + n_steps + warm + 2
+    s = oracle.Session(m, len(lengths), cap)
+    cur = []
+    for i, (tt, tp, seed) in enumerate(lengths):
+        ph, bert, sem = synth.session_inputs(seed, tt, tp)
+        x = m.embed_prefill(ph, bert, sem)
+        cur.append(s.prefill(i, x, tp)[0])
+    slots = np.arange(len(lengths))
+    cur = np.array(cur, dtype=np.int32)
+    for _ in range(warm):
+        cur, _ = s.decode(slots, cur)
+    t0 = time.perf_counter()
+    for _ in range(n_steps):
+        cur, _ = s.decode(slots, cur)
+    dt = time.perf_counter() - t0
+    return {"value": round(len(lengths) * n_steps / dt, 3), "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"{len(lengths)} sessions of {workload}, {n_steps} decode steps after prefill "
+                      f"(oracle restatement; ggml is absent from the reference snapshot)"}
+
+
+# ------------------------------------------------------------------------------------------------
+# reference arm
+# ------------------------------------------------------------------------------------------------
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import oracle
+    import synth
+    w = synth.WORKLOADS[args.workload]
+    path = synth.ensure_gguf(w["wtype"], w["seed"], n_layer=24)
+    cores = os.cpu_count() or 1
+    oracle.set_threads(cores)
+    m = oracle.Model(path)
+    n_sess = min(args.cpu_sessions, w["sessions"])
+    lengths = synth.workload_lengths(args.workload)[:n_sess]
+    W, K = args.warmup, args.steps
+    cap = max(tt + tp for tt, tp, _ in lengths) + W + K + 2
+    s = oracle.Session(m, n_sess, cap)
+    cur = []
+    for i, (tt, tp, seed) in enumerate(lengths):
+        ph, bert, sem = synth.session_inputs(seed, tt, tp)
+        cur.append(s.prefill(i, m.embed_prefill(ph, bert, sem), tp)[0])
+    slots = np.arange(n_sess)
+    cur = np.array(cur, dtype=np.int32)
+    for _ in range(W):
+        cur, _ = s.decode(slots, cur)
+    t0 = time.perf_counter()
+    for _ in range(K):
+        cur, _ = s.decode(slots, cur)
+    dt = time.perf_counter() - t0
+    value = n_sess * K / dt
+    sample = (f"{n_sess} sessions of {args.workload} per step (bounded sample), oracle restatement of the "
+              f"reference CPU arithmetic; ggml is an empty submodule in the reference and cannot be built")
+    print(json.dumps({
+        "impl": "reference",
+        "metric": "T2S decode tokens/s (batched sessions)",
+        "value": round(value, 3),
+        "unit": "tokens/s",
+        "n_gpus": args.gpus,
+        "steps": K,
+        "warmup": W,
+        "ms_per_step": round(dt * 1e3 / K, 3),
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "int8xint8->f32 (Q4_K weights), f16 KV",
+        "data": "synthetic",
+        "config": {"workload": args.workload, "sessions_timed": n_sess, "weights": w["wtype"]},
+        "cpu_baseline": {"value": round(value, 3), "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": round(value, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="bs2048_q4_k")
+    ap.add_argument("--cpu-sessions", type=int, default=8)
+    ap.add_argument("--cpu-steps", type=int, default=20)
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -518,6 +518,7 @@ struct t2sx_session {
     int32_t* ring = nullptr;
     int32_t* ring_step = nullptr;
     int ring_len = 256;
+    int graph_kernels = 0;         // kernel nodes in the captured step graph
     int32_t* scratch_i = nullptr;  // [n_slots]
     int last_rows = 0;             // rows of the last logits
     const float* last_logits = nullptr;
@@ -861,6 +862,15 @@ static int prepare_decode(t2sx_session* s, int n_steps) {
             enqueue_step(s);
             cudaError_t e = cudaStreamEndCapture(s->st, &g);
             if (e != cudaSuccess) return fail(T2SX_ERR_CUDA, "decode graph capture: %s", cudaGetErrorString(e));
+            size_t nn = 0;
+            cudaGraphGetNodes(g, nullptr, &nn);
+            std::vector<cudaGraphNode_t> nodes(nn);
+            if (nn) cudaGraphGetNodes(g, nodes.data(), &nn);
+            s->graph_kernels = 0;
+            for (auto nd : nodes) {
+                cudaGraphNodeType ty;
+                if (cudaGraphNodeGetType(nd, &ty) == cudaSuccess && ty == cudaGraphNodeTypeKernel) ++s->graph_kernels;
+            }
             e = cudaGraphInstantiate(&s->graph, g, 0);
             cudaGraphDestroy(g);
             if (e != cudaSuccess) { s->graph = nullptr; return fail(T2SX_ERR_CUDA, "decode graph instantiate: %s", cudaGetErrorString(e)); }
@@ -945,6 +955,7 @@ extern "C" int t2sx_decode_step_host(t2sx_session* s, const int32_t* tokens_in, 
     if ((rc = launch_steps(s, 1))) return rc;
     if (tokens_out) CK(cudaMemcpyAsync(tokens_out, s->dec.tok, T * 4, cudaMemcpyDeviceToHost, s->st));
     CK(cudaStreamSynchronize(s->st));
+    CK(cudaEventElapsedTime(&s->last_ms, s->ev0, s->ev1));
     return T2SX_OK;
 }
 
@@ -990,6 +1001,51 @@ extern "C" int t2sx_set_seen(t2sx_session* s, int32_t slot, const uint8_t* seen)
     CK(cudaSetDevice(s->m->device));
     CK(cudaMemcpyAsync(s->seen + (size_t)slot * s->V, seen, s->V, cudaMemcpyHostToDevice, s->st));
     CK(cudaStreamSynchronize(s->st));
+    return T2SX_OK;
+}
+
+extern "C" int t2sx_decode_graph_kernels(t2sx_session* s, int32_t* n) {
+    if (!s || !n) return fail(T2SX_ERR_INVALID, "null argument");
+    *n = s->graph ? s->graph_kernels : 0;
+    return T2SX_OK;
+}
+
+// Average device time of one launch of each kernel class of the decode step, replayed on the
+// state left by the last decode step (all replayed kernels are idempotent there).
+extern "C" int t2sx_profile_step(t2sx_session* s, int32_t iters, float* ms) {
+    if (!s || !ms || iters <= 0) return fail(T2SX_ERR_INVALID, "t2sx_profile_step: bad arguments");
+    if (!s->graph) return fail(T2SX_ERR_STATE, "t2sx_profile_step: run a decode step first");
+    CK(cudaSetDevice(s->m->device));
+    const t2sx_model* m = s->m;
+    Work& w = s->dec;
+    const int T = (int)s->active.size();
+    Rows rows = rows_of(s, w);
+    KVView kv = kv_of(s);
+    ActQ a = act_of(w);
+    const LayerD& L = m->layers[0];
+    auto timeit = [&](int idx, auto&& fn) -> int {
+        fn();
+        CK(cudaEventRecord(s->ev0, s->st));
+        for (int i = 0; i < iters; ++i) fn();
+        CK(cudaEventRecord(s->ev1, s->st));
+        CK(cudaEventSynchronize(s->ev1));
+        float t = 0.0f;
+        CK(cudaEventElapsedTime(&t, s->ev0, s->ev1));
+        ms[idx] = t / iters;
+        return T2SX_OK;
+    };
+    int rc;
+    if ((rc = timeit(0, [&] { attention_decode(T, w.q16, rows, kv, 0, kAttnScale, w.attn, s->st); }))) return rc;
+    quantize_act(L.qkv.type, w.x, T, kD, a, s->st);
+    if ((rc = timeit(1, [&] { matmul(L.qkv, a, T, L.qkv_b, 0, w.qkv, s->st); }))) return rc;
+    if ((rc = timeit(2, [&] { matmul(L.out, a, T, L.out_b, 0, w.o, s->st); }))) return rc;
+    if ((rc = timeit(3, [&] { matmul(L.up, a, T, L.up_b, 1, w.h, s->st); }))) return rc;
+    if ((rc = timeit(5, [&] { matmul(m->lm_head, a, T, nullptr, 0, w.logits, s->st); }))) return rc;
+    quantize_act(L.down.type, w.h, T, s->ff, a, s->st);
+    if ((rc = timeit(4, [&] { matmul(L.down, a, T, L.down_b, 0, w.f, s->st); }))) return rc;
+    if ((rc = timeit(6, [&] { residual_layernorm(T, w.ln1, w.f, L.ln2_w, L.ln2_b, 1e-5f, w.o, s->st); }))) return rc;
+    if ((rc = timeit(7, [&] { quantize_act(L.down.type, w.h, T, s->ff, a, s->st); }))) return rc;
+    CK(cudaGetLastError());
     return T2SX_OK;
 }
 

@@ -48,6 +48,8 @@ SIGNATURES = {
     "t2sx_read_kv": (C.c_int, [_P, _I, _I, _I, _P]),
     "t2sx_set_seen": (C.c_int, [_P, _I, _P]),
     "t2sx_last_decode_ms": (C.c_int, [_P, _P]),
+    "t2sx_decode_graph_kernels": (C.c_int, [_P, _P]),
+    "t2sx_profile_step": (C.c_int, [_P, _I, _P]),
     "t2sx_weight_create": (C.c_int, [_I, _I, _P, _I64, _I64, _P]),
     "t2sx_weight_free": (None, [_P]),
     "t2sx_matmul": (C.c_int, [_P, _P, _I64, _P, _P, _P]),
@@ -220,6 +222,17 @@ class Session:
         v = C.c_float(0)
         _ck(lib().t2sx_last_decode_ms(self.h, C.byref(v)))
         return v.value
+
+    def graph_kernels(self) -> int:
+        n = C.c_int32(0)
+        _ck(lib().t2sx_decode_graph_kernels(self.h, C.byref(n)))
+        return n.value
+
+    def profile_step(self, iters: int = 20):
+        ms = np.zeros(8, dtype=np.float32)
+        _ck(lib().t2sx_profile_step(self.h, iters, _p(ms)))
+        return dict(zip(["attention", "mm_qkv", "mm_out", "mm_up", "mm_down", "mm_lm_head", "residual_ln",
+                         "quant_2048"], ms.tolist()))
 
     def read_logits(self, max_rows: int | None = None):
         max_rows = max_rows or self.n_slots

@@ -125,8 +125,16 @@ T2SX_API int t2sx_read_kv(t2sx_session* s, int32_t slot, int32_t layer, int32_t 
 /* Seen-token mask used by the repetition penalty (t2s_session_get_seen_mask, t2s.h:487): set
  * one slot's mask (uint8 [vocab], nonzero = seen).  The device marks every sampled token. */
 T2SX_API int t2sx_set_seen(t2sx_session* s, int32_t slot, const uint8_t* seen);
-/* Device time of the last t2sx_decode / t2sx_decode_async batch, in ms (CUDA events). */
+/* Device time of the last t2sx_decode / t2sx_decode_async batch or t2sx_decode_step_host step
+ * (graph execution only, without the host copies), in ms (CUDA events). */
 T2SX_API int t2sx_last_decode_ms(t2sx_session* s, float* ms);
+/* Kernel nodes in the captured decode-step graph (kernels launched per step). */
+T2SX_API int t2sx_decode_graph_kernels(t2sx_session* s, int32_t* n);
+/* Average device ms of one launch of each decode-step kernel class, replayed on the state of
+ * the last decode step: ms[0] attention (one layer), ms[1..5] matmuls qkv, out, ffn-up,
+ * ffn-down, lm_head (with their bias/ReLU epilogues), ms[6] residual+LayerNorm,
+ * ms[7] activation quantisation of the 2048-wide FFN rows.  ms must hold 8 floats. */
+T2SX_API int t2sx_profile_step(t2sx_session* s, int32_t iters, float* ms);
 
 /* ---- kernels on caller-provided device buffers (isolated measurements) ------------------- */
 
