@@ -128,7 +128,7 @@ def run_ours(args):
         torch.cuda.set_device(local)
     t2sx_build.build()
     w = synth.WORKLOADS[args.workload]
-    total_sessions = w["sessions"]
+    total_sessions = w["sessions"] if args.sessions is None else args.sessions * world
     per = total_sessions // world
     lo = rank * per
     lengths_all = session_prompts(args.workload, total_sessions)
@@ -192,12 +192,14 @@ def run_ours(args):
     barrier()
     torch.cuda.synchronize()
     dev_ms = 0.0
+    torch.cuda.cudart().cudaProfilerStart()   # profilers started with --profile-from-start off see only this loop
     with ClockSampler(local) as clk:
         t0 = time.perf_counter()
         for _ in range(K):
             cur = sess.decode_step_host(cur, want_tokens=True)
             dev_ms += sess.last_decode_ms()
         wall_s = time.perf_counter() - t0
+    torch.cuda.cudart().cudaProfilerStop()
     barrier()
     t_max = max_over_ranks(dev_ms / 1e3)
     e2e_max = max_over_ranks(wall_s)
@@ -368,6 +370,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="bs2048_q4_k")
+    ap.add_argument("--sessions", type=int, default=None,
+                    help="sessions per GPU (default: the workload's total / GPUs); smaller cases for profiling")
     ap.add_argument("--cpu-sessions", type=int, default=8)
     ap.add_argument("--cpu-steps", type=int, default=20)
     ap.add_argument("--no-cpu", action="store_true")
