@@ -185,6 +185,7 @@ def run_ours(args):
         cur = sess.decode_step_host(cur, want_tokens=True)
     n_kernels = sess.graph_kernels()
     ctx_before = np.array([sess.slot_n_pos(i) for i in range(per)], dtype=np.int64)
+    prof_start = sess.profile_step(iters=10)
 
     # ---- timed region: K decode steps through the C ABI with host buffers every step ----
     # (e2e = wall clock of the loop incl. the per-step host<->device token copies;
@@ -267,6 +268,7 @@ def run_ours(args):
                 "launch_ms": round(prof["attention"], 4),
             },
             "kernel_ms": {k: round(v, 4) for k, v in prof.items()},
+            "kernel_ms_at_start": {k: round(v, 4) for k, v in prof_start.items()},
             "clocks": clocks,
             "first_tokens": [int(t) for t in first[:4]],
         }

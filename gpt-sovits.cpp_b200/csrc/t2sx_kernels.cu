@@ -398,8 +398,9 @@ __global__ void __launch_bounds__(256) k_mm_tiled(DevW W, ActQ A, int M, const f
 }
 
 void matmul(const DevW& W, const ActQ& a, int M, const float* bias, int relu, float* y, cudaStream_t st) {
-    const bool tiled = M > kSmallM && (W.type == W_Q8_0 || W.type == W_Q4_0 || W.type == W_Q4_K);
-    if (tiled) {
+    const bool quant = W.type == W_Q8_0 || W.type == W_Q4_0 || W.type == W_Q4_K;
+    if (quant && M > kSmallM && matmul_mma(W, a, M, bias, relu, y, st)) return;
+    if (quant && M > kSmallM) {
         dim3 grid((W.N + 63) / 64, (M + 63) / 64);
         switch (W.type) {
             case W_Q8_0: k_mm_tiled<W_Q8_0><<<grid, 256, 0, st>>>(W, a, M, bias, relu, y); break;
@@ -508,14 +509,15 @@ __device__ __forceinline__ void load_row32(const uint16_t* p, float* out) {
     }
 }
 
-// Decode attention: one CTA of 128 threads per (row, head).  Position lane t = threadIdx.x
-// folds positions t, t+128, ... with the online update; lanes merge by an xor butterfly inside
-// each warp, then the four warps merge as ((w0,w1),(w2,w3)).
+// Decode attention: one warp per (row, head), four heads of a row per CTA.  Position lane
+// t = lane folds positions t, t+32, ... with the online update; the 32 lanes merge in the
+// order of an xor butterfly (partners 16, 8, 4, 2, 1).  The merge is symmetric, so every lane
+// ends with the same state and lane d writes output dim d.
 __global__ void __launch_bounds__(128) k_attn_decode(const uint16_t* __restrict__ q16, Rows rows, KVView kv, int layer,
                                                      float scale, float* __restrict__ out) {
-    __shared__ float s_m[4], s_l[4], s_o[4][kHeadDim];
-    const int r = blockIdx.x, h = blockIdx.y;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int r = blockIdx.x;
+    const int h = blockIdx.y * 4 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
     const int s = rows.slot[r];
     const int L = rows.L[r];
     float q[kHeadDim];
@@ -523,7 +525,7 @@ __global__ void __launch_bounds__(128) k_attn_decode(const uint16_t* __restrict_
     AttnState st;
     st_empty(st);
     const int32_t* pt = kv.ptab + (size_t)s * kv.max_pages;
-    for (int i = tid; i < L; i += kAttnLanes) {
+    for (int i = lane; i < L; i += kAttnLanes) {
         const int page = pt[i / kPage];
         const size_t kb = kv_off(kv, page, layer, 0, h, i % kPage);
         const size_t vb = kv_off(kv, page, layer, 1, h, i % kPage);
@@ -551,27 +553,12 @@ __global__ void __launch_bounds__(128) k_attn_decode(const uint16_t* __restrict_
     float mine = 0.0f;
 #pragma unroll
     for (int d = 0; d < kHeadDim; ++d) if (d == lane) mine = st.o[d];
-    s_o[warp][lane] = mine;
-    if (lane == 0) { s_m[warp] = st.m; s_l[warp] = st.l; }
-    __syncthreads();
-    if (warp == 0) {
-        float M01, a01, b01, l01, M23, a23, b23, l23, M, a, b, l;
-        bool e01, e23, e;
-        st_merge_scalars(s_m[0], s_l[0], s_m[1], s_l[1], M01, a01, b01, l01, e01);
-        st_merge_scalars(s_m[2], s_l[2], s_m[3], s_l[3], M23, a23, b23, l23, e23);
-        const float o01 = e01 ? 0.0f : __fadd_rn(__fmul_rn(s_o[0][lane], a01), __fmul_rn(s_o[1][lane], b01));
-        const float o23 = e23 ? 0.0f : __fadd_rn(__fmul_rn(s_o[2][lane], a23), __fmul_rn(s_o[3][lane], b23));
-        const float m01 = e01 ? __int_as_float(0xff800000) : M01;
-        const float m23 = e23 ? __int_as_float(0xff800000) : M23;
-        st_merge_scalars(m01, l01, m23, l23, M, a, b, l, e);
-        const float o = e ? 0.0f : __fadd_rn(__fmul_rn(o01, a), __fmul_rn(o23, b));
-        out[(size_t)r * kD + h * kHeadDim + lane] = __fmul_rn(o, __fdiv_rn(1.0f, l));
-    }
+    out[(size_t)r * kD + h * kHeadDim + lane] = __fmul_rn(mine, __fdiv_rn(1.0f, st.l));
 }
 
 void attention_decode(int T, const uint16_t* q16, Rows rows, KVView kv, int layer, float scale, float* out,
                       cudaStream_t st) {
-    if (T > 0) k_attn_decode<<<dim3(T, kHeads), kAttnLanes, 0, st>>>(q16, rows, kv, layer, scale, out);
+    if (T > 0) k_attn_decode<<<dim3(T, kHeads / 4), 128, 0, st>>>(q16, rows, kv, layer, scale, out);
 }
 
 // Prefill attention: one thread per (row, head) folds its prefix sequentially.

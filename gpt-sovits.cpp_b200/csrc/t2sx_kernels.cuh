@@ -57,6 +57,8 @@ struct Rows {
 
 void quantize_act(int wtype, const float* x, int M, int K, ActQ& a, cudaStream_t st);
 void matmul(const DevW& W, const ActQ& a, int M, const float* bias, int relu, float* y, cudaStream_t st);
+// Tensor-core path (mma.sync s8) for M > 32; false if the shape is not supported.
+bool matmul_mma(const DevW& W, const ActQ& a, int M, const float* bias, int relu, float* y, cudaStream_t st);
 void embed_decode(int T, const int32_t* row_slot, const int32_t* token_in, const int32_t* n_pos,
                   const int32_t* audio_off, const uint16_t* emb16, const float* emb32, int emb_rows,
                   const float* pe, int pe_rows, float alpha, Rows rows, float* x, cudaStream_t st);

@@ -14,7 +14,7 @@ constexpr int kD = 512;        // d_model
 constexpr int kHeads = 16;
 constexpr int kHeadDim = 32;
 constexpr int kPage = 64;      // KV positions per page
-constexpr int kAttnLanes = 128;  // decode attention: position lanes per (row, head)
+constexpr int kAttnLanes = 32;   // decode attention: position lanes per (row, head)
 
 // e^x: Cody-Waite reduction x = k*ln2 + r (ln2 split in a 16-bit head and a tail so k*head
 // is exact), e^r from its Taylor series to degree 7 in Horner form with fused multiply-adds,

@@ -1,0 +1,313 @@
+// Tensor-core quantised matmul for batched rows (M > 32): y[m][n] = bias[n] + W[n] . x[m].
+//
+// One mma.sync.m16n8k32 (s8 x s8 -> s32, zero accumulator) computes the exact integer dot of
+// one 32-element quantisation block for a 16 (weight rows) x 8 (activation rows) tile, so the
+// per-block float fold of the canonical order -- acc = fma(dw_b * dx_b, (float)isum_b, acc),
+// blocks in increasing order -- runs unchanged on the MMA results (Q4_K: the sub-block sums are
+// combined with their 6-bit scales / mins in integers and folded once per super-block).
+//
+// CTA: 256 threads = 8 warps as 4 (n) x 2 (m); warp tile 32 weight rows x (8*MT) rows.
+// K is staged 4 blocks (128 elements) at a time through shared memory, double buffered with
+// cp.async.  Weight fragments are read straight from the ggml block bytes: a Q8_0 block row is
+// the A fragment's byte order; a Q4_0 block's 16 bytes hold elements j (low nibble) and j+16
+// (high nibble), i.e. exactly the a0/a2 (and a1/a3) register pairs of one 32-bit load.
+#include "t2sx_kernels.cuh"
+#include "t2sx_math.cuh"
+
+namespace t2sx {
+
+__device__ __forceinline__ void mma_s8(int (&c)[4], int a0, int a1, int a2, int a3, int b0, int b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};\n"
+        : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool valid) {
+    const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+    const int n = valid ? 16 : 0;
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(s), "l"(gmem), "r"(n));
+}
+__device__ __forceinline__ void cp_async4(void* smem, const void* gmem, bool valid) {
+    const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+    const int n = valid ? 4 : 0;
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(s), "l"(gmem), "r"(n));
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N>
+__device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
+
+__device__ __forceinline__ int lds32(const uint8_t* p) { return *reinterpret_cast<const int*>(p); }
+
+// exact int -> float for |i| < 2^22 (block dots of Q8_0 / Q4_0 are below 2^19)
+__device__ __forceinline__ float i2f_small(int i) { return __fsub_rn(__int_as_float(0x4B400000 + i), 12582912.0f); }
+
+constexpr int BN = 128;          // weight rows per CTA
+constexpr int KB = 4;            // 32-element blocks per stage
+constexpr int XROW = KB * 32 + 16;   // smem bytes per activation row (int8, padded)
+
+template <int WT, int MT_>
+struct Cfg {
+    static constexpr int MT = MT_;                                // m8 tiles per warp
+    static constexpr int BM = 2 * 8 * MT;                         // activation rows per CTA
+    static constexpr int WROW = (WT == W_Q8_0) ? KB * 32 + 16 : KB * 16 + 16;  // weight bytes per row
+    static constexpr int W_BYTES = BN * WROW;
+    static constexpr int X_BYTES = BM * XROW;
+    static constexpr int DW_BYTES = BN * KB * 4;                  // f32 scales [n][KB] (Q4_K: d,dmin,scm)
+    static constexpr int DX_BYTES = BM * KB * 4;                  // f32 [m][KB] (Q4_K: bs32 int [m][KB])
+    static constexpr int K_EXTRA = (WT == W_Q4_K) ? (BN * 16 + BN * 8 + BM * 4) : 0;  // scm, d+dmin, dx8k
+    static constexpr int STAGE = W_BYTES + X_BYTES + DW_BYTES + DX_BYTES + K_EXTRA;
+    static constexpr int SMEM = 2 * STAGE;
+};
+
+template <int WT, int MT_>
+__global__ void __launch_bounds__(256) k_mm_mma(DevW W, ActQ A, int M, const float* __restrict__ bias, int relu,
+                                                float* __restrict__ y) {
+    using C = Cfg<WT, MT_>;
+    constexpr int MT = C::MT, BM = C::BM, WROW = C::WROW;
+    extern __shared__ __align__(16) uint8_t smem[];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    const int wn = warp & 3, wm = warp >> 2;
+    const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
+    const int N = W.N, K = W.K;
+    const int nb32 = K / 32, nsb = K / 256;
+    const int nstage = K / (32 * KB);
+
+    auto sW = [&](int buf) { return smem + buf * C::STAGE; };
+    auto sX = [&](int buf) { return smem + buf * C::STAGE + C::W_BYTES; };
+    auto sDw = [&](int buf) { return reinterpret_cast<float*>(smem + buf * C::STAGE + C::W_BYTES + C::X_BYTES); };
+    auto sDx = [&](int buf) {
+        return reinterpret_cast<float*>(smem + buf * C::STAGE + C::W_BYTES + C::X_BYTES + C::DW_BYTES);
+    };
+    auto sScm = [&](int buf) { return smem + buf * C::STAGE + C::W_BYTES + C::X_BYTES + C::DW_BYTES + C::DX_BYTES; };
+    auto sDd = [&](int buf) { return reinterpret_cast<float*>(sScm(buf) + BN * 16); };   // [n][2] d, dmin
+    auto sDx8 = [&](int buf) { return reinterpret_cast<float*>(sScm(buf) + BN * 16 + BN * 8); };
+
+    auto load_stage = [&](int stg, int buf) {
+        const int kb0 = stg * KB;
+        uint8_t* w = sW(buf);
+        if (WT == W_Q8_0) {
+            for (int i = tid; i < BN * 8; i += 256) {
+                const int row = i >> 3, c = i & 7, n = n0 + row;
+                const bool ok = n < N;
+                cp_async16(w + row * WROW + c * 16, ok ? (const void*)(W.q8 + (size_t)n * K + kb0 * 32 + c * 16) : (const void*)W.q8, ok);
+            }
+        } else if (WT == W_Q4_0) {
+            for (int i = tid; i < BN * 4; i += 256) {
+                const int row = i >> 2, c = i & 3, n = n0 + row;
+                const bool ok = n < N;
+                cp_async16(w + row * WROW + c * 16, ok ? (const void*)(W.q4 + ((size_t)n * nb32 + kb0 + c) * 16) : (const void*)W.q4, ok);
+            }
+        } else {  // Q4_K: half a super-block (64 nibble bytes) per row per stage
+            const int sb = kb0 >> 3, half = (kb0 >> 2) & 1;
+            for (int i = tid; i < BN * 4; i += 256) {
+                const int row = i >> 2, c = i & 3, n = n0 + row;
+                const bool ok = n < N;
+                cp_async16(w + row * WROW + c * 16,
+                           ok ? (const void*)(W.q4 + ((size_t)n * nsb + sb) * 128 + half * 64 + c * 16) : (const void*)W.q4, ok);
+            }
+            for (int i = tid; i < BN; i += 256) {
+                const int n = n0 + i;
+                const bool ok = n < N;
+                cp_async16(sScm(buf) + i * 16, ok ? (const void*)(W.scm + ((size_t)n * nsb + sb) * 16) : (const void*)W.scm, ok);
+                cp_async4(sDd(buf) + 2 * i, ok ? (const void*)(W.d + (size_t)n * nsb + sb) : (const void*)W.d, ok);
+                cp_async4(sDd(buf) + 2 * i + 1, ok ? (const void*)(W.dmin + (size_t)n * nsb + sb) : (const void*)W.dmin, ok);
+            }
+        }
+        if (WT != W_Q4_K) {
+            for (int i = tid; i < BN; i += 256) {
+                const int n = n0 + i;
+                const bool ok = n < N;
+                cp_async16(sDw(buf) + i * KB, ok ? (const void*)(W.d + (size_t)n * nb32 + kb0) : (const void*)W.d, ok);
+            }
+        }
+        uint8_t* x = sX(buf);
+        for (int i = tid; i < BM * 8; i += 256) {
+            const int row = i >> 3, c = i & 7, m = m0 + row;
+            const bool ok = m < M;
+            cp_async16(x + row * XROW + c * 16, ok ? (const void*)(A.q + (size_t)m * K + kb0 * 32 + c * 16) : (const void*)A.q, ok);
+        }
+        for (int i = tid; i < BM; i += 256) {
+            const int m = m0 + i;
+            const bool ok = m < M;
+            if (WT == W_Q4_K) {
+                cp_async16(sDx(buf) + i * KB, ok ? (const void*)(A.bs + (size_t)m * nb32 + kb0) : (const void*)A.bs, ok);
+                cp_async4(sDx8(buf) + i, ok ? (const void*)(A.d + (size_t)m * nsb + (kb0 >> 3)) : (const void*)A.d, ok);
+            } else {
+                cp_async16(sDx(buf) + i * KB, ok ? (const void*)(A.d + (size_t)m * nb32 + kb0) : (const void*)A.d, ok);
+            }
+        }
+        cp_commit();
+    };
+
+    float acc[2][MT][4], accm[2][MT][4];
+    int sa[2][MT][4], sm[2][MT][4];
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+#pragma unroll
+        for (int j = 0; j < MT; ++j)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) { acc[i][j][e] = 0.0f; accm[i][j][e] = 0.0f; sa[i][j][e] = 0; sm[i][j][e] = 0; }
+
+    load_stage(0, 0);
+    for (int stg = 0; stg < nstage; ++stg) {
+        const int buf = stg & 1;
+        if (stg + 1 < nstage) {
+            load_stage(stg + 1, buf ^ 1);
+            cp_wait<1>();
+        } else {
+            cp_wait<0>();
+        }
+        __syncthreads();
+        const uint8_t* w = sW(buf);
+        const uint8_t* x = sX(buf);
+#pragma unroll
+        for (int blk = 0; blk < KB; ++blk) {
+            int af[2][4];
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+                const int r0 = wn * 32 + i * 16 + g;
+                if (WT == W_Q8_0) {
+                    af[i][0] = lds32(w + r0 * WROW + blk * 32 + t * 4);
+                    af[i][1] = lds32(w + (r0 + 8) * WROW + blk * 32 + t * 4);
+                    af[i][2] = lds32(w + r0 * WROW + blk * 32 + 16 + t * 4);
+                    af[i][3] = lds32(w + (r0 + 8) * WROW + blk * 32 + 16 + t * 4);
+                } else if (WT == W_Q4_0) {
+                    const int w0 = lds32(w + r0 * WROW + blk * 16 + t * 4);
+                    const int w1 = lds32(w + (r0 + 8) * WROW + blk * 16 + t * 4);
+                    af[i][0] = __vsub4(w0 & 0x0F0F0F0F, 0x08080808);
+                    af[i][1] = __vsub4(w1 & 0x0F0F0F0F, 0x08080808);
+                    af[i][2] = __vsub4((w0 >> 4) & 0x0F0F0F0F, 0x08080808);
+                    af[i][3] = __vsub4((w1 >> 4) & 0x0F0F0F0F, 0x08080808);
+                } else {
+                    // sub-block js = 4*half + blk of the super-block; local 32-byte chunk blk>>1,
+                    // nibble blk&1
+                    const int lc = blk >> 1, sh = (blk & 1) * 4;
+                    const int w0 = lds32(w + r0 * WROW + lc * 32 + t * 4);
+                    const int w1 = lds32(w + (r0 + 8) * WROW + lc * 32 + t * 4);
+                    const int w2 = lds32(w + r0 * WROW + lc * 32 + 16 + t * 4);
+                    const int w3 = lds32(w + (r0 + 8) * WROW + lc * 32 + 16 + t * 4);
+                    af[i][0] = (w0 >> sh) & 0x0F0F0F0F;
+                    af[i][1] = (w1 >> sh) & 0x0F0F0F0F;
+                    af[i][2] = (w2 >> sh) & 0x0F0F0F0F;
+                    af[i][3] = (w3 >> sh) & 0x0F0F0F0F;
+                }
+            }
+            int bf[MT][2];
+#pragma unroll
+            for (int j = 0; j < MT; ++j) {
+                const int mr = wm * (8 * MT) + j * 8 + g;
+                bf[j][0] = lds32(x + mr * XROW + blk * 32 + t * 4);
+                bf[j][1] = lds32(x + mr * XROW + blk * 32 + 16 + t * 4);
+            }
+            int is[2][MT][4];
+#pragma unroll
+            for (int i = 0; i < 2; ++i)
+#pragma unroll
+                for (int j = 0; j < MT; ++j)
+                    mma_s8(is[i][j], af[i][0], af[i][1], af[i][2], af[i][3], bf[j][0], bf[j][1]);
+            if (WT == W_Q4_K) {
+                const int js = ((stg & 1) << 2) + blk;   // sub-block index within the super-block
+                const uint8_t* scm = sScm(buf);
+                const int* bs = reinterpret_cast<const int*>(sDx(buf));
+#pragma unroll
+                for (int i = 0; i < 2; ++i) {
+                    const int nr = wn * 32 + i * 16 + g;
+                    const int sc0 = scm[nr * 16 + js], sc1 = scm[(nr + 8) * 16 + js];
+                    const int mn0 = scm[nr * 16 + 8 + js], mn1 = scm[(nr + 8) * 16 + 8 + js];
+#pragma unroll
+                    for (int j = 0; j < MT; ++j) {
+                        const int mr = wm * (8 * MT) + j * 8 + 2 * t;
+                        const int b0 = bs[mr * KB + blk], b1 = bs[(mr + 1) * KB + blk];
+                        sa[i][j][0] += sc0 * is[i][j][0]; sm[i][j][0] += mn0 * b0;
+                        sa[i][j][1] += sc0 * is[i][j][1]; sm[i][j][1] += mn0 * b1;
+                        sa[i][j][2] += sc1 * is[i][j][2]; sm[i][j][2] += mn1 * b0;
+                        sa[i][j][3] += sc1 * is[i][j][3]; sm[i][j][3] += mn1 * b1;
+                    }
+                }
+            } else {
+                const float* dw = sDw(buf);
+                const float* dx = sDx(buf);
+#pragma unroll
+                for (int i = 0; i < 2; ++i) {
+                    const int nr = wn * 32 + i * 16 + g;
+                    const float w0 = dw[nr * KB + blk], w1 = dw[(nr + 8) * KB + blk];
+#pragma unroll
+                    for (int j = 0; j < MT; ++j) {
+                        const int mr = wm * (8 * MT) + j * 8 + 2 * t;
+                        const float x0 = dx[mr * KB + blk], x1 = dx[(mr + 1) * KB + blk];
+                        acc[i][j][0] = __fmaf_rn(__fmul_rn(w0, x0), i2f_small(is[i][j][0]), acc[i][j][0]);
+                        acc[i][j][1] = __fmaf_rn(__fmul_rn(w0, x1), i2f_small(is[i][j][1]), acc[i][j][1]);
+                        acc[i][j][2] = __fmaf_rn(__fmul_rn(w1, x0), i2f_small(is[i][j][2]), acc[i][j][2]);
+                        acc[i][j][3] = __fmaf_rn(__fmul_rn(w1, x1), i2f_small(is[i][j][3]), acc[i][j][3]);
+                    }
+                }
+            }
+        }
+        if (WT == W_Q4_K && (stg & 1)) {   // end of a super-block: fold the integer sums
+            const float* dd = sDd(buf);
+            const float* dx8 = sDx8(buf);
+#pragma unroll
+            for (int i = 0; i < 2; ++i) {
+                const int nr = wn * 32 + i * 16 + g;
+                const float dw0 = dd[2 * nr], dm0 = dd[2 * nr + 1], dw1 = dd[2 * (nr + 8)], dm1 = dd[2 * (nr + 8) + 1];
+#pragma unroll
+                for (int j = 0; j < MT; ++j) {
+                    const int mr = wm * (8 * MT) + j * 8 + 2 * t;
+                    const float x0 = dx8[mr], x1 = dx8[mr + 1];
+                    const float wv[4] = {dw0, dw0, dw1, dw1}, mv[4] = {dm0, dm0, dm1, dm1}, xv[4] = {x0, x1, x0, x1};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        acc[i][j][e] = __fmaf_rn(__fmul_rn(xv[e], wv[e]), (float)sa[i][j][e], acc[i][j][e]);
+                        accm[i][j][e] = __fmaf_rn(__fmul_rn(-xv[e], mv[e]), (float)sm[i][j][e], accm[i][j][e]);
+                        sa[i][j][e] = 0;
+                        sm[i][j][e] = 0;
+                    }
+                }
+            }
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+#pragma unroll
+        for (int j = 0; j < MT; ++j)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int n = n0 + wn * 32 + i * 16 + g + ((e >> 1) << 3);
+                const int m = m0 + wm * (8 * MT) + j * 8 + 2 * t + (e & 1);
+                if (n < N && m < M) {
+                    float v = (WT == W_Q4_K) ? __fadd_rn(acc[i][j][e], accm[i][j][e]) : acc[i][j][e];
+                    if (bias) v = __fadd_rn(v, bias[n]);
+                    if (relu) v = (v > 0.0f) ? v : 0.0f;
+                    y[(size_t)m * N + n] = v;
+                }
+            }
+}
+
+template <int WT, int MT>
+static void launch_mma(const DevW& W, const ActQ& a, int M, const float* bias, int relu, float* y, cudaStream_t st) {
+    using C = Cfg<WT, MT>;
+    static bool configured = false;   // the attribute is per function; set once per process
+    if (!configured) {
+        cudaFuncSetAttribute(k_mm_mma<WT, MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+        configured = true;
+    }
+    dim3 grid((W.N + BN - 1) / BN, (M + C::BM - 1) / C::BM);
+    k_mm_mma<WT, MT><<<grid, 256, C::SMEM, st>>>(W, a, M, bias, relu, y);
+}
+
+bool matmul_mma(const DevW& W, const ActQ& a, int M, const float* bias, int relu, float* y, cudaStream_t st) {
+    if (W.K % (32 * KB)) return false;
+    // 64-row activation tiles when they still give two CTAs per SM, else 32-row tiles
+    const bool wide = (long)((W.N + BN - 1) / BN) * ((M + 63) / 64) >= 2 * 148;
+    switch (W.type) {
+        case W_Q8_0: wide ? launch_mma<W_Q8_0, 4>(W, a, M, bias, relu, y, st) : launch_mma<W_Q8_0, 2>(W, a, M, bias, relu, y, st); return true;
+        case W_Q4_0: wide ? launch_mma<W_Q4_0, 4>(W, a, M, bias, relu, y, st) : launch_mma<W_Q4_0, 2>(W, a, M, bias, relu, y, st); return true;
+        case W_Q4_K: launch_mma<W_Q4_K, 2>(W, a, M, bias, relu, y, st); return true;
+    }
+    return false;
+}
+
+}  // namespace t2sx

@@ -28,8 +28,8 @@
 //               strided sequential sums combined by an xor butterfly.
 //   flash_attn  K/V rounded to f16 by set_rows, Q rounded to f16; score = 32-term dot (4
 //               sequential fma chains of 8, summed pairwise) * (1/sqrt(32)); softmax-weighted V
-//               accumulated in f32 with the online (running-max) update.  Decode: 128 position
-//               lanes (lane = pos mod 128) merged by a butterfly; prefill: one sequential lane.
+//               accumulated in f32 with the online (running-max) update.  Decode: 32 position
+//               lanes (lane = pos mod 32) merged by an xor butterfly; prefill: one sequential lane.
 //               ggml's F16-V kernel keeps its VKQ accumulator in f16; this order keeps f32.
 //   exp         own Cody-Waite + degree-7 Taylor polynomial (t2s_expf below), identical on GPU.
 #include "t2s_oracle.h"
@@ -406,28 +406,24 @@ static inline AttnState st_merge(const AttnState& A, const AttnState& B) {
 }
 
 static const float kAttnScale = 1.0f / sqrtf(32.0f);
-static const int kAttnLanes = 128;
+static const int kAttnLanes = 32;
 
-// q holds the f32 values of the f16-rounded query.
+// q holds the f32 values of the f16-rounded query.  32 position lanes (lane = position mod 32,
+// ascending within a lane), merged in the order of an xor butterfly (partners 16, 8, 4, 2, 1).
 static void attn_decode_head(const float* q, const uint16_t* k, const uint16_t* v, int L,
                              int64_t stride, float* out) {
-    std::vector<AttnState> lane(kAttnLanes);
+    AttnState lane[kAttnLanes];
     for (auto& s : lane) st_empty(s);
     for (int i = 0; i < L; ++i) {
         const float s = dot32(q, k + i * stride) * kAttnScale;
         st_update(lane[i % kAttnLanes], s, v + i * stride);
     }
-    AttnState W[4];
-    for (int w = 0; w < 4; ++w) {
-        AttnState* ln = &lane[32 * w];
-        for (int off = 16; off >= 1; off >>= 1) {
-            AttnState t[32];
-            for (int l = 0; l < 32; ++l) t[l] = st_merge(ln[l], ln[l ^ off]);
-            for (int l = 0; l < 32; ++l) ln[l] = t[l];
-        }
-        W[w] = ln[0];
+    for (int off = 16; off >= 1; off >>= 1) {
+        AttnState t[kAttnLanes];
+        for (int l = 0; l < kAttnLanes; ++l) t[l] = st_merge(lane[l], lane[l ^ off]);
+        for (int l = 0; l < kAttnLanes; ++l) lane[l] = t[l];
     }
-    const AttnState R = st_merge(st_merge(W[0], W[1]), st_merge(W[2], W[3]));
+    const AttnState& R = lane[0];
     const float inv = 1.0f / R.l;
     for (int d = 0; d < 32; ++d) out[d] = R.o[d] * inv;
 }
