@@ -1085,6 +1085,10 @@ extern "C" int t2sx_weight_create(int32_t device, int32_t type, const void* host
     return T2SX_OK;
 }
 
+int32_t t2sx_weight_device_of(const t2sx_weight* w) { return w->device; }
+const DevW* t2sx_weight_devw_of(const t2sx_weight* w) { return &w->w; }
+int t2sx_set_error(int code, const char* msg) { return fail(code, "%s", msg); }
+
 extern "C" void t2sx_weight_free(t2sx_weight* w) {
     if (!w) return;
     cudaSetDevice(w->device);

@@ -53,7 +53,9 @@ SIGNATURES = {
     "t2sx_weight_create": (C.c_int, [_I, _I, _P, _I64, _I64, _P]),
     "t2sx_weight_free": (None, [_P]),
     "t2sx_matmul": (C.c_int, [_P, _P, _I64, _P, _P, _P]),
+    "t2sx_matmul_noalloc": (C.c_int, [_P, _P, _I64, _P, _P, _P]),
 }
+NOALLOC_MAX_ELEMS = 1 << 21
 
 
 class T2SXError(RuntimeError):
@@ -277,6 +279,11 @@ class Weight:
     def matmul(self, x_ptr: int, M: int, y_ptr: int, bias_ptr: int | None = None, stream: int = 0):
         _ck(lib().t2sx_matmul(self.h, C.c_void_p(x_ptr), M, None if bias_ptr is None else C.c_void_p(bias_ptr),
                               C.c_void_p(y_ptr), C.c_void_p(stream)))
+
+    def matmul_noalloc(self, x_ptr: int, M: int, y_ptr: int, bias_ptr: int | None = None, stream: int = 0):
+        """Same result as matmul(), using the library's fixed scratch instead of allocating."""
+        _ck(lib().t2sx_matmul_noalloc(self.h, C.c_void_p(x_ptr), M, None if bias_ptr is None else C.c_void_p(bias_ptr),
+                                      C.c_void_p(y_ptr), C.c_void_p(stream)))
 
     def close(self):
         if self.h:

@@ -149,6 +149,18 @@ T2SX_API void t2sx_weight_free(t2sx_weight* w);
 T2SX_API int t2sx_matmul(t2sx_weight* w, const float* x_dev, int64_t M, const float* bias_dev, float* y_dev,
                 void* stream);
 
+/* No counterpart in the reference (its ggml graphs allocate through the backend).  The same
+ * matmul as t2sx_matmul, for callers that cannot allocate device memory at call time -- e.g. a
+ * streaming server's synthesis thread, where cudaMalloc may synchronise the device and stall
+ * every other stream, or a host application that has pre-reserved the device memory budget.
+ * Scratch is a fixed array inside the library (every GPU that loads it holds about 4.5 MiB until
+ * exit); M * K must not exceed T2SX_NOALLOC_MAX_ELEMS or the call fails with T2SX_ERR_INVALID.
+ * The first call on a device looks up that array's device address (make it before any stream
+ * capture).  All calls share the array, so calls that overlap on the GPU race: serialise them. */
+#define T2SX_NOALLOC_MAX_ELEMS (1 << 21)
+T2SX_API int t2sx_matmul_noalloc(t2sx_weight* w, const float* x_dev, int64_t M, const float* bias_dev,
+                                 float* y_dev, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
