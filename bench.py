@@ -127,12 +127,13 @@ def run_ours(args):
     else:
         torch.cuda.set_device(local)
     t2sx_build.build()
+    import shard
     w = synth.WORKLOADS[args.workload]
     total_sessions = w["sessions"] if args.sessions is None else args.sessions * world
-    per = total_sessions // world
-    lo = rank * per
+    lo, hi = shard.session_shard(total_sessions, world, rank)
+    per = hi - lo
     lengths_all = session_prompts(args.workload, total_sessions)
-    mine = lengths_all[lo:lo + per]
+    mine = lengths_all[lo:hi]
     path = synth.ensure_gguf(w["wtype"], w["seed"], n_layer=24)
 
     W, K = args.warmup, args.steps
@@ -164,20 +165,10 @@ def run_ours(args):
             dist.barrier()
 
     def max_over_ranks(v: float) -> float:
-        if world == 1:
-            return v
-        import torch.distributed as dist
-        t = torch.tensor([v], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return shard.max_over_ranks(v, device="cuda")
 
     def sum_over_ranks(v: float) -> float:
-        if world == 1:
-            return v
-        import torch.distributed as dist
-        t = torch.tensor([v], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.SUM)
-        return float(t.item())
+        return shard.sum_over_ranks(v, device="cuda")
 
     # ---- warm-up: W host-driven steps (also captures the step graph) ----
     cur = first.copy()
