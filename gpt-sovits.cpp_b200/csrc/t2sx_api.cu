@@ -13,6 +13,7 @@
 #include <cstring>
 #include <map>
 #include <memory>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -305,6 +306,10 @@ struct LayerD {
 
 struct t2sx_model {
     int device = 0;
+    // A model freed while sessions still use it is released when the last of them is freed.
+    std::mutex mu;
+    int live_sessions = 0;
+    bool free_requested = false;
     uint32_t hp[9] = {512, 512, 16, 2048, 24, 1025, 732, 1024, 192};
     int32_t wtypes[4] = {-1, -1, -1, -1};
     char* arena = nullptr;
@@ -428,10 +433,20 @@ extern "C" int t2sx_model_load(const char* path, int32_t device, t2sx_model** ou
     return T2SX_OK;
 }
 
-extern "C" void t2sx_model_free(t2sx_model* m) {
-    if (!m) return;
+static void release_model(t2sx_model* m) {
     if (m->arena) { cudaSetDevice(m->device); cudaFree(m->arena); }
     delete m;
+}
+
+extern "C" void t2sx_model_free(t2sx_model* m) {
+    if (!m) return;
+    {
+        std::lock_guard<std::mutex> lk(m->mu);
+        if (m->free_requested) return;
+        m->free_requested = true;
+        if (m->live_sessions > 0) return;   // released by the last t2sx_session_free
+    }
+    release_model(m);
 }
 
 extern "C" int t2sx_model_hparams(const t2sx_model* m, uint32_t* hp, int32_t* wtypes) {
@@ -458,7 +473,7 @@ struct Work {
     uint16_t *q16, *ah;
     int8_t* aq;
     float* ad;
-    int32_t *abs, *row_slot, *row_pos, *row_L, *tok, *lastrow;
+    int32_t *abs, *row_slot, *row_pos, *row_L, *tok, *lastrow, *greedy;
 };
 
 static size_t work_bytes(int R, int V, int ff) {
@@ -468,7 +483,7 @@ static size_t work_bytes(int R, int V, int ff) {
     add((size_t)R * kD * 4); add((size_t)R * ff * 4); add((size_t)R * kD * 4); add((size_t)R * V * 4); add((size_t)R * kD * 4);
     add((size_t)R * kD * 2); add((size_t)R * ff * 2); add((size_t)R * ff); add((size_t)R * (ff / 32) * 4);
     add((size_t)R * (ff / 32) * 4);
-    for (int i = 0; i < 5; ++i) add((size_t)R * 4);
+    for (int i = 0; i < 6; ++i) add((size_t)R * 4);
     return b;
 }
 
@@ -489,12 +504,15 @@ static int work_alloc(Work& w, int R, int V, int ff) {
     w.abs = (int32_t*)take((size_t)R * (ff / 32) * 4);
     w.row_slot = (int32_t*)take((size_t)R * 4); w.row_pos = (int32_t*)take((size_t)R * 4);
     w.row_L = (int32_t*)take((size_t)R * 4); w.tok = (int32_t*)take((size_t)R * 4); w.lastrow = (int32_t*)take((size_t)R * 4);
+    w.greedy = (int32_t*)take((size_t)R * 4);
     w.cap = R;
     return T2SX_OK;
 }
 
 struct t2sx_session {
     const t2sx_model* m = nullptr;
+    int device = 0;
+    bool counted = false;          // holds a reference on the model
     int n_slots = 0, slot_size = 0, pages_per_slot = 0, n_layer = 0, V = 0, ff = 0;
     t2sx_sampler_config cfg{};
     cudaStream_t st = nullptr;
@@ -522,6 +540,10 @@ struct t2sx_session {
     int32_t* scratch_i = nullptr;  // [n_slots]
     int last_rows = 0;             // rows of the last logits
     const float* last_logits = nullptr;
+    const int32_t* last_greedy = nullptr;
+    float* noise = nullptr;        // [n_slots][V] Exp(1) noise by sorted position (stochastic sampling)
+    bool noise_on = false;
+    bool graph_noise = false;      // sampler kind captured in the step graph
     float last_ms = 0.0f;
     std::vector<int32_t> active;   // slots in row order
 };
@@ -572,17 +594,27 @@ static void run_layers(t2sx_session* s, Work& w, int T, bool decode) {
 
 static void free_session(t2sx_session* s) {
     if (!s) return;
-    cudaSetDevice(s->m->device);
+    cudaSetDevice(s->device);
     if (s->st) cudaStreamSynchronize(s->st);
     if (s->graph) cudaGraphExecDestroy(s->graph);
     for (void* p : {(void*)s->pool, (void*)s->ptab, (void*)s->n_pos, (void*)s->audio_off, (void*)s->token_in, (void*)s->cap,
                     (void*)s->err, (void*)s->seen, (void*)s->pe, (void*)s->dec.mem, (void*)s->pre.mem, (void*)s->ring,
-                    (void*)s->ring_step, (void*)s->scratch_i})
+                    (void*)s->ring_step, (void*)s->scratch_i, (void*)s->noise})
         if (p) cudaFree(p);
     if (s->ev0) cudaEventDestroy(s->ev0);
     if (s->ev1) cudaEventDestroy(s->ev1);
     if (s->st) cudaStreamDestroy(s->st);
+    t2sx_model* m = const_cast<t2sx_model*>(s->m);
+    const bool counted = s->counted;
     delete s;
+    if (m && counted) {
+        bool release = false;
+        {
+            std::lock_guard<std::mutex> lk(m->mu);
+            release = (--m->live_sessions == 0) && m->free_requested;
+        }
+        if (release) release_model(m);
+    }
 }
 
 extern "C" int t2sx_session_create(const t2sx_model* m, uint32_t n_slots, uint32_t slot_size, const t2sx_sampler_config* cfg,
@@ -594,6 +626,13 @@ extern "C" int t2sx_session_create(const t2sx_model* m, uint32_t n_slots, uint32
     CK(cudaSetDevice(m->device));
     t2sx_session* s = new t2sx_session();
     s->m = m;
+    s->device = m->device;
+    {
+        std::lock_guard<std::mutex> lk(const_cast<t2sx_model*>(m)->mu);
+        if (m->free_requested) { delete s; return fail(T2SX_ERR_STATE, "t2sx_session_create: model already freed"); }
+        ++const_cast<t2sx_model*>(m)->live_sessions;
+        s->counted = true;
+    }
     s->n_slots = (int)n_slots; s->slot_size = (int)slot_size;
     s->pages_per_slot = (int)((slot_size + kPage - 1) / kPage);
     s->n_layer = (int)m->hp[4]; s->V = (int)m->hp[5]; s->ff = (int)m->hp[3];
@@ -731,6 +770,9 @@ static int check_err_flag(t2sx_session* s) {
     return T2SX_OK;
 }
 
+static void run_sampler(t2sx_session* s, int T, const float* logits, const int32_t* row_slot, const uint8_t* seen,
+                        int32_t* tok, int32_t* greedy);
+
 extern "C" int t2sx_prefill(t2sx_session* s, int32_t n, const int32_t* slots, const int32_t* n_query, const int32_t* t_prompt,
                             const float* x, int32_t x_on_device, int32_t* tokens_out) {
     if (!s || n <= 0 || !slots || !n_query || !t_prompt || !x) return fail(T2SX_ERR_INVALID, "t2sx_prefill: bad arguments");
@@ -796,12 +838,13 @@ extern "C" int t2sx_prefill(t2sx_session* s, int32_t n, const int32_t* slots, co
         matmul(m->lm_head, a, ns, nullptr, 0, w.logits, s->st);
         for (int i = i0; i < i1; ++i) rs[i - i0] = slots[i];
         CK(cudaMemcpyAsync(w.row_slot, rs.data(), ns * 4, cudaMemcpyHostToDevice, s->st));
-        sample_greedy(ns, w.logits, s->V, w.row_slot, nullptr, 1.0f, 1.0f, s->cfg.eos_mask, (int)m->hp[7], w.tok, s->st);
+        run_sampler(s, ns, w.logits, w.row_slot, nullptr, w.tok, w.greedy);
         CK(cudaGetLastError());
         CK(cudaMemcpyAsync(toks.data() + i0, w.tok, ns * 4, cudaMemcpyDeviceToHost, s->st));
         CK(cudaStreamSynchronize(s->st));
         s->last_rows = ns;
         s->last_logits = w.logits;
+        s->last_greedy = w.greedy;
         xoff += rows;
         i0 = i1;
     }
@@ -825,6 +868,27 @@ extern "C" int t2sx_prefill(t2sx_session* s, int32_t n, const int32_t* slots, co
     return T2SX_OK;
 }
 
+// Sampler of one pass: the greedy argmax kernel, or the full chain when noise is set.
+static void run_sampler(t2sx_session* s, int T, const float* logits, const int32_t* row_slot, const uint8_t* seen,
+                        int32_t* tok, int32_t* greedy) {
+    const t2sx_model* m = s->m;
+    const float rp = s->cfg.repetition_penalty;
+    if (!s->noise_on) {
+        sample_greedy(T, logits, s->V, row_slot, seen, rp, 1.0f / rp, s->cfg.eos_mask, (int)m->hp[7], tok, greedy, s->st);
+        return;
+    }
+    SamplerArgs a;
+    a.top_k = s->cfg.top_k;
+    a.top_p = s->cfg.top_p;
+    a.inv_t = 1.0f / fmaxf(s->cfg.temperature, 1.0e-5f);
+    a.rp = rp;
+    a.inv_rp = 1.0f / rp;
+    a.eos_mask = s->cfg.eos_mask;
+    a.eos = (int)m->hp[7];
+    a.noise = s->noise;
+    sample_full(T, logits, s->V, row_slot, seen, a, tok, greedy, s->st);
+}
+
 // Record one decode step for the active rows on s->st (captured into the step graph).
 static void enqueue_step(t2sx_session* s) {
     const t2sx_model* m = s->m;
@@ -837,8 +901,7 @@ static void enqueue_step(t2sx_session* s) {
     ActQ a = act_of(w);
     quantize_act(m->lm_head.type, w.x, T, kD, a, s->st);
     matmul(m->lm_head, a, T, nullptr, 0, w.logits, s->st);
-    const float rp = s->cfg.repetition_penalty;
-    sample_greedy(T, w.logits, s->V, w.row_slot, s->seen, rp, 1.0f / rp, s->cfg.eos_mask, (int)m->hp[7], w.tok, s->st);
+    run_sampler(s, T, w.logits, w.row_slot, s->seen, w.tok, w.greedy);
     advance(T, w.row_slot, w.tok, s->token_in, s->n_pos, s->seen, s->V, s->ring, s->ring_len, s->ring_step, s->st);
 }
 
@@ -855,13 +918,16 @@ static int prepare_decode(t2sx_session* s, int n_steps) {
     if (s->dec_dirty) {
         CK(cudaMemcpyAsync(s->dec.row_slot, s->active.data(), T * 4, cudaMemcpyHostToDevice, s->st));
         CK(cudaStreamSynchronize(s->st));
-        if (s->graph && s->dec_rows != T) { cudaGraphExecDestroy(s->graph); s->graph = nullptr; }
+        CK(cudaGetLastError());
+        if (s->graph && (s->dec_rows != T || s->graph_noise != s->noise_on)) { cudaGraphExecDestroy(s->graph); s->graph = nullptr; }
         if (!s->graph) {
             cudaGraph_t g;
             CK(cudaStreamBeginCapture(s->st, cudaStreamCaptureModeThreadLocal));
             enqueue_step(s);
             cudaError_t e = cudaStreamEndCapture(s->st, &g);
             if (e != cudaSuccess) return fail(T2SX_ERR_CUDA, "decode graph capture: %s", cudaGetErrorString(e));
+            e = cudaGetLastError();
+            if (e != cudaSuccess) { cudaGraphDestroy(g); return fail(T2SX_ERR_CUDA, "decode step launch during capture: %s", cudaGetErrorString(e)); }
             size_t nn = 0;
             cudaGraphGetNodes(g, nullptr, &nn);
             std::vector<cudaGraphNode_t> nodes(nn);
@@ -875,6 +941,7 @@ static int prepare_decode(t2sx_session* s, int n_steps) {
             cudaGraphDestroy(g);
             if (e != cudaSuccess) { s->graph = nullptr; return fail(T2SX_ERR_CUDA, "decode graph instantiate: %s", cudaGetErrorString(e)); }
             s->dec_rows = T;
+            s->graph_noise = s->noise_on;
         }
         s->dec_dirty = false;
     }
@@ -888,6 +955,7 @@ static int launch_steps(t2sx_session* s, int n_steps) {
     for (int sl : s->active) s->n_pos_h[sl] += n_steps;
     s->last_rows = (int)s->active.size();
     s->last_logits = s->dec.logits;
+    s->last_greedy = s->dec.greedy;
     return T2SX_OK;
 }
 
@@ -895,6 +963,10 @@ extern "C" int t2sx_decode_async(t2sx_session* s, int32_t n_steps) {
     if (!s || n_steps < 0) return fail(T2SX_ERR_INVALID, "t2sx_decode_async: bad arguments");
     if (n_steps == 0) return T2SX_OK;
     CK(cudaSetDevice(s->m->device));
+    {
+        const cudaError_t stale = cudaGetLastError();
+        if (stale != cudaSuccess) return fail(T2SX_ERR_CUDA, "pending CUDA error before decode: %s", cudaGetErrorString(stale));
+    }
     int rc;
     if ((rc = prepare_decode(s, n_steps))) return rc;
     CK(cudaMemsetAsync(s->ring_step, 0, 4, s->st));
@@ -913,6 +985,10 @@ extern "C" int t2sx_decode(t2sx_session* s, int32_t n_steps, int32_t* tokens_out
     if (!s || n_steps < 0) return fail(T2SX_ERR_INVALID, "t2sx_decode: bad arguments");
     if (n_steps == 0) return T2SX_OK;
     CK(cudaSetDevice(s->m->device));
+    {
+        const cudaError_t stale = cudaGetLastError();
+        if (stale != cudaSuccess) return fail(T2SX_ERR_CUDA, "pending CUDA error before decode: %s", cudaGetErrorString(stale));
+    }
     int rc;
     if ((rc = prepare_decode(s, n_steps))) return rc;
     const int T = (int)s->active.size();
@@ -941,6 +1017,10 @@ __global__ void k_scatter_tokens(int T, const int32_t* row_slot, const int32_t* 
 extern "C" int t2sx_decode_step_host(t2sx_session* s, const int32_t* tokens_in, int32_t* tokens_out) {
     if (!s) return fail(T2SX_ERR_INVALID, "null session");
     CK(cudaSetDevice(s->m->device));
+    {
+        const cudaError_t stale = cudaGetLastError();
+        if (stale != cudaSuccess) return fail(T2SX_ERR_CUDA, "pending CUDA error before decode: %s", cudaGetErrorString(stale));
+    }
     int rc;
     if ((rc = prepare_decode(s, 1))) return rc;
     const int T = (int)s->active.size();
@@ -1046,6 +1126,30 @@ extern "C" int t2sx_profile_step(t2sx_session* s, int32_t iters, float* ms) {
     if ((rc = timeit(6, [&] { residual_layernorm(T, w.ln1, w.f, L.ln2_w, L.ln2_b, 1e-5f, w.o, s->st); }))) return rc;
     if ((rc = timeit(7, [&] { quantize_act(L.down.type, w.h, T, s->ff, a, s->st); }))) return rc;
     CK(cudaGetLastError());
+    return T2SX_OK;
+}
+
+extern "C" int t2sx_set_exp_noise(t2sx_session* s, const float* noise, int32_t rows) {
+    if (!s || rows < 0 || rows > s->n_slots) return fail(T2SX_ERR_INVALID, "t2sx_set_exp_noise: bad arguments");
+    CK(cudaSetDevice(s->m->device));
+    const bool on = noise != nullptr && rows > 0;
+    if (on) {
+        if (!s->noise) CK(cudaMalloc(&s->noise, (size_t)s->n_slots * s->V * 4));
+        CK(cudaMemcpyAsync(s->noise, noise, (size_t)rows * s->V * 4, cudaMemcpyHostToDevice, s->st));
+        CK(cudaStreamSynchronize(s->st));
+    }
+    if (on != s->noise_on) { s->noise_on = on; s->dec_dirty = true; }
+    return T2SX_OK;
+}
+
+extern "C" int t2sx_read_greedy(t2sx_session* s, int32_t* out, int32_t max_rows, int32_t* rows) {
+    if (!s || !out) return fail(T2SX_ERR_INVALID, "null argument");
+    if (!s->last_greedy) return fail(T2SX_ERR_STATE, "no pass has run yet");
+    CK(cudaSetDevice(s->m->device));
+    CK(cudaStreamSynchronize(s->st));
+    const int n = s->last_rows < max_rows ? s->last_rows : max_rows;
+    CK(cudaMemcpy(out, s->last_greedy, (size_t)n * 4, cudaMemcpyDeviceToHost));
+    if (rows) *rows = n;
     return T2SX_OK;
 }
 

@@ -635,7 +635,7 @@ void residual_layernorm(int T, const float* a, const float* b, const float* g, c
 // then the first index of the maximum = sorted_indices[0] of the descending argsort).
 __global__ void k_sample_greedy(const float* __restrict__ logits, int V, const int32_t* __restrict__ row_slot,
                                 const uint8_t* __restrict__ seen, float rp, float inv_rp, int eos_mask, int eos,
-                                int32_t* __restrict__ tok_out) {
+                                int32_t* __restrict__ tok_out, int32_t* __restrict__ greedy_out) {
     __shared__ float s_v[8];
     __shared__ int s_i[8];
     const int r = blockIdx.x;
@@ -652,7 +652,7 @@ __global__ void k_sample_greedy(const float* __restrict__ logits, int V, const i
             const float s = sn[v] ? 1.0f : 0.0f;
             l = __fadd_rn(l, __fmul_rn(s, __fsub_rn(sel, l)));
         }
-        if (eos_mask && v == eos) l = __int_as_float(0xff800000);
+        if (eos_mask && v == eos) l = kEosMasked;
         if (l > best || bi == 0x7fffffff) { best = l; bi = v; }
     }
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -668,12 +668,149 @@ __global__ void k_sample_greedy(const float* __restrict__ logits, int V, const i
         for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
             if (s_v[w] > best || (s_v[w] == best && s_i[w] < bi)) { best = s_v[w]; bi = s_i[w]; }
         tok_out[r] = bi;
+        if (greedy_out) greedy_out[r] = bi;
+    }
+}
+
+// ---- full sampler chain (block.cpp:52-115, 191-271) ----------------------------------------
+// One CTA of 1024 threads per row: repetition penalty, descending argsort of the 1025 logits by a
+// bitonic network over 2048 (key, index) pairs (ties by lower index; padding sorts last), then in
+// sorted order: top-p (softmax, sequential f32 cumsum, first position above the threshold kept),
+// temperature, top-k by pivot, softmax, argmax of probs / noise (noise indexed by sorted position).
+constexpr int kSortN = 2048;
+
+__device__ void softmax_block(float* s, float* p, int n, double* s_lane, float* s_scalar) {
+    const int tid = threadIdx.x;
+    const float mx = s[0];   // rows are sorted in descending order and filters keep position 0
+    for (int i = tid; i < n; i += blockDim.x) p[i] = t2s_expf(__fsub_rn(s[i], mx));
+    __syncthreads();
+    if (tid < 32) {
+        double acc = 0.0;
+        for (int i = tid; i < n; i += 32) acc = __dadd_rn(acc, (double)p[i]);
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) acc = __dadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, off));
+        if (tid == 0) s_scalar[0] = __double2float_rn(__ddiv_rn(1.0, acc));
+    }
+    __syncthreads();
+    const float inv = s_scalar[0];
+    for (int i = tid; i < n; i += blockDim.x) p[i] = __fmul_rn(p[i], inv);
+    __syncthreads();
+}
+
+__global__ void __launch_bounds__(1024) k_sample_full(const float* __restrict__ logits, int V,
+                                                      const int32_t* __restrict__ row_slot,
+                                                      const uint8_t* __restrict__ seen, SamplerArgs a,
+                                                      int32_t* __restrict__ tok_out, int32_t* __restrict__ greedy_out) {
+    __shared__ float key[kSortN];
+    __shared__ int idx[kSortN];
+    __shared__ float prob[kSortN];
+    __shared__ double s_lane[32];
+    __shared__ float s_scalar[2];
+    __shared__ int s_cut;
+    __shared__ float s_bv[32];
+    __shared__ int s_bi[32];
+    const int r = blockIdx.x, tid = threadIdx.x;
+    const float* lg = logits + (size_t)r * V;
+    const uint8_t* sn = seen ? seen + (size_t)row_slot[r] * V : nullptr;
+    for (int i = tid; i < kSortN; i += blockDim.x) {
+        float l = __int_as_float(0xff800000);
+        int id = 0x7fffffff;
+        if (i < V) {
+            l = lg[i];
+            if (sn && a.rp != 1.0f) {
+                const float pos = __fmul_rn(l, a.inv_rp), neg = __fmul_rn(l, a.rp);
+                const float negm = (-l > 0.0f) ? 1.0f : 0.0f;
+                const float sel = __fadd_rn(pos, __fmul_rn(negm, __fsub_rn(neg, pos)));
+                const float sv = sn[i] ? 1.0f : 0.0f;
+                l = __fadd_rn(l, __fmul_rn(sv, __fsub_rn(sel, l)));
+            }
+            if (a.eos_mask && i == a.eos) l = kEosMasked;
+            id = i;
+        }
+        key[i] = l;
+        idx[i] = id;
+    }
+    __syncthreads();
+    // bitonic sort, descending by key, ascending by index on equal keys
+    for (int k = 2; k <= kSortN; k <<= 1) {
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            for (int t = tid; t < kSortN / 2; t += blockDim.x) {
+                const int i = 2 * t - (t & (j - 1));
+                const int p = i + j;
+                const float ki = key[i], kp = key[p];
+                const int ii = idx[i], ip = idx[p];
+                const bool i_first = (ki > kp) || (ki == kp && ii < ip);
+                const bool desc = (i & k) == 0;
+                if (desc != i_first) { key[i] = kp; key[p] = ki; idx[i] = ip; idx[p] = ii; }
+            }
+            __syncthreads();
+        }
+    }
+    if (tid == 0) greedy_out[r] = idx[0];
+    if (!a.noise) {
+        if (tid == 0) tok_out[r] = idx[0];
+        return;
+    }
+    float* s = key;
+    if (a.top_p < 1.0f && V > 1) {
+        softmax_block(s, prob, V, s_lane, s_scalar);
+        if (tid == 0) {
+            float cum = 0.0f;
+            int cut = V;
+            for (int i = 0; i < V; ++i) {
+                cum = __fadd_rn(cum, prob[i]);
+                if (__fsub_rn(cum, a.top_p) > 0.0f) { cut = i + 1; break; }
+            }
+            s_cut = cut;
+        }
+        __syncthreads();
+        for (int i = s_cut + tid; i < V; i += blockDim.x) s[i] = __fadd_rn(s[i], __fsub_rn(-1.0e10f, s[i]));
+        __syncthreads();
+    }
+    for (int i = tid; i < V; i += blockDim.x) s[i] = __fmul_rn(s[i], a.inv_t);
+    __syncthreads();
+    if (a.top_k > 0 && a.top_k < V) {
+        const float pivot = s[a.top_k - 1];
+        __syncthreads();
+        for (int i = tid; i < V; i += blockDim.x)
+            if (__fsub_rn(pivot, s[i]) > 0.0f) s[i] = __fadd_rn(s[i], __fsub_rn(-1.0e10f, s[i]));
+        __syncthreads();
+    }
+    softmax_block(s, prob, V, s_lane, s_scalar);
+    const float* nz = a.noise + (size_t)r * V;
+    float bv = 0.0f;
+    int bi = 0x7fffffff;
+    for (int i = tid; i < V; i += blockDim.x) {
+        const float sc = __fdiv_rn(prob[i], nz[i]);
+        if (bi == 0x7fffffff || sc > bv) { bv = sc; bi = i; }
+    }
+    const int lane = tid & 31, warp = tid >> 5;
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+        if (oi != 0x7fffffff && (bi == 0x7fffffff || ov > bv || (ov == bv && oi < bi))) { bv = ov; bi = oi; }
+    }
+    if (lane == 0) { s_bv[warp] = bv; s_bi[warp] = bi; }
+    __syncthreads();
+    if (tid == 0) {
+        for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
+            if (s_bi[w] != 0x7fffffff && (bi == 0x7fffffff || s_bv[w] > bv || (s_bv[w] == bv && s_bi[w] < bi))) {
+                bv = s_bv[w];
+                bi = s_bi[w];
+            }
+        tok_out[r] = idx[bi];
     }
 }
 
 void sample_greedy(int T, const float* logits, int V, const int32_t* row_slot, const uint8_t* seen, float rp,
-                   float inv_rp, int eos_mask, int eos, int32_t* tok_out, cudaStream_t st) {
-    if (T > 0) k_sample_greedy<<<T, 256, 0, st>>>(logits, V, row_slot, seen, rp, inv_rp, eos_mask, eos, tok_out);
+                   float inv_rp, int eos_mask, int eos, int32_t* tok_out, int32_t* greedy_out, cudaStream_t st) {
+    if (T > 0) k_sample_greedy<<<T, 256, 0, st>>>(logits, V, row_slot, seen, rp, inv_rp, eos_mask, eos, tok_out, greedy_out);
+}
+
+void sample_full(int T, const float* logits, int V, const int32_t* row_slot, const uint8_t* seen, const SamplerArgs& a,
+                 int32_t* tok_out, int32_t* greedy_out, cudaStream_t st) {
+    if (T > 0) k_sample_full<<<T, 1024, 0, st>>>(logits, V, row_slot, seen, a, tok_out, greedy_out);
 }
 
 // End of a decode step (session.cpp:247-284 on the device): feed the sampled token back,

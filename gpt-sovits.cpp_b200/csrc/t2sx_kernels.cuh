@@ -69,8 +69,20 @@ void attention_prefill(int T, const uint16_t* q16, Rows rows, KVView kv, int lay
                        cudaStream_t st);
 void residual_layernorm(int T, const float* a, const float* b, const float* g, const float* beta, float eps,
                         float* y, cudaStream_t st);
+// Logit given to EOS when EOS is masked (finite, so the masked-lerp filters stay finite).
+constexpr float kEosMasked = -1.0e30f;
 void sample_greedy(int T, const float* logits, int V, const int32_t* row_slot, const uint8_t* seen, float rp,
-                   float inv_rp, int eos_mask, int eos, int32_t* tok_out, cudaStream_t st);
+                   float inv_rp, int eos_mask, int eos, int32_t* tok_out, int32_t* greedy_out, cudaStream_t st);
+struct SamplerArgs {
+    int top_k;
+    float top_p;
+    float inv_t;       // 1 / max(temperature, 1e-5)
+    float rp, inv_rp;  // repetition penalty and its reciprocal
+    int eos_mask, eos;
+    const float* noise;  // [rows][V] Exp(1) noise by sorted position, or null (greedy)
+};
+void sample_full(int T, const float* logits, int V, const int32_t* row_slot, const uint8_t* seen, const SamplerArgs& a,
+                 int32_t* tok_out, int32_t* greedy_out, cudaStream_t st);
 void advance(int T, const int32_t* row_slot, const int32_t* tok, int32_t* token_in, int32_t* n_pos, uint8_t* seen,
              int V, int32_t* ring, int ring_len, int32_t* ring_step, cudaStream_t st);
 void gather_rows(int n, const float* src, const int32_t* idx, int ld, float* dst, cudaStream_t st);

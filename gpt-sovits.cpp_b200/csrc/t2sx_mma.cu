@@ -291,7 +291,8 @@ static void launch_mma(const DevW& W, const ActQ& a, int M, const float* bias, i
     using C = Cfg<WT, MT>;
     static bool configured = false;   // the attribute is per function; set once per process
     if (!configured) {
-        cudaFuncSetAttribute(k_mm_mma<WT, MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+        if (cudaFuncSetAttribute(k_mm_mma<WT, MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess)
+            return;   // the launch below then fails and the caller's launch check reports it
         configured = true;
     }
     dim3 grid((W.N + BN - 1) / BN, (M + C::BM - 1) / C::BM);

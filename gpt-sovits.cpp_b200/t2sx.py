@@ -48,6 +48,8 @@ SIGNATURES = {
     "t2sx_read_kv": (C.c_int, [_P, _I, _I, _I, _P]),
     "t2sx_set_seen": (C.c_int, [_P, _I, _P]),
     "t2sx_last_decode_ms": (C.c_int, [_P, _P]),
+    "t2sx_set_exp_noise": (C.c_int, [_P, _P, _I]),
+    "t2sx_read_greedy": (C.c_int, [_P, _P, _I, _P]),
     "t2sx_decode_graph_kernels": (C.c_int, [_P, _P]),
     "t2sx_profile_step": (C.c_int, [_P, _I, _P]),
     "t2sx_weight_create": (C.c_int, [_I, _I, _P, _I64, _I64, _P]),
@@ -250,6 +252,21 @@ class Session:
         if rc < 0 or rc != n:
             _ck(rc if rc > 0 else ERR_INVALID)
         return out[:n]
+
+    def set_exp_noise(self, noise):
+        """Exp(1) noise [rows][vocab] for the following passes (None: back to greedy)."""
+        if noise is None:
+            _ck(lib().t2sx_set_exp_noise(self.h, None, 0))
+            return
+        noise = np.ascontiguousarray(noise, dtype=np.float32).reshape(-1, self.model.vocab)
+        _ck(lib().t2sx_set_exp_noise(self.h, _p(noise), noise.shape[0]))
+
+    def read_greedy(self, max_rows: int | None = None):
+        max_rows = max_rows or self.n_slots
+        out = np.zeros(max_rows, dtype=np.int32)
+        rows = C.c_int32(0)
+        _ck(lib().t2sx_read_greedy(self.h, _p(out), max_rows, C.byref(rows)))
+        return out[: rows.value]
 
     def set_seen(self, slot: int, seen):
         seen = np.ascontiguousarray(seen, dtype=np.uint8)

@@ -125,6 +125,15 @@ T2SX_API int t2sx_read_kv(t2sx_session* s, int32_t slot, int32_t layer, int32_t 
 /* Seen-token mask used by the repetition penalty (t2s_session_get_seen_mask, t2s.h:487): set
  * one slot's mask (uint8 [vocab], nonzero = seen).  The device marks every sampled token. */
 T2SX_API int t2sx_set_seen(t2sx_session* s, int32_t slot, const uint8_t* seen);
+/* Stochastic sampling (exp_noise input of the reference sampler, t2s.h:27-28,488): noise holds
+ * rows x vocab Exp(1) samples (host), row i used by pass row i (decode: active slots in row order;
+ * prefill: slots in call order) and indexed by *sorted* position, as in the reference graph
+ * (score = probs_sorted / noise, block.cpp:258-267).  The full chain -- repetition penalty,
+ * argsort, top-p, temperature, top-k, softmax, argmax(probs / noise) -- then replaces the greedy
+ * pick for every following pass until noise is set again; noise == NULL returns to greedy. */
+T2SX_API int t2sx_set_exp_noise(t2sx_session* s, const float* noise, int32_t rows);
+/* Greedy (argmax) tokens of the last pass, next to the sampled ones (t2s_session_get_greedy). */
+T2SX_API int t2sx_read_greedy(t2sx_session* s, int32_t* out, int32_t max_rows, int32_t* rows);
 /* Device time of the last t2sx_decode / t2sx_decode_async batch or t2sx_decode_step_host step
  * (graph execution only, without the host copies), in ms (CUDA events). */
 T2SX_API int t2sx_last_decode_ms(t2sx_session* s, float* ms);

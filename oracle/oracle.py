@@ -49,6 +49,8 @@ def lib():
             "orc_prefill": (I, [P, I, P, I, I, I, P, P, P]),
             "orc_decode_step": (I, [P, I, P, P, P, F, I, P, P]),
             "orc_slot_n_pos": (I, [P, I]), "orc_read_kv": (I, [P, I, I, I, P]),
+            "orc_sample": (I, [P, I, P, P, P, I, F, F, F, I, P, P]),
+            "orc_decode_step2": (I, [P, I, P, P, P, P, I, F, F, F, I, P, P, P]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -109,6 +111,18 @@ class Model:
         assert rc == 0
         return x
 
+    def sample(self, logits, seen=None, noise=None, top_k=15, top_p=1.0, temperature=1.0, rep_penalty=1.0,
+               eos_mask=True):
+        logits = np.ascontiguousarray(logits, dtype=np.float32).reshape(-1, self.vocab)
+        n = logits.shape[0]
+        seen_a = None if seen is None else np.ascontiguousarray(seen, dtype=np.float32).reshape(n, self.vocab)
+        noise_a = None if noise is None else np.ascontiguousarray(noise, dtype=np.float32).reshape(n, self.vocab)
+        sampled = np.zeros(n, dtype=np.int32)
+        greedy = np.zeros(n, dtype=np.int32)
+        lib().orc_sample(self.h, n, ptr(logits), ptr(seen_a), ptr(noise_a), int(top_k), float(top_p),
+                         float(temperature), float(rep_penalty), int(eos_mask), ptr(sampled), ptr(greedy))
+        return sampled, greedy
+
     def close(self):
         if self.h:
             lib().orc_model_free(self.h)
@@ -149,6 +163,22 @@ class Session:
         if rc != 0:
             raise RuntimeError("oracle decode rejected")
         return out, logits
+
+    def decode_sampled(self, slots, tokens, noise, seen=None, top_k=15, top_p=1.0, temperature=1.0,
+                       rep_penalty=1.0, eos_mask=True):
+        slots = np.ascontiguousarray(slots, dtype=np.int32)
+        tokens = np.ascontiguousarray(tokens, dtype=np.int32)
+        n, V = slots.size, self.model.vocab
+        noise_a = None if noise is None else np.ascontiguousarray(noise, dtype=np.float32).reshape(n, V)
+        seen_a = None if seen is None else np.ascontiguousarray(seen, dtype=np.float32).reshape(n, V)
+        sampled = np.empty(n, dtype=np.int32)
+        greedy = np.empty(n, dtype=np.int32)
+        rc = lib().orc_decode_step2(self.h, n, ptr(slots), ptr(tokens), ptr(seen_a), ptr(noise_a), int(top_k),
+                                    float(top_p), float(temperature), float(rep_penalty), int(eos_mask),
+                                    ptr(sampled), ptr(greedy), None)
+        if rc != 0:
+            raise RuntimeError("oracle decode rejected")
+        return sampled, greedy
 
     def n_pos(self, slot):
         return lib().orc_slot_n_pos(self.h, slot)

@@ -651,9 +651,15 @@ static void forward_rows(Session* S, int64_t T, const int* slot, const int* pos,
     }
 }
 
-// Greedy pick over penalised logits (block.cpp:117-138, 221, 319-323).  EOS masking is a
-// harness rule (the reference sampler has no EOS input): logit[eos] := -inf after the penalty.
-static int32_t pick_greedy(Model* m, float* logits, const float* seen, float rp, int eos_mask) {
+// Logit given to EOS when EOS is masked (a harness rule: the reference sampler has no EOS
+// input).  Finite, so that ggml's masked-lerp filters (base + m*(fill - base)) stay finite.
+static const float kEosMasked = -1.0e30f;
+static const float kMaskLogit = -1.0e10f;   // block.cpp:10
+
+struct SamplerCfg { int top_k; float top_p; float temperature; float rp; int eos_mask; };
+
+// Repetition penalty (block.cpp:117-138) as ggml's op sequence, then the EOS rule.
+static void penalise(Model* m, float* logits, const float* seen, float rp, int eos_mask) {
     const int V = (int)m->hp[5];
     if (seen && rp != 1.0f) {
         const float inv = 1.0f / rp;
@@ -666,10 +672,83 @@ static int32_t pick_greedy(Model* m, float* logits, const float* seen, float rp,
             logits[v] = l + s * (sel - l);
         }
     }
-    if (eos_mask && (int)m->hp[7] < V) logits[m->hp[7]] = -INFINITY;
+    if (eos_mask && (int)m->hp[7] < V) logits[m->hp[7]] = kEosMasked;
+}
+
+// Greedy pick (block.cpp:221, 319-323): the first index of the maximum.
+static int32_t pick_greedy(Model* m, float* logits, const float* seen, float rp, int eos_mask) {
+    const int V = (int)m->hp[5];
+    penalise(m, logits, seen, rp, eos_mask);
     int best = 0;
     for (int v = 1; v < V; ++v) if (logits[v] > logits[best]) best = v;
     return best;
+}
+
+// ggml_soft_max over n values: e^(x - max) with the own exp, double sum (32 strided lanes
+// combined by an xor butterfly), scale by (float)(1/sum).
+static void softmax_canon(const float* x, int n, float* p) {
+    float mx = x[0];
+    for (int i = 1; i < n; ++i) if (x[i] > mx) mx = x[i];
+    double lane[32] = {0};
+    for (int i = 0; i < n; ++i) {
+        p[i] = t2s_expf(x[i] - mx);
+        lane[i % 32] += (double)p[i];
+    }
+    const float inv = (float)(1.0 / lanes_sum(lane));
+    for (int i = 0; i < n; ++i) p[i] = p[i] * inv;
+}
+
+// Full sampler chain of one row (block.cpp:52-115, 191-271): penalty, descending argsort (ties
+// by lower index), top-p on the sorted softmax (sequential f32 cumsum, first token above the
+// threshold kept), temperature, top-k by pivot, softmax, argmax of probs / noise, where noise is
+// indexed by sorted position as in the reference graph.  Returns the sampled token.
+static int32_t sample_row(Model* m, const float* logits_in, const float* seen, const float* noise,
+                          const SamplerCfg& c, int32_t* greedy_out) {
+    const int V = (int)m->hp[5];
+    std::vector<float> l(logits_in, logits_in + V);
+    penalise(m, l.data(), seen, c.rp, c.eos_mask);
+    std::vector<int> idx(V);
+    for (int i = 0; i < V; ++i) idx[i] = i;
+    std::sort(idx.begin(), idx.end(), [&](int a, int b) { return l[a] > l[b] || (l[a] == l[b] && a < b); });
+    *greedy_out = idx[0];
+    if (!noise) return idx[0];
+    std::vector<float> s(V), p(V);
+    for (int i = 0; i < V; ++i) s[i] = l[idx[i]];
+    if (c.top_p < 1.0f && V > 1) {
+        softmax_canon(s.data(), V, p.data());
+        float cum = 0.0f;
+        int cut = V;
+        for (int i = 0; i < V; ++i) {
+            cum = cum + p[i];
+            if (cum - c.top_p > 0.0f) { cut = i + 1; break; }
+        }
+        for (int i = cut; i < V; ++i) s[i] = s[i] + (kMaskLogit - s[i]);
+    }
+    const float inv_t = 1.0f / fmaxf(c.temperature, 1.0e-5f);
+    for (int i = 0; i < V; ++i) s[i] = s[i] * inv_t;
+    if (c.top_k > 0 && c.top_k < V) {
+        const float pivot = s[c.top_k - 1];
+        for (int i = 0; i < V; ++i) if (pivot - s[i] > 0.0f) s[i] = s[i] + (kMaskLogit - s[i]);
+    }
+    softmax_canon(s.data(), V, p.data());
+    int best = 0;
+    float best_v = p[0] / noise[0];
+    for (int i = 1; i < V; ++i) {
+        const float sc = p[i] / noise[i];
+        if (sc > best_v) { best_v = sc; best = i; }
+    }
+    return idx[best];
+}
+
+int orc_sample(void* model, int n, const float* logits, const float* seen, const float* noise, int top_k, float top_p,
+               float temperature, float rp, int eos_mask, int32_t* sampled, int32_t* greedy) {
+    Model* m = (Model*)model;
+    const int V = (int)m->hp[5];
+    const SamplerCfg c{top_k, top_p, temperature, rp, eos_mask};
+    for (int r = 0; r < n; ++r)
+        sampled[r] = sample_row(m, logits + (size_t)r * V, seen ? seen + (size_t)r * V : nullptr,
+                                noise ? noise + (size_t)r * V : nullptr, c, &greedy[r]);
+    return 0;
 }
 
 int orc_prefill(void* sess, int slot, const float* x, int nq, int T_prompt, int eos_mask, int32_t* token_out, float* logits_out,
@@ -697,9 +776,8 @@ int orc_prefill(void* sess, int slot, const float* x, int nq, int T_prompt, int 
     return 0;
 }
 
-int orc_decode_step(void* sess, int n, const int32_t* slots, const int32_t* tokens_in, const float* seen, float rp,
-                    int eos_mask, int32_t* tokens_out, float* logits_out) {
-    Session* S = (Session*)sess;
+// Forward of one decode step for n slots; fills logits [n][V] and advances n_pos.
+static int decode_forward(Session* S, int n, const int32_t* slots, const int32_t* tokens_in, std::vector<float>& logits) {
     Model* m = S->m;
     const int d = (int)m->hp[1], V = (int)m->hp[5];
 #ifdef _OPENMP
@@ -721,14 +799,32 @@ int orc_decode_step(void* sess, int n, const int32_t* slots, const int32_t* toke
         sl[i] = s; pos[i] = S->n_pos[s]; L[i] = S->n_pos[s] + 1;
     }
     forward_rows(S, n, sl.data(), pos.data(), L.data(), true, x.data());
-    std::vector<float> logits((size_t)n * V);
+    logits.assign((size_t)n * V, 0.0f);
     matmul_rows(m->lm_head, nullptr, x.data(), n, logits.data());
-    if (logits_out) memcpy(logits_out, logits.data(), sizeof(float) * logits.size());
-    for (int i = 0; i < n; ++i) {
-        tokens_out[i] = pick_greedy(m, &logits[(size_t)i * V], seen ? seen + (size_t)i * V : nullptr, rp, eos_mask);
-        S->n_pos[slots[i]] += 1;
-    }
+    for (int i = 0; i < n; ++i) S->n_pos[slots[i]] += 1;
     return 0;
+}
+
+int orc_decode_step(void* sess, int n, const int32_t* slots, const int32_t* tokens_in, const float* seen, float rp,
+                    int eos_mask, int32_t* tokens_out, float* logits_out) {
+    Session* S = (Session*)sess;
+    const int V = (int)S->m->hp[5];
+    std::vector<float> logits;
+    if (decode_forward(S, n, slots, tokens_in, logits)) return -1;
+    if (logits_out) memcpy(logits_out, logits.data(), sizeof(float) * logits.size());
+    for (int i = 0; i < n; ++i)
+        tokens_out[i] = pick_greedy(S->m, &logits[(size_t)i * V], seen ? seen + (size_t)i * V : nullptr, rp, eos_mask);
+    return 0;
+}
+
+int orc_decode_step2(void* sess, int n, const int32_t* slots, const int32_t* tokens_in, const float* seen,
+                     const float* noise, int top_k, float top_p, float temperature, float rp, int eos_mask,
+                     int32_t* sampled_out, int32_t* greedy_out, float* logits_out) {
+    Session* S = (Session*)sess;
+    std::vector<float> logits;
+    if (decode_forward(S, n, slots, tokens_in, logits)) return -1;
+    if (logits_out) memcpy(logits_out, logits.data(), sizeof(float) * logits.size());
+    return orc_sample(S->m, n, logits.data(), seen, noise, top_k, top_p, temperature, rp, eos_mask, sampled_out, greedy_out);
 }
 
 int orc_read_kv(void* sess, int slot, int layer, int which, uint16_t* out) {

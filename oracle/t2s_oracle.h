@@ -63,7 +63,17 @@ int      orc_prefill(void* sess, int slot, const float* x, int nq, int T_prompt,
 int      orc_decode_step(void* sess, int n, const int32_t* slots, const int32_t* tokens_in,
                          const float* seen, float rep_penalty, int eos_mask,
                          int32_t* tokens_out, float* logits_out);
+// Decode step with the full sampler (noise f32 [n][vocab] by sorted position, or null).
+int      orc_decode_step2(void* sess, int n, const int32_t* slots, const int32_t* tokens_in,
+                          const float* seen, const float* noise, int top_k, float top_p,
+                          float temperature, float rp, int eos_mask, int32_t* sampled_out,
+                          int32_t* greedy_out, float* logits_out);
 int      orc_slot_n_pos(void* sess, int slot);
+// Sampler chain (block.cpp:52-348) on n rows of logits f32 [n][vocab]; seen f32 [n][vocab] or
+// null; noise f32 [n][vocab] Exp(1) samples indexed by sorted position, or null (greedy).
+int      orc_sample(void* model, int n, const float* logits, const float* seen, const float* noise,
+                    int top_k, float top_p, float temperature, float rp, int eos_mask,
+                    int32_t* sampled, int32_t* greedy);
 // Read back the slot's cached K or V (f16) of one layer: [n_pos][d].
 int      orc_read_kv(void* sess, int slot, int layer, int which, uint16_t* out);
 

@@ -171,3 +171,74 @@ def test_slot_reuse_and_errors(t2sx_mod):
     with pytest.raises(T.T2SXError) as e:
         T.Model("/nonexistent/path.gguf")
     assert e.value.code == T.ERR_IO
+
+
+SAMPLER_CONFIGS = [
+    dict(top_k=15, top_p=1.0, temperature=1.0, repetition_penalty=1.35),   # reference defaults
+    dict(top_k=0, top_p=0.95, temperature=1.0, repetition_penalty=1.0),
+    dict(top_k=1, top_p=1.0, temperature=1.0, repetition_penalty=1.0),
+    dict(top_k=1025, top_p=0.5, temperature=0.7, repetition_penalty=1.35),
+    dict(top_k=5, top_p=0.8, temperature=0.0, repetition_penalty=1.0),
+]
+
+
+@pytest.mark.parametrize("cfg", SAMPLER_CONFIGS, ids=lambda c: "k{top_k}-p{top_p}-t{temperature}-rp{repetition_penalty}".format(**c))
+def test_stochastic_sampler_stream_bit_exact(t2sx_mod, orc, cfg):
+    """Full sampler chain (block.cpp:52-348) with caller-supplied Exp(1) noise: sampled and greedy
+    tokens equal the oracle's at every step, with the sampled token fed back."""
+    _need_gpu()
+    import synth
+    path = synth.ensure_gguf("q8_0", 7, n_layer=2)
+    m_gpu, m_orc = t2sx_mod.Model(path), orc.Model(path)
+    lengths = [(30, 20, 31), (12, 40, 32), (50, 5, 33)]
+    n, steps, V = len(lengths), 24, m_orc.vocab
+    cap = max(tt + tp for tt, tp, _ in lengths) + steps + 2
+    s_gpu = t2sx_mod.Session(m_gpu, n, cap, eos_mask=True, **cfg)
+    s_orc = orc.Session(m_orc, n, cap)
+    xs, nq, tps, cur = [], [], [], []
+    for i, (tt, tp, seed) in enumerate(lengths):
+        ph, bert, sem = synth.session_inputs(seed, tt, tp)
+        x = m_orc.embed_prefill(ph, bert, sem)
+        xs.append(x); nq.append(tt + tp); tps.append(tp)
+        cur.append(s_orc.prefill(i, x, tp, eos_mask=True)[0])
+    first = s_gpu.prefill(np.arange(n), nq, tps, np.concatenate(xs))
+    assert list(first) == cur
+    cur = np.array(cur, dtype=np.int32)
+    seen = np.zeros((n, V), dtype=np.float32)
+    seen[np.arange(n), cur] = 1.0
+    rng = np.random.default_rng(42)
+    for step in range(steps):
+        noise = rng.exponential(size=(n, V)).astype(np.float32)
+        s_gpu.set_exp_noise(noise)
+        got = s_gpu.decode_step_host(cur)
+        got_greedy = s_gpu.read_greedy(n)
+        ref, ref_greedy = s_orc.decode_sampled(np.arange(n), cur, noise,
+                                               seen=seen if cfg["repetition_penalty"] != 1.0 else None,
+                                               top_k=cfg["top_k"], top_p=cfg["top_p"], temperature=cfg["temperature"],
+                                               rep_penalty=cfg["repetition_penalty"], eos_mask=True)
+        assert np.array_equal(got_greedy, ref_greedy), (step, got_greedy, ref_greedy)
+        assert np.array_equal(got, ref), (step, got, ref)
+        seen[np.arange(n), ref] = 1.0
+        cur = ref
+    s_gpu.set_exp_noise(None)
+
+
+def test_model_freed_before_session(t2sx_mod):
+    """Freeing the model first (e.g. Python's cyclic GC finalising in any order) defers the release
+    until its last session is freed; the session keeps working and no CUDA error is left pending."""
+    _need_gpu()
+    import synth
+    T = t2sx_mod
+    path = synth.ensure_gguf("q8_0", 7, n_layer=2)
+    m = T.Model(path)
+    s = T.Session(m, 1, 64, repetition_penalty=1.0, eos_mask=True)
+    x = np.random.default_rng(1).standard_normal((12, 512), dtype=np.float32)
+    s.prefill([0], [12], [6], x)
+    m.close()
+    toks = s.decode(4)
+    assert toks.shape == (4, 1)
+    s.close()
+    m2 = T.Model(path)
+    s2 = T.Session(m2, 1, 64, repetition_penalty=1.0, eos_mask=True)
+    s2.prefill([0], [12], [6], x)
+    assert np.array_equal(s2.decode(4), toks)
