@@ -184,12 +184,15 @@ def run_ours(args):
     barrier()
     torch.cuda.synchronize()
     dev_ms = 0.0
+    step_ms = []
     torch.cuda.cudart().cudaProfilerStart()   # profilers started with --profile-from-start off see only this loop
     with ClockSampler(local) as clk:
         t0 = time.perf_counter()
         for _ in range(K):
             cur = sess.decode_step_host(cur, want_tokens=True)
-            dev_ms += sess.last_decode_ms()
+            ms = sess.last_decode_ms()
+            step_ms.append(ms)
+            dev_ms += ms
         wall_s = time.perf_counter() - t0
     torch.cuda.cudart().cudaProfilerStop()
     barrier()
@@ -223,6 +226,7 @@ def run_ours(args):
             "steps": K,
             "warmup": W,
             "ms_per_step": round(t_max * 1e3 / K, 4),
+            "p50_step_ms": round(float(np.median(step_ms)), 4),
             "higher_is_better": True,
             "scaling": "strong",
             "vs_baseline": None,

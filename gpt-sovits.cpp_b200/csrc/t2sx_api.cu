@@ -538,6 +538,7 @@ struct t2sx_session {
     int ring_len = 256;
     int graph_kernels = 0;         // kernel nodes in the captured step graph
     int32_t* scratch_i = nullptr;  // [n_slots]
+    int32_t* tail_ctr = nullptr;   // ticket of the last-CTA matmul tails (self-resetting)
     int last_rows = 0;             // rows of the last logits
     const float* last_logits = nullptr;
     const int32_t* last_greedy = nullptr;
@@ -568,27 +569,67 @@ static ActQ act_of(Work& w) {
 
 static const float kAttnScale = 1.0f / sqrtf((float)kHeadDim);
 
-// The 24 post-norm layers over T rows (block.cpp:513-637), x in w.x, result in w.x.
-static void run_layers(t2sx_session* s, Work& w, int T, bool decode) {
+static ActQ act_for(Work& w, const float* f32_input) {
+    ActQ a = act_of(w);
+    a.f = f32_input;   // read directly by F32-weight matmuls
+    return a;
+}
+
+// The post-norm layers over T rows (block.cpp:513-637).  On entry w.x holds the input rows (f32)
+// and the activation buffer holds them in layer 0's QKV dot type; on exit w.x holds the output
+// rows and, when final_qtype >= 0, the activation buffer holds them in that dot type.  For one or
+// two rows the residual + LayerNorm runs in the last CTA of the preceding matmul; otherwise it is
+// its own kernel.
+static void run_layers(t2sx_session* s, Work& w, int T, bool decode, int final_qtype) {
     const t2sx_model* m = s->m;
     Rows rows = rows_of(s, w);
     KVView kv = kv_of(s);
-    ActQ a = act_of(w);
-    for (int l = 0; l < s->n_layer; ++l) {
+    // last-CTA LayerNorm tails pay off only for one or two rows (the tail runs on one CTA)
+    const bool small = T <= 2;
+    const int nl = s->n_layer;
+    for (int l = 0; l < nl; ++l) {
         const LayerD& L = m->layers[l];
-        quantize_act(L.qkv.type, w.x, T, kD, a, s->st);
-        matmul(L.qkv, a, T, L.qkv_b, 0, w.qkv, s->st);
-        qkv_post(T, w.qkv, rows, kv, l, w.q16, s->st);
-        if (decode) attention_decode(T, w.q16, rows, kv, l, kAttnScale, w.attn, s->st);
-        else attention_prefill(T, w.q16, rows, kv, l, kAttnScale, w.attn, s->st);
-        quantize_act(L.out.type, w.attn, T, kD, a, s->st);
-        matmul(L.out, a, T, L.out_b, 0, w.o, s->st);
-        residual_layernorm(T, w.x, w.o, L.ln1_w, L.ln1_b, 1e-5f, w.ln1, s->st);
-        quantize_act(L.up.type, w.ln1, T, kD, a, s->st);
-        matmul(L.up, a, T, L.up_b, 1, w.h, s->st);
-        quantize_act(L.down.type, w.h, T, s->ff, a, s->st);
-        matmul(L.down, a, T, L.down_b, 0, w.f, s->st);
-        residual_layernorm(T, w.ln1, w.f, L.ln2_w, L.ln2_b, 1e-5f, w.x, s->st);
+        const int next_q = (l + 1 < nl) ? m->layers[l + 1].qkv.type : final_qtype;
+        QKVStore qs;
+        qs.rows = rows;
+        qs.kv = kv;
+        qs.layer = l;
+        qs.q16 = w.q16;
+        Epi e_qkv;
+        e_qkv.qkv = &qs;
+        matmul(L.qkv, act_for(w, w.x), T, L.qkv_b, 0, nullptr, s->st, e_qkv);
+        if (decode) {
+            attention_decode(T, w.q16, rows, kv, l, kAttnScale, w.attn, L.out.type, act_of(w), s->st);
+        } else {
+            attention_prefill(T, w.q16, rows, kv, l, kAttnScale, w.attn, s->st);
+            ActQ a = act_of(w);
+            quantize_act(L.out.type, w.attn, T, kD, a, s->st);
+        }
+        if (small) {
+            Tail t1;
+            t1.kind = 1; t1.resid = w.x; t1.g = L.ln1_w; t1.beta = L.ln1_b; t1.eps = 1e-5f; t1.y_out = w.ln1;
+            t1.qtype = L.up.type; t1.qo = act_of(w); t1.counter = s->tail_ctr;
+            Epi e1;
+            e1.tail = &t1;
+            matmul(L.out, act_for(w, w.attn), T, L.out_b, 0, w.o, s->st, e1);
+            matmul(L.up, act_for(w, w.ln1), T, L.up_b, 1, w.h, s->st);
+            ActQ ah = act_of(w);
+            quantize_act(L.down.type, w.h, T, s->ff, ah, s->st);
+            Tail t3;
+            t3.kind = 1; t3.resid = w.ln1; t3.g = L.ln2_w; t3.beta = L.ln2_b; t3.eps = 1e-5f; t3.y_out = w.x;
+            t3.qtype = next_q; t3.qo = act_of(w); t3.counter = s->tail_ctr;
+            Epi e3;
+            e3.tail = &t3;
+            matmul(L.down, act_for(w, w.h), T, L.down_b, 0, w.f, s->st, e3);
+        } else {
+            matmul(L.out, act_for(w, w.attn), T, L.out_b, 0, w.o, s->st);
+            residual_layernorm(T, w.x, w.o, L.ln1_w, L.ln1_b, 1e-5f, w.ln1, L.up.type, act_of(w), s->st);
+            matmul(L.up, act_for(w, w.ln1), T, L.up_b, 1, w.h, s->st);
+            ActQ a = act_of(w);
+            quantize_act(L.down.type, w.h, T, s->ff, a, s->st);
+            matmul(L.down, act_for(w, w.h), T, L.down_b, 0, w.f, s->st);
+            residual_layernorm(T, w.ln1, w.f, L.ln2_w, L.ln2_b, 1e-5f, w.x, next_q, act_of(w), s->st);
+        }
     }
 }
 
@@ -599,7 +640,7 @@ static void free_session(t2sx_session* s) {
     if (s->graph) cudaGraphExecDestroy(s->graph);
     for (void* p : {(void*)s->pool, (void*)s->ptab, (void*)s->n_pos, (void*)s->audio_off, (void*)s->token_in, (void*)s->cap,
                     (void*)s->err, (void*)s->seen, (void*)s->pe, (void*)s->dec.mem, (void*)s->pre.mem, (void*)s->ring,
-                    (void*)s->ring_step, (void*)s->scratch_i, (void*)s->noise})
+                    (void*)s->ring_step, (void*)s->scratch_i, (void*)s->noise, (void*)s->tail_ctr})
         if (p) cudaFree(p);
     if (s->ev0) cudaEventDestroy(s->ev0);
     if (s->ev1) cudaEventDestroy(s->ev1);
@@ -655,6 +696,7 @@ extern "C" int t2sx_session_create(const t2sx_model* m, uint32_t n_slots, uint32
     ck(cudaMalloc(&s->token_in, n_slots * 4), "state"); ck(cudaMalloc(&s->cap, n_slots * 4), "state");
     ck(cudaMalloc(&s->err, 4), "state"); ck(cudaMalloc(&s->scratch_i, n_slots * 4), "state");
     ck(cudaMalloc(&s->ring_step, 4), "state");
+    ck(cudaMalloc(&s->tail_ctr, 4), "state");
     if (s->cfg.repetition_penalty != 1.0f) ck(cudaMalloc(&s->seen, (size_t)n_slots * s->V), "seen mask");
     ck(cudaMalloc(&s->pe, (size_t)slot_size * kD * 4), "PE table");
     if (rc) { free_session(s); return rc; }
@@ -666,6 +708,7 @@ extern "C" int t2sx_session_create(const t2sx_model* m, uint32_t n_slots, uint32
     ck(cudaMemset(s->n_pos, 0, n_slots * 4), "memset"); ck(cudaMemset(s->audio_off, 0, n_slots * 4), "memset");
     ck(cudaMemset(s->token_in, 0, n_slots * 4), "memset"); ck(cudaMemset(s->cap, 0, n_slots * 4), "memset");
     ck(cudaMemset(s->err, 0, 4), "memset");
+    ck(cudaMemset(s->tail_ctr, 0, 4), "memset");
     if (s->seen) ck(cudaMemset(s->seen, 0, (size_t)n_slots * s->V), "memset");
     if (rc) { free_session(s); return rc; }
     s->free_pages.resize(npages);
@@ -746,7 +789,7 @@ extern "C" int t2sx_embed_prefill(t2sx_session* s, const int32_t* phones, const 
     if (T_prompt) CK(cudaMemcpyAsync(d_sem, sem, T_prompt * 4, cudaMemcpyHostToDevice, s->st));
     if (T_text) {
         CK(cudaMemcpyAsync(w.h, bert, (size_t)T_text * 1024 * 4, cudaMemcpyHostToDevice, s->st));
-        ActQ a = act_of(w);
+        ActQ a = act_for(w, w.h);
         quantize_act(m->bert.type, w.h, T_text, 1024, a, s->st);
         matmul(m->bert, a, T_text, m->bert_b, 0, w.o, s->st);
     }
@@ -830,10 +873,14 @@ extern "C" int t2sx_prefill(t2sx_session* s, int32_t n, const int32_t* slots, co
         CK(cudaMemcpyAsync(w.row_L, rl.data(), T * 4, cudaMemcpyHostToDevice, s->st));
         CK(cudaMemcpyAsync(w.lastrow, last.data(), ns * 4, cudaMemcpyHostToDevice, s->st));
         CK(cudaMemcpyAsync(w.x, x + xoff * kD, (size_t)T * kD * 4, x_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, s->st));
-        run_layers(s, w, T, false);
+        {
+            ActQ a0 = act_of(w);
+            quantize_act(m->layers[0].qkv.type, w.x, T, kD, a0, s->st);
+        }
+        run_layers(s, w, T, false, -1);
         // sampler on each slot's last row
         gather_rows(ns, w.x, w.lastrow, kD, w.xl, s->st);
-        ActQ a = act_of(w);
+        ActQ a = act_for(w, w.xl);
         quantize_act(m->lm_head.type, w.xl, ns, kD, a, s->st);
         matmul(m->lm_head, a, ns, nullptr, 0, w.logits, s->st);
         for (int i = i0; i < i1; ++i) rs[i - i0] = slots[i];
@@ -896,11 +943,9 @@ static void enqueue_step(t2sx_session* s) {
     const int T = (int)s->active.size();
     Rows rows = rows_of(s, w);
     embed_decode(T, w.row_slot, s->token_in, s->n_pos, s->audio_off, m->audio16, m->audio32, m->audio_rows, s->pe, s->slot_size,
-                 m->alpha_audio, rows, w.x, s->st);
-    run_layers(s, w, T, true);
-    ActQ a = act_of(w);
-    quantize_act(m->lm_head.type, w.x, T, kD, a, s->st);
-    matmul(m->lm_head, a, T, nullptr, 0, w.logits, s->st);
+                 m->alpha_audio, rows, w.x, m->layers[0].qkv.type, act_of(w), s->st);
+    run_layers(s, w, T, true, m->lm_head.type);
+    matmul(m->lm_head, act_for(w, w.x), T, nullptr, 0, w.logits, s->st);
     run_sampler(s, T, w.logits, w.row_slot, s->seen, w.tok, w.greedy);
     advance(T, w.row_slot, w.tok, s->token_in, s->n_pos, s->seen, s->V, s->ring, s->ring_len, s->ring_step, s->st);
 }
@@ -1115,7 +1160,7 @@ extern "C" int t2sx_profile_step(t2sx_session* s, int32_t iters, float* ms) {
         return T2SX_OK;
     };
     int rc;
-    if ((rc = timeit(0, [&] { attention_decode(T, w.q16, rows, kv, 0, kAttnScale, w.attn, s->st); }))) return rc;
+    if ((rc = timeit(0, [&] { attention_decode(T, w.q16, rows, kv, 0, kAttnScale, w.attn, L.out.type, a, s->st); }))) return rc;
     quantize_act(L.qkv.type, w.x, T, kD, a, s->st);
     if ((rc = timeit(1, [&] { matmul(L.qkv, a, T, L.qkv_b, 0, w.qkv, s->st); }))) return rc;
     if ((rc = timeit(2, [&] { matmul(L.out, a, T, L.out_b, 0, w.o, s->st); }))) return rc;
@@ -1123,7 +1168,7 @@ extern "C" int t2sx_profile_step(t2sx_session* s, int32_t iters, float* ms) {
     if ((rc = timeit(5, [&] { matmul(m->lm_head, a, T, nullptr, 0, w.logits, s->st); }))) return rc;
     quantize_act(L.down.type, w.h, T, s->ff, a, s->st);
     if ((rc = timeit(4, [&] { matmul(L.down, a, T, L.down_b, 0, w.f, s->st); }))) return rc;
-    if ((rc = timeit(6, [&] { residual_layernorm(T, w.ln1, w.f, L.ln2_w, L.ln2_b, 1e-5f, w.o, s->st); }))) return rc;
+    if ((rc = timeit(6, [&] { residual_layernorm(T, w.ln1, w.f, L.ln2_w, L.ln2_b, 1e-5f, w.o, -1, a, s->st); }))) return rc;
     if ((rc = timeit(7, [&] { quantize_act(L.down.type, w.h, T, s->ff, a, s->st); }))) return rc;
     CK(cudaGetLastError());
     return T2SX_OK;

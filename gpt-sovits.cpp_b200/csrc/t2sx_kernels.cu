@@ -17,67 +17,75 @@ __global__ void k_quant_q8_0(const float* __restrict__ x, int64_t nblk, int8_t* 
                              float* __restrict__ d) {
     const int lane = threadIdx.x & 31;
     const int64_t wstride = ((int64_t)gridDim.x * blockDim.x) >> 5;
-    for (int64_t b = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; b < nblk; b += wstride) {
-        const float v = x[b * 32 + lane];
-        float a = fabsf(v);
-#pragma unroll
-        for (int off = 16; off >= 1; off >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, off));
-        const float dd = __fdiv_rn(a, 127.0f);
-        const float id = (a != 0.0f) ? __fdiv_rn(127.0f, a) : 0.0f;
-        float r = rintf(__fmul_rn(v, id));
-        r = fminf(fmaxf(r, -128.0f), 127.0f);
-        q[b * 32 + lane] = (int8_t)(int)r;
-        if (lane == 0) d[b] = __half2float(__float2half_rn(dd));
-    }
+    for (int64_t b = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; b < nblk; b += wstride)
+        q[b * 32 + lane] = (int8_t)q8_0_lane(x[b * 32 + lane], d + b, lane);
 }
 
-// Q8_K (ggml quantize_row_q8_K_ref rule): one warp per 256-element block, 8 elements per lane.
+// Q8_K of one 256-element block by one warp, 8 consecutive elements per lane: q, d and the sums
+// of the eight 32-element groups.  `ldcg` reads through L2 (data written by other CTAs).
+__device__ __forceinline__ void quant_block_q8_K(const float* __restrict__ xb, int lane, bool ldcg,
+                                                 int8_t* __restrict__ qb, float* __restrict__ d_slot,
+                                                 int32_t* __restrict__ bs8) {
+    const float4* p = reinterpret_cast<const float4*>(xb + lane * 8);
+    const float4 x0 = ldcg ? __ldcg(p) : p[0];
+    const float4 x1 = ldcg ? __ldcg(p + 1) : p[1];
+    const float v[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+    AbsMax am{0.0f, 0.0f, 0x7fffffff};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) absmax_take(am, v[i], lane * 8 + i);
+    am = absmax_warp(am);
+    const float iscale = q8k_iscale(am);
+    int qv[8];
+    int sum = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) { qv[i] = q8k_q(iscale, v[i]); sum += qv[i]; }
+    if (lane == 0) *d_slot = q8k_d(iscale);
+    int2 packed;
+    packed.x = (qv[0] & 0xff) | ((qv[1] & 0xff) << 8) | ((qv[2] & 0xff) << 16) | ((qv[3] & 0xff) << 24);
+    packed.y = (qv[4] & 0xff) | ((qv[5] & 0xff) << 8) | ((qv[6] & 0xff) << 16) | ((qv[7] & 0xff) << 24);
+    *reinterpret_cast<int2*>(qb + lane * 8) = packed;
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+    if ((lane & 3) == 0) bs8[lane >> 2] = sum;
+}
+
+// Q8_K (ggml quantize_row_q8_K_ref rule): one warp per 256-element block.
 __global__ void k_quant_q8_K(const float* __restrict__ x, int64_t nblk, int8_t* __restrict__ q,
                              float* __restrict__ d, int32_t* __restrict__ bs) {
     const int lane = threadIdx.x & 31;
     const int64_t wstride = ((int64_t)gridDim.x * blockDim.x) >> 5;
-    for (int64_t b = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; b < nblk; b += wstride) {
-        const float4* xp = reinterpret_cast<const float4*>(x + b * 256 + lane * 8);
-        const float4 x0 = xp[0], x1 = xp[1];
-        const float v[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-        float amax = 0.0f, mx = 0.0f;
-        int idx = 0x7fffffff;
+    for (int64_t b = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; b < nblk; b += wstride)
+        quant_block_q8_K(x + b * 256, lane, false, q + b * 256, d + b, bs + b * 8);
+}
+
+// A 512-wide row held by one warp, lane l holding elements l + 32 t (t < 16), converted to the
+// dot type of a weight format with the same rules as the k_quant_* kernels.  wtype < 0 or F32:
+// nothing to write (an F32 matmul reads the f32 row itself).
+__device__ void quant_row512_strided(const float (&y)[kD / 32], int lane, int wtype, const ActQ& o, size_t row) {
+    if (wtype == W_Q8_0 || wtype == W_Q4_0) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const float a = fabsf(v[i]);
-            if (a > amax) { amax = a; mx = v[i]; idx = lane * 8 + i; }
-        }
+        for (int t = 0; t < kD / 32; ++t)
+            o.q[row * kD + 32 * t + lane] = (int8_t)q8_0_lane(y[t], o.d + row * (kD / 32) + t, lane);
+    } else if (wtype == W_Q4_K) {
 #pragma unroll
-        for (int off = 16; off >= 1; off >>= 1) {
-            const float oa = __shfl_xor_sync(0xffffffffu, amax, off);
-            const float om = __shfl_xor_sync(0xffffffffu, mx, off);
-            const int oi = __shfl_xor_sync(0xffffffffu, idx, off);
-            if (oa > amax || (oa == amax && oi < idx)) { amax = oa; mx = om; idx = oi; }
-        }
-        int8_t qv[8];
-        int sum = 0;
-        if (amax == 0.0f) {
+        for (int B = 0; B < kD / 256; ++B) {
+            AbsMax am{0.0f, 0.0f, 0x7fffffff};
 #pragma unroll
-            for (int i = 0; i < 8; ++i) qv[i] = 0;
-        } else {
-            const float iscale = __fdiv_rn(-127.0f, mx);
+            for (int k = 0; k < 8; ++k) absmax_take(am, y[8 * B + k], lane + 32 * k);
+            am = absmax_warp(am);
+            const float iscale = q8k_iscale(am);
+            if (lane == 0) o.d[row * (kD / 256) + B] = q8k_d(iscale);
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const float r = rintf(__fmul_rn(iscale, v[i]));
-                const int iv = r > 127.0f ? 127 : (int)r;
-                qv[i] = (int8_t)iv;
-                sum += iv;
+            for (int k = 0; k < 8; ++k) {
+                const int qv = q8k_q(iscale, y[8 * B + k]);
+                o.q[row * kD + 256 * B + 32 * k + lane] = (int8_t)qv;
+                const int sum = warp_sum_i(qv);
+                if (lane == 0) o.bs[row * (kD / 32) + 8 * B + k] = sum;
             }
-            if (lane == 0) d[b] = __fdiv_rn(1.0f, iscale);
         }
-        if (amax == 0.0f && lane == 0) d[b] = 0.0f;
-        int2 packed;
-        packed.x = (qv[0] & 0xff) | ((qv[1] & 0xff) << 8) | ((qv[2] & 0xff) << 16) | ((qv[3] & 0xff) << 24);
-        packed.y = (qv[4] & 0xff) | ((qv[5] & 0xff) << 8) | ((qv[6] & 0xff) << 16) | ((qv[7] & 0xff) << 24);
-        *reinterpret_cast<int2*>(q + b * 256 + lane * 8) = packed;
-        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-        if ((lane & 3) == 0) bs[b * 8 + (lane >> 2)] = sum;
+    } else if (wtype == W_F16) {
+#pragma unroll
+        for (int t = 0; t < kD / 32; ++t) o.h[row * kD + 32 * t + lane] = f2h(y[t]);
     }
 }
 
@@ -132,16 +140,107 @@ __device__ __forceinline__ float epi(float acc, const float* bias, int n, int re
 
 constexpr int kSmallM = 32;
 
+__device__ __forceinline__ size_t kv_off(const KVView& kv, int page, int layer, int which, int head, int pos_in_page) {
+    return (((((size_t)page * kv.n_layer + layer) * 2 + which) * kHeads + head) * kPage + pos_in_page) * kHeadDim;
+}
+
+// QKV projection output element (row m, column n) -> Q as f16 for attention, K / V as f16 into
+// the row's cache page (ggml_set_rows into an F16 cache, block.cpp:557-573).
+__device__ __forceinline__ void qkv_store(const QKVStore& e, int m, int n, float v) {
+    const uint16_t h = f2h(v);
+    if (n < kD) { e.q16[(size_t)m * kD + n] = h; return; }
+    const int pos = e.rows.pos[m];
+    const int s = e.rows.slot[m];
+    if (pos < 0 || pos >= e.rows.cap[s]) return;
+    const int page = e.kv.ptab[(size_t)s * e.kv.max_pages + pos / kPage];
+    const int which = (n - kD) / kD, j = (n - kD) % kD;
+    e.kv.pool[kv_off(e.kv, page, e.layer, which, j / kHeadDim, pos % kPage) + (j % kHeadDim)] = h;
+}
+
+// y = LN(a + b) * g + beta for one row held by one warp (ggml_norm + mul + add,
+// block.cpp:615-619 / :630-634): lane l sums elements l, l+32, ... in double, the lanes combine
+// by an xor butterfly.  `b_l2` reads b through L2 (written by other CTAs of the same kernel).
+__device__ void ln_row_warp(const float* __restrict__ a, const float* __restrict__ b, bool b_l2,
+                            const float* __restrict__ g, const float* __restrict__ beta, float eps, int lane,
+                            float (&out)[kD / 32]) {
+    float v[kD / 32];
+    double s = 0.0;
+#pragma unroll
+    for (int t = 0; t < kD / 32; ++t) {
+        const int i = lane + 32 * t;
+        v[t] = __fadd_rn(a[i], b_l2 ? __ldcg(b + i) : b[i]);
+        s = __dadd_rn(s, (double)v[t]);
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) s = __dadd_rn(s, __shfl_xor_sync(0xffffffffu, s, off));
+    const float mean = __double2float_rn(__ddiv_rn(s, (double)kD));
+    double s2 = 0.0;
+#pragma unroll
+    for (int t = 0; t < kD / 32; ++t) {
+        v[t] = __fsub_rn(v[t], mean);
+        s2 = __dadd_rn(s2, (double)__fmul_rn(v[t], v[t]));
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) s2 = __dadd_rn(s2, __shfl_xor_sync(0xffffffffu, s2, off));
+    const float var = __double2float_rn(__ddiv_rn(s2, (double)kD));
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+#pragma unroll
+    for (int t = 0; t < kD / 32; ++t) {
+        const int i = lane + 32 * t;
+        out[t] = __fadd_rn(__fmul_rn(__fmul_rn(v[t], scale), g[i]), beta[i]);
+    }
+}
+
+// Work of the last CTA of a small-M matmul, once every CTA's output is written: residual +
+// LayerNorm of the M rows (kind 1) or quantisation of the M output rows (kind 2), into the
+// next matmul's dot type.
+__device__ void run_tail(const Tail& tl, const float* __restrict__ y, int M, int N) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    if (tl.kind == 1) {
+        for (int m = warp; m < M; m += nw) {
+            float out[kD / 32];
+            ln_row_warp(tl.resid + (size_t)m * kD, y + (size_t)m * kD, true, tl.g, tl.beta, tl.eps, lane, out);
+#pragma unroll
+            for (int t = 0; t < kD / 32; ++t) tl.y_out[(size_t)m * kD + lane + 32 * t] = out[t];
+            quant_row512_strided(out, lane, tl.qtype, tl.qo, (size_t)m);
+        }
+    } else if (tl.kind == 2) {
+        if (tl.qtype == W_Q8_0 || tl.qtype == W_Q4_0) {
+            const int nb = M * (N / 32);
+            for (int b = warp; b < nb; b += nw)
+                tl.qo.q[(size_t)b * 32 + lane] = (int8_t)q8_0_lane(__ldcg(y + (size_t)b * 32 + lane), tl.qo.d + b, lane);
+        } else if (tl.qtype == W_Q4_K) {
+            const int nb = M * (N / 256);
+            for (int b = warp; b < nb; b += nw)
+                quant_block_q8_K(y + (size_t)b * 256, lane, true, tl.qo.q + (size_t)b * 256, tl.qo.d + b,
+                                 tl.qo.bs + (size_t)b * 8);
+        } else if (tl.qtype == W_F16) {
+            for (int i = threadIdx.x; i < M * N; i += blockDim.x) tl.qo.h[i] = f2h(__ldcg(y + i));
+        }
+    }
+}
+
+// Last-CTA election (threadfence + ticket): no CTA waits for another.  The last CTA runs the
+// tail and resets the ticket for the next launch.
+__device__ __forceinline__ void tail_if_last(const Tail& tl, const float* y, int M, int N) {
+    __shared__ int s_last;
+    __threadfence();   // this thread's outputs are visible device-wide before the ticket
+    __syncthreads();
+    if (threadIdx.x == 0) s_last = (atomicAdd(tl.counter, 1) == (int)gridDim.x - 1);
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    run_tail(tl, y, M, N);
+    if (threadIdx.x == 0) *tl.counter = 0;
+}
+
 // Small-M kernel: one warp per weight row; lanes compute block partials (phase A) into shared
-// memory, then lane m runs the ordered chain of row m (phase B).
+// memory, then lane m runs the ordered chain of row m (phase B).  Optional epilogues: QKV store
+// (Q and the K/V cache append) and a last-CTA tail.
 template <int WT>
-__global__ void __launch_bounds__(128) k_mm_small(DevW W, ActQ A, int M, const float* __restrict__ bias, int relu,
-                                                  float* __restrict__ y) {
-    __shared__ int s_a[4][kSmallM][64];
-    __shared__ int s_m[4][kSmallM][8];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n = blockIdx.x * 4 + warp;
-    if (n >= W.N) return;
+__device__ __forceinline__ void mm_small_row(const DevW& W, const ActQ& A, int M, const float* __restrict__ bias, int relu,
+                                             float* __restrict__ y, const QKVStore* qkv, int (&s_a)[kSmallM][64],
+                                             int (&s_m)[kSmallM][8], int n, int lane) {
     const int K = W.K;
     if (WT == W_Q8_0 || WT == W_Q4_0) {
         const int nb = K / 32;
@@ -157,7 +256,7 @@ __global__ void __launch_bounds__(128) k_mm_small(DevW W, ActQ A, int M, const f
             }
             for (int m = 0; m < M; ++m) {
                 const int4* xp = reinterpret_cast<const int4*>(A.q + (size_t)m * K + b * 32);
-                s_a[warp][m][b] = dp8(w0, w1, xp[0], xp[1]);
+                s_a[m][b] = dp8(w0, w1, xp[0], xp[1]);
             }
         }
         __syncwarp();
@@ -166,9 +265,9 @@ __global__ void __launch_bounds__(128) k_mm_small(DevW W, ActQ A, int M, const f
             float acc = 0.0f;
             for (int b = 0; b < nb; ++b) {
                 const float dd = __fmul_rn(W.d[(size_t)n * nb + b], A.d[(size_t)m * nb + b]);
-                acc = __fmaf_rn(dd, (float)s_a[warp][m][b], acc);
+                acc = __fmaf_rn(dd, (float)s_a[m][b], acc);
             }
-            y[(size_t)m * W.N + n] = epi(acc, bias, n, relu);
+            { const float v_ = epi(acc, bias, n, relu); if (qkv) qkv_store(*qkv, m, n, v_); else y[(size_t)m * W.N + n] = v_; }
         }
     } else if (WT == W_Q4_K) {
         const int nsub = K / 32, nsb = K / 256;
@@ -205,7 +304,7 @@ __global__ void __launch_bounds__(128) k_mm_small(DevW W, ActQ A, int M, const f
                 sm += __shfl_xor_sync(0xffffffffu, sm, 1);
                 sm += __shfl_xor_sync(0xffffffffu, sm, 2);
                 sm += __shfl_xor_sync(0xffffffffu, sm, 4);
-                if (act && js == 0) { s_a[warp][m][sb] = sa; s_m[warp][m][sb] = sm; }
+                if (act && js == 0) { s_a[m][sb] = sa; s_m[m][sb] = sm; }
             }
         }
         __syncwarp();
@@ -216,10 +315,10 @@ __global__ void __launch_bounds__(128) k_mm_small(DevW W, ActQ A, int M, const f
                 const float dx = A.d[(size_t)m * nsb + sb];
                 const float dd = __fmul_rn(dx, W.d[(size_t)n * nsb + sb]);
                 const float dm = __fmul_rn(-dx, W.dmin[(size_t)n * nsb + sb]);
-                acc_a = __fmaf_rn(dd, (float)s_a[warp][m][sb], acc_a);
-                acc_m = __fmaf_rn(dm, (float)s_m[warp][m][sb], acc_m);
+                acc_a = __fmaf_rn(dd, (float)s_a[m][sb], acc_a);
+                acc_m = __fmaf_rn(dm, (float)s_m[m][sb], acc_m);
             }
-            y[(size_t)m * W.N + n] = epi(__fadd_rn(acc_a, acc_m), bias, n, relu);
+            { const float v_ = epi(__fadd_rn(acc_a, acc_m), bias, n, relu); if (qkv) qkv_store(*qkv, m, n, v_); else y[(size_t)m * W.N + n] = v_; }
         }
     } else {  // F16 / F32
         const int nb = K / 32;
@@ -239,176 +338,40 @@ __global__ void __launch_bounds__(128) k_mm_small(DevW W, ActQ A, int M, const f
                     const float xv = (WT == W_F16) ? h2f(A.h[(size_t)m * K + b * 32 + i]) : A.f[(size_t)m * K + b * 32 + i];
                     s = __fmaf_rn(w[i], xv, s);
                 }
-                s_a[warp][m][b] = __float_as_int(s);
+                s_a[m][b] = __float_as_int(s);
             }
         }
         __syncwarp();
         if (lane < M) {
             const int m = lane;
             float acc = 0.0f;
-            for (int b = 0; b < nb; ++b) acc = __fadd_rn(acc, __int_as_float(s_a[warp][m][b]));
-            y[(size_t)m * W.N + n] = epi(acc, bias, n, relu);
+            for (int b = 0; b < nb; ++b) acc = __fadd_rn(acc, __int_as_float(s_a[m][b]));
+            { const float v_ = epi(acc, bias, n, relu); if (qkv) qkv_store(*qkv, m, n, v_); else y[(size_t)m * W.N + n] = v_; }
         }
     }
 }
 
-// Tiled kernel for larger M: 64 weight rows x 64 activation rows per CTA, 256 threads, each a
-// 4x4 register tile; K staged 4 blocks (128 elements) at a time.  Same canonical order.
+
 template <int WT>
-__global__ void __launch_bounds__(256) k_mm_tiled(DevW W, ActQ A, int M, const float* __restrict__ bias, int relu,
-                                                  float* __restrict__ y) {
-    constexpr int KB = 4;
-    __shared__ int4 sW4[KB * 8][16];   // [k-word][n/4]
-    __shared__ int4 sX4[KB * 8][16];   // [k-word][m/4]
-    __shared__ float sDw[KB][64], sDx[KB][64];
-    __shared__ float sDw2[64], sDm2[64], sDx2[64];
-    __shared__ int sSc[KB][64], sMn[KB][64], sBs[KB][64];
-    int* sW = reinterpret_cast<int*>(sW4);
-    int* sX = reinterpret_cast<int*>(sX4);
-    const int tid = threadIdx.x, tn = tid & 15, tm = tid >> 4;
-    const int n0 = blockIdx.x * 64, m0 = blockIdx.y * 64;
-    const int K = W.K, N = W.N;
-    float acc[4][4], acc_m[4][4];
-    int sa[4][4], smi[4][4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) { acc[i][j] = 0.0f; acc_m[i][j] = 0.0f; sa[i][j] = 0; smi[i][j] = 0; }
-    const int nstage = K / (32 * KB);
-    for (int stg = 0; stg < nstage; ++stg) {
-        const int kb0 = stg * KB;  // first 32-block of the stage
-        // ---- stage weights ----
-        for (int idx = tid; idx < 64 * KB; idx += 256) {
-            const int row = idx & 63, blk = idx >> 6, n = n0 + row, b = kb0 + blk;
-            int4 w0 = make_int4(0, 0, 0, 0), w1 = w0;
-            if (n < N) {
-                if (WT == W_Q8_0) {
-                    const int4* wp = reinterpret_cast<const int4*>(W.q8 + (size_t)n * K + b * 32);
-                    w0 = wp[0]; w1 = wp[1];
-                } else if (WT == W_Q4_0) {
-                    const int4 raw = *reinterpret_cast<const int4*>(W.q4 + ((size_t)n * (K / 32) + b) * 16);
-                    w0 = make_int4(q4lo(raw.x), q4lo(raw.y), q4lo(raw.z), q4lo(raw.w));
-                    w1 = make_int4(q4hi(raw.x), q4hi(raw.y), q4hi(raw.z), q4hi(raw.w));
-                } else {  // Q4_K: sub-block b of the row
-                    const int sb = b >> 3, js = b & 7, c = js >> 1, hi = js & 1;
-                    const int4* wp = reinterpret_cast<const int4*>(W.q4 + ((size_t)n * (K / 256) + sb) * 128 + 32 * c);
-                    const int4 r0 = wp[0], r1 = wp[1];
-                    const int sh = hi ? 4 : 0;
-                    w0 = make_int4((r0.x >> sh) & 0x0F0F0F0F, (r0.y >> sh) & 0x0F0F0F0F, (r0.z >> sh) & 0x0F0F0F0F, (r0.w >> sh) & 0x0F0F0F0F);
-                    w1 = make_int4((r1.x >> sh) & 0x0F0F0F0F, (r1.y >> sh) & 0x0F0F0F0F, (r1.z >> sh) & 0x0F0F0F0F, (r1.w >> sh) & 0x0F0F0F0F);
-                }
-            }
-            sW[(blk * 8 + 0) * 64 + row] = w0.x; sW[(blk * 8 + 1) * 64 + row] = w0.y;
-            sW[(blk * 8 + 2) * 64 + row] = w0.z; sW[(blk * 8 + 3) * 64 + row] = w0.w;
-            sW[(blk * 8 + 4) * 64 + row] = w1.x; sW[(blk * 8 + 5) * 64 + row] = w1.y;
-            sW[(blk * 8 + 6) * 64 + row] = w1.z; sW[(blk * 8 + 7) * 64 + row] = w1.w;
-            if (WT == W_Q4_K) {
-                const int sb = b >> 3, js = b & 7;
-                sSc[blk][row] = n < N ? W.scm[((size_t)n * (K / 256) + sb) * 16 + js] : 0;
-                sMn[blk][row] = n < N ? W.scm[((size_t)n * (K / 256) + sb) * 16 + 8 + js] : 0;
-            } else {
-                sDw[blk][row] = n < N ? W.d[(size_t)n * (K / 32) + b] : 0.0f;
-            }
-        }
-        // ---- stage activations ----
-        for (int idx = tid; idx < 64 * KB; idx += 256) {
-            const int row = idx & 63, blk = idx >> 6, m = m0 + row, b = kb0 + blk;
-            int4 x0 = make_int4(0, 0, 0, 0), x1 = x0;
-            if (m < M) {
-                const int4* xp = reinterpret_cast<const int4*>(A.q + (size_t)m * K + b * 32);
-                x0 = xp[0]; x1 = xp[1];
-            }
-            sX[(blk * 8 + 0) * 64 + row] = x0.x; sX[(blk * 8 + 1) * 64 + row] = x0.y;
-            sX[(blk * 8 + 2) * 64 + row] = x0.z; sX[(blk * 8 + 3) * 64 + row] = x0.w;
-            sX[(blk * 8 + 4) * 64 + row] = x1.x; sX[(blk * 8 + 5) * 64 + row] = x1.y;
-            sX[(blk * 8 + 6) * 64 + row] = x1.z; sX[(blk * 8 + 7) * 64 + row] = x1.w;
-            if (WT == W_Q4_K) sBs[blk][row] = m < M ? A.bs[(size_t)m * (K / 32) + b] : 0;
-            else sDx[blk][row] = m < M ? A.d[(size_t)m * (K / 32) + b] : 0.0f;
-        }
-        if (WT == W_Q4_K && (kb0 & 7) == 0 && tid < 64) {
-            const int n = n0 + tid, m = m0 + tid, sb = kb0 >> 3;
-            sDw2[tid] = n < N ? W.d[(size_t)n * (K / 256) + sb] : 0.0f;
-            sDm2[tid] = n < N ? W.dmin[(size_t)n * (K / 256) + sb] : 0.0f;
-            sDx2[tid] = m < M ? A.d[(size_t)m * (K / 256) + sb] : 0.0f;
-        }
-        __syncthreads();
-        // ---- compute ----
-#pragma unroll
-        for (int blk = 0; blk < KB; ++blk) {
-            int is[4][4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-#pragma unroll
-                for (int j = 0; j < 4; ++j) is[i][j] = 0;
-#pragma unroll
-            for (int w = 0; w < 8; ++w) {
-                const int4 a = sW4[blk * 8 + w][tn];
-                const int4 b = sX4[blk * 8 + w][tm];
-                const int av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
-#pragma unroll
-                for (int i = 0; i < 4; ++i)
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) is[i][j] = __dp4a(av[i], bv[j], is[i][j]);
-            }
-            if (WT == W_Q4_K) {
-#pragma unroll
-                for (int i = 0; i < 4; ++i)
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        sa[i][j] += sSc[blk][4 * tn + i] * is[i][j];
-                        smi[i][j] += sMn[blk][4 * tn + i] * sBs[blk][4 * tm + j];
-                    }
-            } else {
-#pragma unroll
-                for (int i = 0; i < 4; ++i)
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const float dd = __fmul_rn(sDw[blk][4 * tn + i], sDx[blk][4 * tm + j]);
-                        acc[i][j] = __fmaf_rn(dd, (float)is[i][j], acc[i][j]);
-                    }
-            }
-        }
-        if (WT == W_Q4_K && ((kb0 + KB) & 7) == 0) {
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const float dx = sDx2[4 * tm + j];
-                    const float dd = __fmul_rn(dx, sDw2[4 * tn + i]);
-                    const float dm = __fmul_rn(-dx, sDm2[4 * tn + i]);
-                    acc[i][j] = __fmaf_rn(dd, (float)sa[i][j], acc[i][j]);
-                    acc_m[i][j] = __fmaf_rn(dm, (float)smi[i][j], acc_m[i][j]);
-                    sa[i][j] = 0; smi[i][j] = 0;
-                }
-        }
-        __syncthreads();
-    }
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const int n = n0 + 4 * tn + i;
-        if (n >= N) continue;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const int m = m0 + 4 * tm + j;
-            if (m >= M) continue;
-            const float r = (WT == W_Q4_K) ? __fadd_rn(acc[i][j], acc_m[i][j]) : acc[i][j];
-            y[(size_t)m * N + n] = epi(r, bias, n, relu);
-        }
-    }
+__global__ void __launch_bounds__(128) k_mm_small(DevW W, ActQ A, int M, const float* __restrict__ bias, int relu,
+                                                  float* __restrict__ y, QKVStore qkv, int use_qkv, Tail tail,
+                                                  int use_tail) {
+    __shared__ int s_a[4][kSmallM][64];
+    __shared__ int s_m[4][kSmallM][8];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n = blockIdx.x * 4 + warp;
+    if (n < W.N) mm_small_row<WT>(W, A, M, bias, relu, y, use_qkv ? &qkv : nullptr, s_a[warp], s_m[warp], n, lane);
+    if (use_tail) tail_if_last(tail, y, M, W.N);
 }
 
-void matmul(const DevW& W, const ActQ& a, int M, const float* bias, int relu, float* y, cudaStream_t st) {
+void matmul(const DevW& W, const ActQ& a, int M, const float* bias, int relu, float* y, cudaStream_t st, const Epi& e) {
     const bool quant = W.type == W_Q8_0 || W.type == W_Q4_0 || W.type == W_Q4_K;
-    if (quant && M > kSmallM && matmul_mma(W, a, M, bias, relu, y, st)) return;
-    if (quant && M > kSmallM) {
-        dim3 grid((W.N + 63) / 64, (M + 63) / 64);
-        switch (W.type) {
-            case W_Q8_0: k_mm_tiled<W_Q8_0><<<grid, 256, 0, st>>>(W, a, M, bias, relu, y); break;
-            case W_Q4_0: k_mm_tiled<W_Q4_0><<<grid, 256, 0, st>>>(W, a, M, bias, relu, y); break;
-            case W_Q4_K: k_mm_tiled<W_Q4_K><<<grid, 256, 0, st>>>(W, a, M, bias, relu, y); break;
-        }
-        return;
-    }
+    if (quant && M > kSmallM && matmul_mma(W, a, M, bias, relu, y, e.qkv, st)) return;
+    QKVStore qkv{};
+    if (e.qkv) qkv = *e.qkv;
+    Tail tail{};
+    const bool use_tail = e.tail && M <= kSmallM;
+    if (use_tail) tail = *e.tail;
     for (int m0 = 0; m0 < M; m0 += kSmallM) {
         const int mm = (M - m0) < kSmallM ? (M - m0) : kSmallM;
         ActQ as = a;
@@ -418,14 +381,22 @@ void matmul(const DevW& W, const ActQ& a, int M, const float* bias, int relu, fl
         if (as.f) as.f += (size_t)m0 * K;
         if (as.d) as.d += (size_t)m0 * (W.type == W_Q4_K ? K / 256 : K / 32);
         if (as.bs) as.bs += (size_t)m0 * (K / 32);
-        float* yy = y + (size_t)m0 * W.N;
+        float* yy = y ? y + (size_t)m0 * W.N : nullptr;
+        QKVStore qq = qkv;
+        if (e.qkv) {
+            qq.rows.slot += m0;
+            qq.rows.pos += m0;
+            qq.rows.L += m0;
+            qq.q16 += (size_t)m0 * kD;
+        }
         const int grid = (W.N + 3) / 4;
+        const int uq = e.qkv ? 1 : 0, ut = use_tail ? 1 : 0;
         switch (W.type) {
-            case W_Q8_0: k_mm_small<W_Q8_0><<<grid, 128, 0, st>>>(W, as, mm, bias, relu, yy); break;
-            case W_Q4_0: k_mm_small<W_Q4_0><<<grid, 128, 0, st>>>(W, as, mm, bias, relu, yy); break;
-            case W_Q4_K: k_mm_small<W_Q4_K><<<grid, 128, 0, st>>>(W, as, mm, bias, relu, yy); break;
-            case W_F16: k_mm_small<W_F16><<<grid, 128, 0, st>>>(W, as, mm, bias, relu, yy); break;
-            default: k_mm_small<W_F32><<<grid, 128, 0, st>>>(W, as, mm, bias, relu, yy); break;
+            case W_Q8_0: k_mm_small<W_Q8_0><<<grid, 128, 0, st>>>(W, as, mm, bias, relu, yy, qq, uq, tail, ut); break;
+            case W_Q4_0: k_mm_small<W_Q4_0><<<grid, 128, 0, st>>>(W, as, mm, bias, relu, yy, qq, uq, tail, ut); break;
+            case W_Q4_K: k_mm_small<W_Q4_K><<<grid, 128, 0, st>>>(W, as, mm, bias, relu, yy, qq, uq, tail, ut); break;
+            case W_F16: k_mm_small<W_F16><<<grid, 128, 0, st>>>(W, as, mm, bias, relu, yy, qq, uq, tail, ut); break;
+            default: k_mm_small<W_F32><<<grid, 128, 0, st>>>(W, as, mm, bias, relu, yy, qq, uq, tail, ut); break;
         }
     }
 }
@@ -434,65 +405,59 @@ void matmul(const DevW& W, const ActQ& a, int M, const float* bias, int relu, fl
 // embedding, KV append, attention, LayerNorm, sampler
 // ============================================================================================
 
-// Decode embedding (session.cpp:337-344): x = emb[tok] + pe[n_pos - audio_offset] * alpha.
-// Also fixes the row's KV position (n_pos) and attended length (n_pos + 1).
-__global__ void k_embed_decode(const int32_t* __restrict__ row_slot, const int32_t* __restrict__ token_in,
+// Decode embedding (session.cpp:337-344): x = emb[tok] + pe[n_pos - audio_offset] * alpha, one
+// warp per row; writes x (f32, the first residual) and x in the first matmul's dot type.  Also
+// fixes the row's KV position (n_pos) and attended length (n_pos + 1).
+__global__ void k_embed_decode(int T, const int32_t* __restrict__ row_slot, const int32_t* __restrict__ token_in,
                                const int32_t* __restrict__ n_pos, const int32_t* __restrict__ audio_off,
-                               const uint16_t* __restrict__ emb16, const float* __restrict__ emb32,
-                               int emb_rows, const float* __restrict__ pe, int pe_rows, float alpha, Rows rows,
-                               float* __restrict__ x) {
-    const int r = blockIdx.x;
+                               const uint16_t* __restrict__ emb16, const float* __restrict__ emb32, int emb_rows,
+                               const float* __restrict__ pe, int pe_rows, float alpha, Rows rows, float* __restrict__ x,
+                               int qtype, ActQ qo) {
+    const int lane = threadIdx.x & 31;
+    const int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    if (r >= T) return;
     const int s = row_slot[r];
     const int pos = n_pos[s];
     const int pp = pos - audio_off[s];
     const int tok = token_in[s];
     const bool ok = pos >= 0 && pos < rows.cap[s] && pp >= 0 && pp < pe_rows && tok >= 0 && tok < emb_rows;
-    if (threadIdx.x == 0) {
+    if (lane == 0) {
         rows.pos[r] = ok ? pos : -1;
         rows.L[r] = ok ? pos + 1 : 0;
         if (!ok) atomicExch(rows.err, 1);
     }
-    for (int d = threadIdx.x; d < kD; d += blockDim.x) {
-        float v = 0.0f;
+    float v[kD / 32];
+#pragma unroll
+    for (int t = 0; t < kD / 32; ++t) {
+        const int d = lane + 32 * t;
+        v[t] = 0.0f;
         if (ok) {
             const float e = emb16 ? h2f(emb16[(size_t)tok * kD + d]) : emb32[(size_t)tok * kD + d];
-            v = __fadd_rn(e, __fmul_rn(pe[(size_t)pp * kD + d], alpha));
+            v[t] = __fadd_rn(e, __fmul_rn(pe[(size_t)pp * kD + d], alpha));
         }
-        x[(size_t)r * kD + d] = v;
+        x[(size_t)r * kD + d] = v[t];
     }
+    quant_row512_strided(v, lane, qtype, qo, (size_t)r);
 }
 
 void embed_decode(int T, const int32_t* row_slot, const int32_t* token_in, const int32_t* n_pos,
                   const int32_t* audio_off, const uint16_t* emb16, const float* emb32, int emb_rows, const float* pe,
-                  int pe_rows, float alpha, Rows rows, float* x, cudaStream_t st) {
+                  int pe_rows, float alpha, Rows rows, float* x, int qtype, ActQ qo, cudaStream_t st) {
     if (T > 0)
-        k_embed_decode<<<T, 128, 0, st>>>(row_slot, token_in, n_pos, audio_off, emb16, emb32, emb_rows, pe, pe_rows, alpha,
-                                          rows, x);
+        k_embed_decode<<<(T + 3) / 4, 128, 0, st>>>(T, row_slot, token_in, n_pos, audio_off, emb16, emb32, emb_rows, pe,
+                                                    pe_rows, alpha, rows, x, qtype, qo);
 }
 
-__device__ __forceinline__ size_t kv_off(const KVView& kv, int page, int layer, int which, int head, int pos_in_page) {
-    return (((((size_t)page * kv.n_layer + layer) * 2 + which) * kHeads + head) * kPage + pos_in_page) * kHeadDim;
-}
-
-// Split the QKV projection: Q -> f16 for attention, K and V -> f16 into the paged cache
-// (ggml_set_rows into an F16 cache, block.cpp:557-573).
-__global__ void k_qkv_post(const float* __restrict__ qkv, Rows rows, KVView kv, int layer, uint16_t* __restrict__ q16) {
-    const int r = blockIdx.x;
-    const int s = rows.slot[r];
-    const int pos = rows.pos[r];
-    const bool ok = pos >= 0 && pos < rows.cap[s];
-    const int page = ok ? kv.ptab[(size_t)s * kv.max_pages + (pos / kPage)] : -1;
-    for (int i = threadIdx.x; i < 3 * kD; i += blockDim.x) {
-        const uint16_t h = f2h(qkv[(size_t)r * 3 * kD + i]);
-        if (i < kD) { q16[(size_t)r * kD + i] = h; continue; }
-        if (page < 0) continue;
-        const int which = (i - kD) / kD, j = (i - kD) % kD;
-        kv.pool[kv_off(kv, page, layer, which, j / kHeadDim, pos % kPage) + (j % kHeadDim)] = h;
+__device__ __forceinline__ void unpack_row32(const uint4 (&u4)[4], float* out) {
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        const uint32_t w[4] = {u4[c].x, u4[c].y, u4[c].z, u4[c].w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            out[c * 8 + 2 * e] = h2f((uint16_t)(w[e] & 0xffffu));
+            out[c * 8 + 2 * e + 1] = h2f((uint16_t)(w[e] >> 16));
+        }
     }
-}
-
-void qkv_post(int T, const float* qkv, Rows rows, KVView kv, int layer, uint16_t* q16, cudaStream_t st) {
-    if (T > 0) k_qkv_post<<<T, 256, 0, st>>>(qkv, rows, kv, layer, q16);
 }
 
 __device__ __forceinline__ void load_row32(const uint16_t* p, float* out) {
@@ -509,14 +474,20 @@ __device__ __forceinline__ void load_row32(const uint16_t* p, float* out) {
     }
 }
 
-// Decode attention: one warp per (row, head), four heads of a row per CTA.  Position lane
+// Decode attention: one warp per (row, head), eight heads of a row per CTA.  Position lane
 // t = lane folds positions t, t+32, ... with the online update; the 32 lanes merge in the
 // order of an xor butterfly (partners 16, 8, 4, 2, 1).  The merge is symmetric, so every lane
-// ends with the same state and lane d writes output dim d.
-__global__ void __launch_bounds__(128) k_attn_decode(const uint16_t* __restrict__ q16, Rows rows, KVView kv, int layer,
-                                                     float scale, float* __restrict__ out) {
+// ends with the same state and lane d owns output dim d.  The output row is written in the
+// out-projection's dot type (a Q8_0 block is one head, a Q8_K block the CTA's eight heads), or
+// as f32 when qtype < 0.
+template <int HPC, bool PIPE>
+__global__ void __launch_bounds__(32 * HPC) k_attn_decode(const uint16_t* __restrict__ q16, Rows rows, KVView kv, int layer,
+                                                          float scale, float* __restrict__ out, int qtype, ActQ qo) {
+    __shared__ AbsMax s_am[8];
+    __shared__ float s_is;
     const int r = blockIdx.x;
-    const int h = blockIdx.y * 4 + (threadIdx.x >> 5);
+    const int warp = threadIdx.x >> 5;
+    const int h = blockIdx.y * HPC + warp;
     const int lane = threadIdx.x & 31;
     const int s = rows.slot[r];
     const int L = rows.L[r];
@@ -525,15 +496,45 @@ __global__ void __launch_bounds__(128) k_attn_decode(const uint16_t* __restrict_
     AttnState st;
     st_empty(st);
     const int32_t* pt = kv.ptab + (size_t)s * kv.max_pages;
-    for (int i = lane; i < L; i += kAttnLanes) {
+    if (!PIPE) {
+        for (int i = lane; i < L; i += kAttnLanes) {
+            const int page = pt[i / kPage];
+            float k[kHeadDim], v[kHeadDim];
+            load_row32(kv.pool + kv_off(kv, page, layer, 0, h, i % kPage), k);
+            load_row32(kv.pool + kv_off(kv, page, layer, 1, h, i % kPage), v);
+            st_update(st, __fmul_rn(dot32(q, k), scale), v);
+        }
+    }
+    // PIPE (small batches, latency-bound): the K/V rows of the lane's next position are in
+    // flight while the current one is folded (fold order unchanged; costs registers)
+    uint4 kr[4], vr[4];
+    int i = PIPE ? lane : L;
+    if (i < L) {
         const int page = pt[i / kPage];
-        const size_t kb = kv_off(kv, page, layer, 0, h, i % kPage);
-        const size_t vb = kv_off(kv, page, layer, 1, h, i % kPage);
+        const uint4* kp = reinterpret_cast<const uint4*>(kv.pool + kv_off(kv, page, layer, 0, h, i % kPage));
+        const uint4* vp = reinterpret_cast<const uint4*>(kv.pool + kv_off(kv, page, layer, 1, h, i % kPage));
+#pragma unroll
+        for (int c = 0; c < 4; ++c) { kr[c] = kp[c]; vr[c] = vp[c]; }
+    }
+    int next_page = (i + kAttnLanes < L) ? pt[(i + kAttnLanes) / kPage] : 0;
+    while (i < L) {
+        const int in = i + kAttnLanes;
+        uint4 kn[4], vn[4];
+        if (in < L) {
+            const uint4* kp = reinterpret_cast<const uint4*>(kv.pool + kv_off(kv, next_page, layer, 0, h, in % kPage));
+            const uint4* vp = reinterpret_cast<const uint4*>(kv.pool + kv_off(kv, next_page, layer, 1, h, in % kPage));
+#pragma unroll
+            for (int c = 0; c < 4; ++c) { kn[c] = kp[c]; vn[c] = vp[c]; }
+            next_page = (in + kAttnLanes < L) ? pt[(in + kAttnLanes) / kPage] : 0;
+        }
         float k[kHeadDim], v[kHeadDim];
-        load_row32(kv.pool + kb, k);
-        load_row32(kv.pool + vb, v);
+        unpack_row32(kr, k);
+        unpack_row32(vr, v);
         const float sc = __fmul_rn(dot32(q, k), scale);
         st_update(st, sc, v);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) { kr[c] = kn[c]; vr[c] = vn[c]; }
+        i = in;
     }
 #pragma unroll
     for (int off = 16; off >= 1; off >>= 1) {
@@ -553,12 +554,48 @@ __global__ void __launch_bounds__(128) k_attn_decode(const uint16_t* __restrict_
     float mine = 0.0f;
 #pragma unroll
     for (int d = 0; d < kHeadDim; ++d) if (d == lane) mine = st.o[d];
-    out[(size_t)r * kD + h * kHeadDim + lane] = __fmul_rn(mine, __fdiv_rn(1.0f, st.l));
+    const float val = __fmul_rn(mine, __fdiv_rn(1.0f, st.l));
+    const size_t e = (size_t)r * kD + h * kHeadDim + lane;
+    if (qtype == W_Q8_0 || qtype == W_Q4_0) {
+        qo.q[e] = (int8_t)q8_0_lane(val, qo.d + (size_t)r * (kD / 32) + h, lane);
+    } else if (qtype == W_Q4_K && HPC == 8) {
+        AbsMax am{0.0f, 0.0f, 0x7fffffff};
+        absmax_take(am, val, warp * kHeadDim + lane);
+        am = absmax_warp(am);
+        if (lane == 0) s_am[warp] = am;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            AbsMax all = s_am[0];
+            for (int w = 1; w < 8; ++w) absmax_merge(all, s_am[w]);
+            const float iscale = q8k_iscale(all);
+            s_is = iscale;
+            qo.d[(size_t)r * (kD / 256) + blockIdx.y] = q8k_d(iscale);
+        }
+        __syncthreads();
+        const int qv = q8k_q(s_is, val);
+        qo.q[e] = (int8_t)qv;
+        const int sum = warp_sum_i(qv);
+        if (lane == 0) qo.bs[(size_t)r * (kD / 32) + h] = sum;
+    } else if (qtype == W_F16) {
+        qo.h[e] = f2h(val);
+    } else {
+        out[e] = val;
+    }
 }
 
-void attention_decode(int T, const uint16_t* q16, Rows rows, KVView kv, int layer, float scale, float* out,
-                      cudaStream_t st) {
-    if (T > 0) k_attn_decode<<<dim3(T, kHeads / 4), 128, 0, st>>>(q16, rows, kv, layer, scale, out);
+void attention_decode(int T, const uint16_t* q16, Rows rows, KVView kv, int layer, float scale, float* out, int qtype,
+                      ActQ qo, cudaStream_t st) {
+    if (T <= 0) return;
+    // a Q8_K output block spans eight heads, so that format needs eight heads per CTA; otherwise
+    // small batches spread the heads over more CTAs
+    if (qtype == W_Q4_K) {
+        if (T < 64) k_attn_decode<8, true><<<dim3(T, kHeads / 8), 256, 0, st>>>(q16, rows, kv, layer, scale, out, qtype, qo);
+        else k_attn_decode<8, false><<<dim3(T, kHeads / 8), 256, 0, st>>>(q16, rows, kv, layer, scale, out, qtype, qo);
+    } else if (T < 64) {
+        k_attn_decode<2, true><<<dim3(T, kHeads / 2), 64, 0, st>>>(q16, rows, kv, layer, scale, out, qtype, qo);
+    } else {
+        k_attn_decode<4, false><<<dim3(T, kHeads / 4), 128, 0, st>>>(q16, rows, kv, layer, scale, out, qtype, qo);
+    }
 }
 
 // Prefill attention: one thread per (row, head) folds its prefix sequentially.
@@ -591,44 +628,24 @@ void attention_prefill(int T, const uint16_t* q16, Rows rows, KVView kv, int lay
     if (T > 0) k_attn_prefill<<<(T * kHeads + 127) / 128, 128, 0, st>>>(T, q16, rows, kv, layer, scale, out);
 }
 
-// y = LN(a + b) * g + beta (ggml_norm + mul + add, block.cpp:615-619 / :630-634).  One warp per
-// row; lane l sums elements l, l+32, ... in double, lanes combine by an xor butterfly.
+// y = LN(a + b) * g + beta, one warp per row (ln_row_warp); the row is also written in the next
+// matmul's dot type when qtype >= 0.
 __global__ void k_residual_ln(int T, const float* __restrict__ a, const float* __restrict__ b,
-                              const float* __restrict__ g, const float* __restrict__ beta, float eps, float* __restrict__ y) {
+                              const float* __restrict__ g, const float* __restrict__ beta, float eps,
+                              float* __restrict__ y, int qtype, ActQ qo) {
     const int lane = threadIdx.x & 31;
     const int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     if (r >= T) return;
-    float v[kD / 32];
-    double s = 0.0;
+    float out[kD / 32];
+    ln_row_warp(a + (size_t)r * kD, b + (size_t)r * kD, false, g, beta, eps, lane, out);
 #pragma unroll
-    for (int t = 0; t < kD / 32; ++t) {
-        const int i = lane + 32 * t;
-        v[t] = __fadd_rn(a[(size_t)r * kD + i], b[(size_t)r * kD + i]);
-        s = __dadd_rn(s, (double)v[t]);
-    }
-#pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) s = __dadd_rn(s, __shfl_xor_sync(0xffffffffu, s, off));
-    const float mean = __double2float_rn(__ddiv_rn(s, (double)kD));
-    double s2 = 0.0;
-#pragma unroll
-    for (int t = 0; t < kD / 32; ++t) {
-        v[t] = __fsub_rn(v[t], mean);
-        s2 = __dadd_rn(s2, (double)__fmul_rn(v[t], v[t]));
-    }
-#pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) s2 = __dadd_rn(s2, __shfl_xor_sync(0xffffffffu, s2, off));
-    const float var = __double2float_rn(__ddiv_rn(s2, (double)kD));
-    const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
-#pragma unroll
-    for (int t = 0; t < kD / 32; ++t) {
-        const int i = lane + 32 * t;
-        y[(size_t)r * kD + i] = __fadd_rn(__fmul_rn(__fmul_rn(v[t], scale), g[i]), beta[i]);
-    }
+    for (int t = 0; t < kD / 32; ++t) y[(size_t)r * kD + lane + 32 * t] = out[t];
+    quant_row512_strided(out, lane, qtype, qo, (size_t)r);
 }
 
 void residual_layernorm(int T, const float* a, const float* b, const float* g, const float* beta, float eps, float* y,
-                        cudaStream_t st) {
-    if (T > 0) k_residual_ln<<<(T + 3) / 4, 128, 0, st>>>(T, a, b, g, beta, eps, y);
+                        int qtype, ActQ qo, cudaStream_t st) {
+    if (T > 0) k_residual_ln<<<(T + 3) / 4, 128, 0, st>>>(T, a, b, g, beta, eps, y, qtype, qo);
 }
 
 // Greedy token over penalised logits (block.cpp:117-138 repetition penalty as masked lerps,

@@ -55,20 +55,49 @@ struct Rows {
     int32_t* err = nullptr;         // device error flag (bounds)
 };
 
+// Output of the QKV projection routed by rows: Q as f16 [T][512], K and V as f16 into the pages.
+struct QKVStore {
+    Rows rows;
+    KVView kv;
+    int layer = 0;
+    uint16_t* q16 = nullptr;
+};
+
+// Work done by the last CTA of a small-M (<= 32 rows) matmul after all its outputs are written:
+// kind 1: y_out = LN(resid + y) * g + beta, plus y_out in dot type qtype into qo;
+// kind 2: y (M x N) in dot type qtype into qo.
+struct Tail {
+    int kind = 0;
+    const float* resid = nullptr;
+    const float* g = nullptr;
+    const float* beta = nullptr;
+    float eps = 1e-5f;
+    float* y_out = nullptr;
+    int qtype = -1;
+    ActQ qo;
+    int32_t* counter = nullptr;   // zero-initialised; reset by the tail
+};
+
+struct Epi {
+    const QKVStore* qkv = nullptr;
+    const Tail* tail = nullptr;
+};
+
 void quantize_act(int wtype, const float* x, int M, int K, ActQ& a, cudaStream_t st);
-void matmul(const DevW& W, const ActQ& a, int M, const float* bias, int relu, float* y, cudaStream_t st);
+void matmul(const DevW& W, const ActQ& a, int M, const float* bias, int relu, float* y, cudaStream_t st,
+            const Epi& epi = Epi());
 // Tensor-core path (mma.sync s8) for M > 32; false if the shape is not supported.
-bool matmul_mma(const DevW& W, const ActQ& a, int M, const float* bias, int relu, float* y, cudaStream_t st);
+bool matmul_mma(const DevW& W, const ActQ& a, int M, const float* bias, int relu, float* y, const QKVStore* qkv,
+                cudaStream_t st);
 void embed_decode(int T, const int32_t* row_slot, const int32_t* token_in, const int32_t* n_pos,
                   const int32_t* audio_off, const uint16_t* emb16, const float* emb32, int emb_rows,
-                  const float* pe, int pe_rows, float alpha, Rows rows, float* x, cudaStream_t st);
-void qkv_post(int T, const float* qkv, Rows rows, KVView kv, int layer, uint16_t* q16, cudaStream_t st);
-void attention_decode(int T, const uint16_t* q16, Rows rows, KVView kv, int layer, float scale, float* out,
-                      cudaStream_t st);
+                  const float* pe, int pe_rows, float alpha, Rows rows, float* x, int qtype, ActQ qo, cudaStream_t st);
+void attention_decode(int T, const uint16_t* q16, Rows rows, KVView kv, int layer, float scale, float* out, int qtype,
+                      ActQ qo, cudaStream_t st);
 void attention_prefill(int T, const uint16_t* q16, Rows rows, KVView kv, int layer, float scale, float* out,
                        cudaStream_t st);
 void residual_layernorm(int T, const float* a, const float* b, const float* g, const float* beta, float eps,
-                        float* y, cudaStream_t st);
+                        float* y, int qtype, ActQ qo, cudaStream_t st);
 // Logit given to EOS when EOS is masked (finite, so the masked-lerp filters stay finite).
 constexpr float kEosMasked = -1.0e30f;
 void sample_greedy(int T, const float* logits, int V, const int32_t* row_slot, const uint8_t* seen, float rp,

@@ -94,3 +94,65 @@ __device__ __forceinline__ float dot32(const float* q, const float* k) {
 }
 
 }  // namespace t2sx
+
+namespace t2sx {
+
+// ---- warp-level quantisation of activations (the rules of the k_quant_* kernels) ----------
+
+__device__ __forceinline__ float warp_max_f(float v) {
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
+    return v;
+}
+__device__ __forceinline__ int warp_sum_i(int v) {
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+    return v;
+}
+
+// Q8_0 of one 32-element block held one value per lane (x86 AVX2 rule of ggml's
+// quantize_row_q8_0): amax, d = amax/127 stored as f16, id = 127/amax, q = rint(v*id).
+// Lane 0 writes the scale (as the f32 value of the f16) to *d_slot.
+__device__ __forceinline__ int q8_0_lane(float v, float* d_slot, int lane) {
+    const float a = warp_max_f(fabsf(v));
+    const float dd = __fdiv_rn(a, 127.0f);
+    const float id = (a != 0.0f) ? __fdiv_rn(127.0f, a) : 0.0f;
+    float r = rintf(__fmul_rn(v, id));
+    r = fminf(fmaxf(r, -128.0f), 127.0f);
+    if (lane == 0) *d_slot = __half2float(__float2half_rn(dd));
+    return (int)r;
+}
+
+// Running (|x| max, signed value, first index) of a Q8_K block (ggml quantize_row_q8_K_ref).
+struct AbsMax {
+    float a, m;
+    int i;
+};
+__device__ __forceinline__ void absmax_take(AbsMax& s, float v, int idx) {
+    const float a = fabsf(v);
+    if (a > s.a || (a == s.a && a > 0.0f && idx < s.i)) { s.a = a; s.m = v; s.i = idx; }
+}
+__device__ __forceinline__ void absmax_merge(AbsMax& s, const AbsMax& o) {
+    if (o.a > s.a || (o.a == s.a && o.i < s.i)) s = o;
+}
+__device__ __forceinline__ AbsMax absmax_warp(AbsMax s) {
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) {
+        AbsMax o;
+        o.a = __shfl_xor_sync(0xffffffffu, s.a, off);
+        o.m = __shfl_xor_sync(0xffffffffu, s.m, off);
+        o.i = __shfl_xor_sync(0xffffffffu, s.i, off);
+        absmax_merge(s, o);
+    }
+    return s;
+}
+// iscale = -127/max of the block (0 for an all-zero block); d = 1/iscale (0 for all-zero).
+__device__ __forceinline__ float q8k_iscale(const AbsMax& s) { return s.a == 0.0f ? 0.0f : __fdiv_rn(-127.0f, s.m); }
+__device__ __forceinline__ float q8k_d(float iscale) { return iscale == 0.0f ? 0.0f : __fdiv_rn(1.0f, iscale); }
+__device__ __forceinline__ int q8k_q(float iscale, float v) {
+    if (iscale == 0.0f) return 0;
+    const float r = rintf(__fmul_rn(iscale, v));
+    return r > 127.0f ? 127 : (int)r;
+}
+
+}  // namespace t2sx

@@ -60,9 +60,25 @@ struct Cfg {
     static constexpr int SMEM = 2 * STAGE;
 };
 
+__device__ __forceinline__ size_t kv_off_m(const KVView& kv, int page, int layer, int which, int head, int pos_in_page) {
+    return (((((size_t)page * kv.n_layer + layer) * 2 + which) * kHeads + head) * kPage + pos_in_page) * kHeadDim;
+}
+
+// QKV projection output element -> Q as f16, K / V as f16 into the row's cache page.
+__device__ __forceinline__ void qkv_store_m(const QKVStore& e, int m, int n, float v) {
+    const uint16_t h = f2h(v);
+    if (n < kD) { e.q16[(size_t)m * kD + n] = h; return; }
+    const int pos = e.rows.pos[m];
+    const int s = e.rows.slot[m];
+    if (pos < 0 || pos >= e.rows.cap[s]) return;
+    const int page = e.kv.ptab[(size_t)s * e.kv.max_pages + pos / kPage];
+    const int which = (n - kD) / kD, j = (n - kD) % kD;
+    e.kv.pool[kv_off_m(e.kv, page, e.layer, which, j / kHeadDim, pos % kPage) + (j % kHeadDim)] = h;
+}
+
 template <int WT, int MT_>
 __global__ void __launch_bounds__(256) k_mm_mma(DevW W, ActQ A, int M, const float* __restrict__ bias, int relu,
-                                                float* __restrict__ y) {
+                                                float* __restrict__ y, QKVStore qkv, int use_qkv) {
     using C = Cfg<WT, MT_>;
     constexpr int MT = C::MT, BM = C::BM, WROW = C::WROW;
     extern __shared__ __align__(16) uint8_t smem[];
@@ -281,13 +297,15 @@ __global__ void __launch_bounds__(256) k_mm_mma(DevW W, ActQ A, int M, const flo
                     float v = (WT == W_Q4_K) ? __fadd_rn(acc[i][j][e], accm[i][j][e]) : acc[i][j][e];
                     if (bias) v = __fadd_rn(v, bias[n]);
                     if (relu) v = (v > 0.0f) ? v : 0.0f;
-                    y[(size_t)m * N + n] = v;
+                    if (use_qkv) qkv_store_m(qkv, m, n, v);
+                    else y[(size_t)m * N + n] = v;
                 }
             }
 }
 
 template <int WT, int MT>
-static void launch_mma(const DevW& W, const ActQ& a, int M, const float* bias, int relu, float* y, cudaStream_t st) {
+static void launch_mma(const DevW& W, const ActQ& a, int M, const float* bias, int relu, float* y, const QKVStore* qkv,
+                       cudaStream_t st) {
     using C = Cfg<WT, MT>;
     static bool configured = false;   // the attribute is per function; set once per process
     if (!configured) {
@@ -296,17 +314,20 @@ static void launch_mma(const DevW& W, const ActQ& a, int M, const float* bias, i
         configured = true;
     }
     dim3 grid((W.N + BN - 1) / BN, (M + C::BM - 1) / C::BM);
-    k_mm_mma<WT, MT><<<grid, 256, C::SMEM, st>>>(W, a, M, bias, relu, y);
+    QKVStore q{};
+    if (qkv) q = *qkv;
+    k_mm_mma<WT, MT><<<grid, 256, C::SMEM, st>>>(W, a, M, bias, relu, y, q, qkv ? 1 : 0);
 }
 
-bool matmul_mma(const DevW& W, const ActQ& a, int M, const float* bias, int relu, float* y, cudaStream_t st) {
+bool matmul_mma(const DevW& W, const ActQ& a, int M, const float* bias, int relu, float* y, const QKVStore* qkv,
+                cudaStream_t st) {
     if (W.K % (32 * KB)) return false;
     // 64-row activation tiles when they still give two CTAs per SM, else 32-row tiles
     const bool wide = (long)((W.N + BN - 1) / BN) * ((M + 63) / 64) >= 2 * 148;
     switch (W.type) {
-        case W_Q8_0: wide ? launch_mma<W_Q8_0, 4>(W, a, M, bias, relu, y, st) : launch_mma<W_Q8_0, 2>(W, a, M, bias, relu, y, st); return true;
-        case W_Q4_0: wide ? launch_mma<W_Q4_0, 4>(W, a, M, bias, relu, y, st) : launch_mma<W_Q4_0, 2>(W, a, M, bias, relu, y, st); return true;
-        case W_Q4_K: launch_mma<W_Q4_K, 2>(W, a, M, bias, relu, y, st); return true;
+        case W_Q8_0: wide ? launch_mma<W_Q8_0, 4>(W, a, M, bias, relu, y, qkv, st) : launch_mma<W_Q8_0, 2>(W, a, M, bias, relu, y, qkv, st); return true;
+        case W_Q4_0: wide ? launch_mma<W_Q4_0, 4>(W, a, M, bias, relu, y, qkv, st) : launch_mma<W_Q4_0, 2>(W, a, M, bias, relu, y, qkv, st); return true;
+        case W_Q4_K: launch_mma<W_Q4_K, 2>(W, a, M, bias, relu, y, qkv, st); return true;
     }
     return false;
 }
