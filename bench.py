@@ -360,6 +360,54 @@ def run_reference(args):
     }))
 
 
+def run_matmul_sweep(args):
+    """Isolated dequant-matmul sweep: weight shapes of the layer (qkv, out, ffn-up, ffn-down,
+    lm_head) x formats x activation rows, through t2sx_matmul (activation quantisation + matmul),
+    N(0,0.02) weights, N(0,1) activations, seeded per shape.  One JSON line per case."""
+    import torch
+    import gguf
+    import synth
+    import t2sx
+    import build as t2sx_build
+    t2sx_build.build()
+    torch.cuda.set_device(0)
+    shapes = [(1536, 512), (512, 512), (2048, 512), (512, 2048), (1025, 512)]
+    fmts = args.formats.split(",")
+    rows = [int(v) for v in args.rows.split(",")]
+    tid = {"q8_0": 8, "q4_0": 2, "q4_k": 12, "f16": 1}
+    stream = torch.cuda.current_stream()
+    for fmt in fmts:
+        for (N, K) in shapes:
+            rng = np.random.default_rng(hash((N, K, fmt)) % (2 ** 32))
+            w = (rng.standard_normal((N, K), dtype=np.float32) * np.float32(0.02)).astype(np.float32)
+            if fmt == "q4_k":
+                wb = synth.quantize_q4_k(w)
+            elif fmt == "f16":
+                wb = w.astype(np.float16).view(np.uint8)
+            else:
+                wb = gguf.quantize(w, gguf.GGMLQuantizationType.Q8_0 if fmt == "q8_0" else gguf.GGMLQuantizationType.Q4_0)
+            W = t2sx.Weight(tid[fmt], wb, N, K)
+            wbytes = int(np.asarray(wb).nbytes)
+            for M in rows:
+                x = torch.randn((M, K), dtype=torch.float32, device="cuda", generator=torch.Generator("cuda").manual_seed(M))
+                y = torch.empty((M, N), dtype=torch.float32, device="cuda")
+                for _ in range(3):
+                    W.matmul(x.data_ptr(), M, y.data_ptr(), stream=stream.cuda_stream)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                iters = args.steps
+                e0.record(stream)
+                for _ in range(iters):
+                    W.matmul(x.data_ptr(), M, y.data_ptr(), stream=stream.cuda_stream)
+                e1.record(stream)
+                torch.cuda.synchronize()
+                us = e0.elapsed_time(e1) * 1e3 / iters
+                flops = 2.0 * M * N * K
+                print(json.dumps({"sweep": "matmul", "format": fmt, "N": N, "K": K, "M": M, "us": round(us, 3),
+                                  "tops": round(flops / us / 1e6, 2), "weight_bytes": wbytes,
+                                  "weight_gbs": round(wbytes / us / 1e3, 1)}))
+            W.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -372,10 +420,16 @@ def main():
     ap.add_argument("--cpu-sessions", type=int, default=8)
     ap.add_argument("--cpu-steps", type=int, default=20)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--sweep", choices=["matmul"], default=None,
+                    help="isolated kernel sweep instead of the decode workload (--steps = timed iterations)")
+    ap.add_argument("--formats", default="q8_0,q4_0,q4_k,f16")
+    ap.add_argument("--rows", default="1,8,16,64,256,2048")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
-    if args.impl == "reference":
+    if args.sweep == "matmul":
+        run_matmul_sweep(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

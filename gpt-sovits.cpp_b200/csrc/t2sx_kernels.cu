@@ -6,7 +6,19 @@
 #include "t2sx_kernels.cuh"
 #include "t2sx_math.cuh"
 
+#include <cstdlib>
+
 namespace t2sx {
+
+// Off unless T2SX_PDL=1: measured on B200 inside the step graph it did not shorten the bs=1 step
+// and slowed the 32-row step (early-resident dependents hold SM slots).
+bool pdl_enabled() {
+    static const bool on = [] {
+        const char* e = getenv("T2SX_PDL");
+        return e && e[0] == '1';
+    }();
+    return on;
+}
 
 // ============================================================================================
 // activation quantisation
@@ -15,6 +27,8 @@ namespace t2sx {
 // Q8_0 (x86 AVX2 rule of ggml quantize_row_q8_0): one warp per 32-element block.
 __global__ void k_quant_q8_0(const float* __restrict__ x, int64_t nblk, int8_t* __restrict__ q,
                              float* __restrict__ d) {
+    pdl_trigger();
+    pdl_wait();
     const int lane = threadIdx.x & 31;
     const int64_t wstride = ((int64_t)gridDim.x * blockDim.x) >> 5;
     for (int64_t b = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; b < nblk; b += wstride)
@@ -52,6 +66,8 @@ __device__ __forceinline__ void quant_block_q8_K(const float* __restrict__ xb, i
 // Q8_K (ggml quantize_row_q8_K_ref rule): one warp per 256-element block.
 __global__ void k_quant_q8_K(const float* __restrict__ x, int64_t nblk, int8_t* __restrict__ q,
                              float* __restrict__ d, int32_t* __restrict__ bs) {
+    pdl_trigger();
+    pdl_wait();
     const int lane = threadIdx.x & 31;
     const int64_t wstride = ((int64_t)gridDim.x * blockDim.x) >> 5;
     for (int64_t b = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; b < nblk; b += wstride)
@@ -90,6 +106,8 @@ __device__ void quant_row512_strided(const float (&y)[kD / 32], int lane, int wt
 }
 
 __global__ void k_quant_f16(const float* __restrict__ x, int64_t n, uint16_t* __restrict__ h) {
+    pdl_trigger();
+    pdl_wait();
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
         h[i] = f2h(x[i]);
 }
@@ -104,11 +122,11 @@ static int grid_for(int64_t work, int per_block) {
 void quantize_act(int wtype, const float* x, int M, int K, ActQ& a, cudaStream_t st) {
     const int64_t n = (int64_t)M * K;
     if (wtype == W_Q8_0 || wtype == W_Q4_0) {
-        k_quant_q8_0<<<grid_for(n / 32, 8), 256, 0, st>>>(x, n / 32, a.q, a.d);
+        launch_k(k_quant_q8_0, dim3(grid_for(n / 32, 8)), dim3(256), 0, st, x, n / 32, a.q, a.d);
     } else if (wtype == W_Q4_K) {
-        k_quant_q8_K<<<grid_for(n / 256, 8), 256, 0, st>>>(x, n / 256, a.q, a.d, a.bs);
+        launch_k(k_quant_q8_K, dim3(grid_for(n / 256, 8)), dim3(256), 0, st, x, n / 256, a.q, a.d, a.bs);
     } else if (wtype == W_F16) {
-        k_quant_f16<<<grid_for(n, 256), 256, 0, st>>>(x, n, a.h);
+        launch_k(k_quant_f16, dim3(grid_for(n, 256)), dim3(256), 0, st, x, n, a.h);
     } else {
         a.f = x;
     }
@@ -356,6 +374,8 @@ template <int WT>
 __global__ void __launch_bounds__(128) k_mm_small(DevW W, ActQ A, int M, const float* __restrict__ bias, int relu,
                                                   float* __restrict__ y, QKVStore qkv, int use_qkv, Tail tail,
                                                   int use_tail) {
+    pdl_trigger();
+    pdl_wait();
     __shared__ int s_a[4][kSmallM][64];
     __shared__ int s_m[4][kSmallM][8];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -392,11 +412,11 @@ void matmul(const DevW& W, const ActQ& a, int M, const float* bias, int relu, fl
         const int grid = (W.N + 3) / 4;
         const int uq = e.qkv ? 1 : 0, ut = use_tail ? 1 : 0;
         switch (W.type) {
-            case W_Q8_0: k_mm_small<W_Q8_0><<<grid, 128, 0, st>>>(W, as, mm, bias, relu, yy, qq, uq, tail, ut); break;
-            case W_Q4_0: k_mm_small<W_Q4_0><<<grid, 128, 0, st>>>(W, as, mm, bias, relu, yy, qq, uq, tail, ut); break;
-            case W_Q4_K: k_mm_small<W_Q4_K><<<grid, 128, 0, st>>>(W, as, mm, bias, relu, yy, qq, uq, tail, ut); break;
-            case W_F16: k_mm_small<W_F16><<<grid, 128, 0, st>>>(W, as, mm, bias, relu, yy, qq, uq, tail, ut); break;
-            default: k_mm_small<W_F32><<<grid, 128, 0, st>>>(W, as, mm, bias, relu, yy, qq, uq, tail, ut); break;
+            case W_Q8_0: launch_k(k_mm_small<W_Q8_0>, dim3(grid), dim3(128), 0, st, W, as, mm, bias, relu, yy, qq, uq, tail, ut); break;
+            case W_Q4_0: launch_k(k_mm_small<W_Q4_0>, dim3(grid), dim3(128), 0, st, W, as, mm, bias, relu, yy, qq, uq, tail, ut); break;
+            case W_Q4_K: launch_k(k_mm_small<W_Q4_K>, dim3(grid), dim3(128), 0, st, W, as, mm, bias, relu, yy, qq, uq, tail, ut); break;
+            case W_F16: launch_k(k_mm_small<W_F16>, dim3(grid), dim3(128), 0, st, W, as, mm, bias, relu, yy, qq, uq, tail, ut); break;
+            default: launch_k(k_mm_small<W_F32>, dim3(grid), dim3(128), 0, st, W, as, mm, bias, relu, yy, qq, uq, tail, ut); break;
         }
     }
 }
@@ -413,6 +433,8 @@ __global__ void k_embed_decode(int T, const int32_t* __restrict__ row_slot, cons
                                const uint16_t* __restrict__ emb16, const float* __restrict__ emb32, int emb_rows,
                                const float* __restrict__ pe, int pe_rows, float alpha, Rows rows, float* __restrict__ x,
                                int qtype, ActQ qo) {
+    pdl_trigger();
+    pdl_wait();
     const int lane = threadIdx.x & 31;
     const int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     if (r >= T) return;
@@ -444,7 +466,7 @@ void embed_decode(int T, const int32_t* row_slot, const int32_t* token_in, const
                   const int32_t* audio_off, const uint16_t* emb16, const float* emb32, int emb_rows, const float* pe,
                   int pe_rows, float alpha, Rows rows, float* x, int qtype, ActQ qo, cudaStream_t st) {
     if (T > 0)
-        k_embed_decode<<<(T + 3) / 4, 128, 0, st>>>(T, row_slot, token_in, n_pos, audio_off, emb16, emb32, emb_rows, pe,
+        launch_k(k_embed_decode, dim3((T + 3) / 4), dim3(128), 0, st, T, row_slot, token_in, n_pos, audio_off, emb16, emb32, emb_rows, pe,
                                                     pe_rows, alpha, rows, x, qtype, qo);
 }
 
@@ -483,6 +505,8 @@ __device__ __forceinline__ void load_row32(const uint16_t* p, float* out) {
 template <int HPC, bool PIPE>
 __global__ void __launch_bounds__(32 * HPC) k_attn_decode(const uint16_t* __restrict__ q16, Rows rows, KVView kv, int layer,
                                                           float scale, float* __restrict__ out, int qtype, ActQ qo) {
+    pdl_trigger();
+    pdl_wait();
     __shared__ AbsMax s_am[8];
     __shared__ float s_is;
     const int r = blockIdx.x;
@@ -589,18 +613,20 @@ void attention_decode(int T, const uint16_t* q16, Rows rows, KVView kv, int laye
     // a Q8_K output block spans eight heads, so that format needs eight heads per CTA; otherwise
     // small batches spread the heads over more CTAs
     if (qtype == W_Q4_K) {
-        if (T < 64) k_attn_decode<8, true><<<dim3(T, kHeads / 8), 256, 0, st>>>(q16, rows, kv, layer, scale, out, qtype, qo);
-        else k_attn_decode<8, false><<<dim3(T, kHeads / 8), 256, 0, st>>>(q16, rows, kv, layer, scale, out, qtype, qo);
+        if (T < 64) launch_k((k_attn_decode<8, true>), dim3(dim3(T, kHeads / 8)), dim3(256), 0, st, q16, rows, kv, layer, scale, out, qtype, qo);
+        else launch_k((k_attn_decode<8, false>), dim3(dim3(T, kHeads / 8)), dim3(256), 0, st, q16, rows, kv, layer, scale, out, qtype, qo);
     } else if (T < 64) {
-        k_attn_decode<2, true><<<dim3(T, kHeads / 2), 64, 0, st>>>(q16, rows, kv, layer, scale, out, qtype, qo);
+        launch_k((k_attn_decode<2, true>), dim3(dim3(T, kHeads / 2)), dim3(64), 0, st, q16, rows, kv, layer, scale, out, qtype, qo);
     } else {
-        k_attn_decode<4, false><<<dim3(T, kHeads / 4), 128, 0, st>>>(q16, rows, kv, layer, scale, out, qtype, qo);
+        launch_k((k_attn_decode<4, false>), dim3(dim3(T, kHeads / 4)), dim3(128), 0, st, q16, rows, kv, layer, scale, out, qtype, qo);
     }
 }
 
 // Prefill attention: one thread per (row, head) folds its prefix sequentially.
 __global__ void __launch_bounds__(128) k_attn_prefill(int T, const uint16_t* __restrict__ q16, Rows rows, KVView kv,
                                                       int layer, float scale, float* __restrict__ out) {
+    pdl_trigger();
+    pdl_wait();
     const int idx = blockIdx.x * blockDim.x + threadIdx.x;
     if (idx >= T * kHeads) return;
     const int r = idx / kHeads, h = idx % kHeads;
@@ -625,7 +651,7 @@ __global__ void __launch_bounds__(128) k_attn_prefill(int T, const uint16_t* __r
 
 void attention_prefill(int T, const uint16_t* q16, Rows rows, KVView kv, int layer, float scale, float* out,
                        cudaStream_t st) {
-    if (T > 0) k_attn_prefill<<<(T * kHeads + 127) / 128, 128, 0, st>>>(T, q16, rows, kv, layer, scale, out);
+    if (T > 0) launch_k(k_attn_prefill, dim3((T * kHeads + 127) / 128), dim3(128), 0, st, T, q16, rows, kv, layer, scale, out);
 }
 
 // y = LN(a + b) * g + beta, one warp per row (ln_row_warp); the row is also written in the next
@@ -633,6 +659,8 @@ void attention_prefill(int T, const uint16_t* q16, Rows rows, KVView kv, int lay
 __global__ void k_residual_ln(int T, const float* __restrict__ a, const float* __restrict__ b,
                               const float* __restrict__ g, const float* __restrict__ beta, float eps,
                               float* __restrict__ y, int qtype, ActQ qo) {
+    pdl_trigger();
+    pdl_wait();
     const int lane = threadIdx.x & 31;
     const int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     if (r >= T) return;
@@ -645,7 +673,7 @@ __global__ void k_residual_ln(int T, const float* __restrict__ a, const float* _
 
 void residual_layernorm(int T, const float* a, const float* b, const float* g, const float* beta, float eps, float* y,
                         int qtype, ActQ qo, cudaStream_t st) {
-    if (T > 0) k_residual_ln<<<(T + 3) / 4, 128, 0, st>>>(T, a, b, g, beta, eps, y, qtype, qo);
+    if (T > 0) launch_k(k_residual_ln, dim3((T + 3) / 4), dim3(128), 0, st, T, a, b, g, beta, eps, y, qtype, qo);
 }
 
 // Greedy token over penalised logits (block.cpp:117-138 repetition penalty as masked lerps,
@@ -653,6 +681,8 @@ void residual_layernorm(int T, const float* a, const float* b, const float* g, c
 __global__ void k_sample_greedy(const float* __restrict__ logits, int V, const int32_t* __restrict__ row_slot,
                                 const uint8_t* __restrict__ seen, float rp, float inv_rp, int eos_mask, int eos,
                                 int32_t* __restrict__ tok_out, int32_t* __restrict__ greedy_out) {
+    pdl_trigger();
+    pdl_wait();
     __shared__ float s_v[8];
     __shared__ int s_i[8];
     const int r = blockIdx.x;
@@ -718,6 +748,8 @@ __global__ void __launch_bounds__(1024) k_sample_full(const float* __restrict__ 
                                                       const int32_t* __restrict__ row_slot,
                                                       const uint8_t* __restrict__ seen, SamplerArgs a,
                                                       int32_t* __restrict__ tok_out, int32_t* __restrict__ greedy_out) {
+    pdl_trigger();
+    pdl_wait();
     __shared__ float key[kSortN];
     __shared__ int idx[kSortN];
     __shared__ float prob[kSortN];
@@ -822,12 +854,12 @@ __global__ void __launch_bounds__(1024) k_sample_full(const float* __restrict__ 
 
 void sample_greedy(int T, const float* logits, int V, const int32_t* row_slot, const uint8_t* seen, float rp,
                    float inv_rp, int eos_mask, int eos, int32_t* tok_out, int32_t* greedy_out, cudaStream_t st) {
-    if (T > 0) k_sample_greedy<<<T, 256, 0, st>>>(logits, V, row_slot, seen, rp, inv_rp, eos_mask, eos, tok_out, greedy_out);
+    if (T > 0) launch_k(k_sample_greedy, dim3(T), dim3(256), 0, st, logits, V, row_slot, seen, rp, inv_rp, eos_mask, eos, tok_out, greedy_out);
 }
 
 void sample_full(int T, const float* logits, int V, const int32_t* row_slot, const uint8_t* seen, const SamplerArgs& a,
                  int32_t* tok_out, int32_t* greedy_out, cudaStream_t st) {
-    if (T > 0) k_sample_full<<<T, 1024, 0, st>>>(logits, V, row_slot, seen, a, tok_out, greedy_out);
+    if (T > 0) launch_k(k_sample_full, dim3(T), dim3(1024), 0, st, logits, V, row_slot, seen, a, tok_out, greedy_out);
 }
 
 // End of a decode step (session.cpp:247-284 on the device): feed the sampled token back,
@@ -835,6 +867,8 @@ void sample_full(int T, const float* logits, int V, const int32_t* row_slot, con
 __global__ void k_advance(int T, const int32_t* __restrict__ row_slot, const int32_t* __restrict__ tok,
                           int32_t* __restrict__ token_in, int32_t* __restrict__ n_pos, uint8_t* __restrict__ seen, int V,
                           int32_t* __restrict__ ring, int ring_len, int32_t* __restrict__ ring_step) {
+    pdl_trigger();
+    pdl_wait();
     const int step = *ring_step;
     for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < T; r += gridDim.x * blockDim.x) {
         const int s = row_slot[r];
@@ -846,23 +880,27 @@ __global__ void k_advance(int T, const int32_t* __restrict__ row_slot, const int
     }
 }
 
-__global__ void k_step_inc(int32_t* ring_step) { *ring_step += 1; }
+__global__ void k_step_inc(int32_t* ring_step) {
+    pdl_trigger();
+    pdl_wait(); *ring_step += 1; }
 
 void advance(int T, const int32_t* row_slot, const int32_t* tok, int32_t* token_in, int32_t* n_pos, uint8_t* seen,
              int V, int32_t* ring, int ring_len, int32_t* ring_step, cudaStream_t st) {
-    if (T > 0) k_advance<<<(T + 255) / 256, 256, 0, st>>>(T, row_slot, tok, token_in, n_pos, seen, V, ring, ring_len, ring_step);
-    k_step_inc<<<1, 1, 0, st>>>(ring_step);
+    if (T > 0) launch_k(k_advance, dim3((T + 255) / 256), dim3(256), 0, st, T, row_slot, tok, token_in, n_pos, seen, V, ring, ring_len, ring_step);
+    launch_k(k_step_inc, dim3(1), dim3(1), 0, st, ring_step);
 }
 
 __global__ void k_gather_rows(int n, const float* __restrict__ src, const int32_t* __restrict__ idx, int ld,
                               float* __restrict__ dst) {
+    pdl_trigger();
+    pdl_wait();
     const int r = blockIdx.x;
     if (r >= n) return;
     for (int c = threadIdx.x; c < ld; c += blockDim.x) dst[(size_t)r * ld + c] = src[(size_t)idx[r] * ld + c];
 }
 
 void gather_rows(int n, const float* src, const int32_t* idx, int ld, float* dst, cudaStream_t st) {
-    if (n > 0) k_gather_rows<<<n, 128, 0, st>>>(n, src, idx, ld, dst);
+    if (n > 0) launch_k(k_gather_rows, dim3(n), dim3(128), 0, st, n, src, idx, ld, dst);
 }
 
 // Prefill input rows (block.cpp:424-468): text row t = (emb_t + bert_proj_t) + pe[t]*alpha_t,
@@ -872,6 +910,8 @@ __global__ void k_embed_prefill(int T_text, int T_prompt, const int32_t* __restr
                                 const uint16_t* __restrict__ text16, const float* __restrict__ text32,
                                 const uint16_t* __restrict__ audio16, const float* __restrict__ audio32,
                                 const float* __restrict__ pe, float alpha_t, float alpha_a, float* __restrict__ x) {
+    pdl_trigger();
+    pdl_wait();
     const int r = blockIdx.x;
     for (int d = threadIdx.x; d < kD; d += blockDim.x) {
         float v;
@@ -894,7 +934,7 @@ void embed_prefill_rows(int T_text, int T_prompt, const int32_t* phones, const i
                         const float* pe, float alpha_t, float alpha_a, float* x, cudaStream_t st) {
     const int T = T_text + T_prompt;
     if (T > 0)
-        k_embed_prefill<<<T, 128, 0, st>>>(T_text, T_prompt, phones, sem, bert_proj, text16, text32, audio16, audio32, pe,
+        launch_k(k_embed_prefill, dim3(T), dim3(128), 0, st, T_text, T_prompt, phones, sem, bert_proj, text16, text32, audio16, audio32, pe,
                                            alpha_t, alpha_a, x);
 }
 

@@ -3,7 +3,29 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 namespace t2sx {
+
+// With T2SX_PDL=1 in the environment, kernels are launched with programmatic stream
+// serialization (PDL): each kernel lets its successor launch early and waits for its predecessor
+// before touching data that predecessor produced (see pdl_wait in t2sx_math.cuh).
+bool pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+inline void launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
+    cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 enum WType : int { W_F32 = 0, W_F16 = 1, W_Q4_0 = 2, W_Q8_0 = 8, W_Q4_K = 12 };
 

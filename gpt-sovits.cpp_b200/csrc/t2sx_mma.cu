@@ -89,6 +89,8 @@ __global__ void __launch_bounds__(256) k_mm_mma(DevW W, ActQ A, int M, const flo
     const int N = W.N, K = W.K;
     const int nb32 = K / 32, nsb = K / 256;
     const int nstage = K / (32 * KB);
+    pdl_trigger();
+    pdl_wait();
 
     auto sW = [&](int buf) { return smem + buf * C::STAGE; };
     auto sX = [&](int buf) { return smem + buf * C::STAGE + C::W_BYTES; };
@@ -316,7 +318,7 @@ static void launch_mma(const DevW& W, const ActQ& a, int M, const float* bias, i
     dim3 grid((W.N + BN - 1) / BN, (M + C::BM - 1) / C::BM);
     QKVStore q{};
     if (qkv) q = *qkv;
-    k_mm_mma<WT, MT><<<grid, 256, C::SMEM, st>>>(W, a, M, bias, relu, y, q, qkv ? 1 : 0);
+    launch_k((k_mm_mma<WT, MT>), grid, dim3(256), C::SMEM, st, W, a, M, bias, relu, y, q, qkv ? 1 : 0);
 }
 
 bool matmul_mma(const DevW& W, const ActQ& a, int M, const float* bias, int relu, float* y, const QKVStore* qkv,
