@@ -123,7 +123,8 @@ static std::vector<uint8_t> as_bytes(const std::vector<T>& v) {
 // Offsets of a repacked weight inside the arena (resolved to pointers after upload).
 struct WOff {
     int type = -1, N = 0, K = 0;
-    size_t q8 = SIZE_MAX, q4 = SIZE_MAX, d = SIZE_MAX, dmin = SIZE_MAX, scm = SIZE_MAX, h = SIZE_MAX, f = SIZE_MAX;
+    int tc_npad = 0;
+    size_t q8 = SIZE_MAX, tcw = SIZE_MAX, q4 = SIZE_MAX, d = SIZE_MAX, dmin = SIZE_MAX, scm = SIZE_MAX, h = SIZE_MAX, f = SIZE_MAX;
 };
 
 static bool repack_weight(int type, const uint8_t* src, int64_t N, int64_t K, Arena& ar, WOff& w) {
@@ -173,7 +174,33 @@ static bool repack_weight(int type, const uint8_t* src, int64_t N, int64_t K, Ar
                 }
                 memcpy(&q[(n * nsb + b) * 128], blk + 16, 128);
             }
+        // Planes for the tcgen05 path, int8 [3][Npad][K] in element order (Npad = N rounded up to
+        // 128, padding rows zero): p = sc_j * q with sub-block j of the element, plane 0 = p & 127,
+        // plane 1 = p >> 7, plane 2 = mn_j.  Then for activation block values x:
+        //   sum_k plane0*x + 128 * sum_k plane1*x = sum_j sc_j * (sum_{k in j} q*x)   and
+        //   sum_k plane2*x = sum_j mn_j * (sum_{k in j} x),
+        // the two integer sums of the Q4_K dot, exactly.  Within a super-block, byte j of 32-byte
+        // chunk c holds element 64c + j (low nibble, sub-block 2c) and 64c + 32 + j (high, 2c + 1).
+        const int64_t Npad = (N + 127) / 128 * 128;
+        std::vector<int8_t> x((size_t)3 * Npad * K, 0);
+        for (int64_t n = 0; n < N; ++n)
+            for (int64_t b = 0; b < nsb; ++b) {
+                const uint8_t* o = &scm[(n * nsb + b) * 16];
+                for (int c = 0; c < 4; ++c)
+                    for (int j = 0; j < 32; ++j) {
+                        const uint8_t v = q[(n * nsb + b) * 128 + c * 32 + j];
+                        for (int h = 0; h < 2; ++h) {
+                            const int sub = 2 * c + h, e = c * 64 + h * 32 + j;
+                            const int p = o[sub] * ((h ? v >> 4 : v) & 15);
+                            const size_t at = (size_t)n * K + b * 256 + e;
+                            x[at] = (int8_t)(p & 127);
+                            x[(size_t)Npad * K + at] = (int8_t)(p >> 7);
+                            x[(size_t)2 * Npad * K + at] = (int8_t)o[8 + sub];
+                        }
+                    }
+            }
         w.q4 = ar.add(std::move(q)); w.d = ar.add(as_bytes(d)); w.dmin = ar.add(as_bytes(dm)); w.scm = ar.add(std::move(scm));
+        w.tcw = ar.add(as_bytes(x)); w.tc_npad = (int)Npad;
     } else if (type == W_F16) {
         std::vector<uint8_t> b(src, src + (size_t)N * K * 2);
         w.h = ar.add(std::move(b));
@@ -190,7 +217,7 @@ static DevW resolve(const WOff& o, char* base) {
     DevW w;
     w.type = o.type; w.N = o.N; w.K = o.K;
     auto P = [&](size_t off) -> char* { return off == SIZE_MAX ? nullptr : base + off; };
-    w.q8 = (const int8_t*)P(o.q8); w.q4 = (const uint8_t*)P(o.q4); w.d = (const float*)P(o.d);
+    w.q8 = (const int8_t*)P(o.q8); w.tcw = (const int8_t*)P(o.tcw); w.tc_npad = o.tc_npad; w.q4 = (const uint8_t*)P(o.q4); w.d = (const float*)P(o.d);
     w.dmin = (const float*)P(o.dmin); w.scm = (const uint8_t*)P(o.scm); w.h = (const uint16_t*)P(o.h);
     w.f = (const float*)P(o.f);
     return w;

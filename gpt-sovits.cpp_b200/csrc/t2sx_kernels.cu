@@ -384,8 +384,18 @@ __global__ void __launch_bounds__(128) k_mm_small(DevW W, ActQ A, int M, const f
     if (use_tail) tail_if_last(tail, y, M, W.N);
 }
 
+int tc_min_rows() {
+    static const int v = [] {
+        const char* e = getenv("T2SX_TC_MIN_ROWS");
+        const int r = e ? atoi(e) : 64;
+        return r > 0 ? r : 64;
+    }();
+    return v;
+}
+
 void matmul(const DevW& W, const ActQ& a, int M, const float* bias, int relu, float* y, cudaStream_t st, const Epi& e) {
     const bool quant = W.type == W_Q8_0 || W.type == W_Q4_0 || W.type == W_Q4_K;
+    if (quant && M >= tc_min_rows() && matmul_tc(W, a, M, bias, relu, y, e.qkv, st)) return;
     if (quant && M > kSmallM && matmul_mma(W, a, M, bias, relu, y, e.qkv, st)) return;
     QKVStore qkv{};
     if (e.qkv) qkv = *e.qkv;

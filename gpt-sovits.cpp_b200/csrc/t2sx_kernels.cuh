@@ -38,6 +38,8 @@ enum WType : int { W_F32 = 0, W_F16 = 1, W_Q4_0 = 2, W_Q8_0 = 8, W_Q4_K = 12 };
 struct DevW {
     int type = -1, N = 0, K = 0;
     const int8_t* q8 = nullptr;
+    const int8_t* tcw = nullptr;   // Q4_K: int8 planes [3][tc_npad][K] for the tcgen05 path (see repack)
+    int tc_npad = 0;
     const uint8_t* q4 = nullptr;
     const float* d = nullptr;
     const float* dmin = nullptr;
@@ -108,6 +110,11 @@ struct Epi {
 void quantize_act(int wtype, const float* x, int M, int K, ActQ& a, cudaStream_t st);
 void matmul(const DevW& W, const ActQ& a, int M, const float* bias, int relu, float* y, cudaStream_t st,
             const Epi& epi = Epi());
+// tcgen05 path (TMA-fed, TMEM accumulators; Q4_K weights) for large M; false if not supported.
+bool matmul_tc(const DevW& W, const ActQ& a, int M, const float* bias, int relu, float* y, const QKVStore* qkv,
+               cudaStream_t st);
+// Rows from which matmul() takes the tcgen05 path (T2SX_TC_MIN_ROWS overrides).
+int tc_min_rows();
 // Tensor-core path (mma.sync s8) for M > 32; false if the shape is not supported.
 bool matmul_mma(const DevW& W, const ActQ& a, int M, const float* bias, int relu, float* y, const QKVStore* qkv,
                 cudaStream_t st);
