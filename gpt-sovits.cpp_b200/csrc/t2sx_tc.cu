@@ -18,8 +18,8 @@
 // Persistent CTAs (one per SM) walk 128-row x 64-row output tiles; 12 warps in 3 warpgroups:
 //   warp 0     : TMA producer (cp.async.bulk.tensor, 128-byte swizzle), 3-stage ring of half
 //                super-blocks (3 weight planes x 128 rows x 128 B + 64 activation rows x 128 B);
-//   warp 1     : one thread issues the 12 MMAs of a stage and the tcgen05.commit arrivals;
-//   warps 2-3  : idle (they complete the control warpgroup, which gives registers back);
+//   warps 1-3  : one thread each issues one weight plane's MMAs (4 per stage) and its tcgen05.commit
+//                arrivals (the barriers count the three issuers);
 //   warps 4-11 : fold -- warp w owns TMEM lanes 32*(w%4).. (weight rows) and 32 of the 64 columns,
 //                reads them in 8-column groups (next group's load in flight while folding), resets
 //                them to the start pattern, and stages the finished tile in smem for coalesced stores.
@@ -249,9 +249,9 @@ k_mm_tc_q4k(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUt
     const int n_tiles = tiles_n * tiles_m;
 
     if (tid == 0) {
-        for (int i = 0; i < NS; ++i) { bar_init(full0 + 8 * i, 1); bar_init(empty0 + 8 * i, 1); }
-        for (int i = 0; i < NBUF; ++i) { bar_init(tfull0 + 8 * i, 1); bar_init(tempty0 + 8 * i, EPI_WARPS); }
-        bar_init(done_bar, 1);
+        for (int i = 0; i < NS; ++i) { bar_init(full0 + 8 * i, 1); bar_init(empty0 + 8 * i, PLANES); }
+        for (int i = 0; i < NBUF; ++i) { bar_init(tfull0 + 8 * i, PLANES); bar_init(tempty0 + 8 * i, EPI_WARPS); }
+        bar_init(done_bar, PLANES);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     }
@@ -279,7 +279,7 @@ k_mm_tc_q4k(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUt
     tc_fence_after();
 
     bool aborted = false;
-    if (warp < EPI_WARP0) {   // control warpgroup: warp 0 TMA, warp 1 MMA, warps 2-3 idle
+    if (warp < EPI_WARP0) {   // control warpgroup: warp 0 TMA, warps 1-3 MMA (one plane each)
         asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;\n" ::"n"(kCtrlRegs));
         if (warp == 0) {
             // ---------------- TMA producer: stages of 128 K-elements, 2 per super-block ----------------
@@ -307,9 +307,10 @@ k_mm_tc_q4k(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUt
                     }
                 }
             }
-        } else if (warp == 1) {
-            // ---------------- MMA issuer ----------------
+        } else {
+            // ---------------- MMA issuers: warp 1 + p issues plane p's 8 MMAs of each super-block ----------------
             if (lane == 0) {
+                const int p = warp - 1;
                 int stg = 0, gsb = 0;
                 const uint64_t d0 = sdesc(smem_u32(smem));
                 for (int t = blockIdx.x; t < n_tiles && !aborted; t += gridDim.x) {
@@ -317,7 +318,7 @@ k_mm_tc_q4k(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUt
                         const int buf = gsb % NBUF;
                         if (!bar_wait(tempty0 + 8 * buf, ((gsb / NBUF) & 1) ^ 1, abort_flag)) { aborted = true; break; }
                         tc_fence_after();
-                        const uint32_t dcol = tmem + (uint32_t)(buf * BUF_COLS);
+                        const uint32_t dcol = tmem + (uint32_t)(buf * BUF_COLS + p * BN);
                         for (int h = 0; h < 2; ++h, ++stg) {
                             const int ss = stg % NS;
                             if (!bar_wait(full0 + 8 * ss, (stg / NS) & 1, abort_flag)) { aborted = true; break; }
@@ -325,19 +326,15 @@ k_mm_tc_q4k(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUt
                             // descriptor start addresses advance in 16-byte units in the low bits
                             const uint64_t dst = d0 + (uint64_t)((ss * STAGE) >> 4);
 #pragma unroll
-                            for (int kk = 0; kk < 4; ++kk) {
-                                const uint64_t bd = dst + (uint64_t)((PLANES * A_PLANE + kk * 32) >> 4);
-#pragma unroll
-                                for (int p = 0; p < PLANES; ++p)
-                                    tc_mma_i8(dcol + (uint32_t)(p * BN), dst + (uint64_t)((p * A_PLANE + kk * 32) >> 4), bd,
-                                              kIdesc, 1u);
-                            }
+                            for (int kk = 0; kk < 4; ++kk)
+                                tc_mma_i8(dcol, dst + (uint64_t)((p * A_PLANE + kk * 32) >> 4),
+                                          dst + (uint64_t)((PLANES * A_PLANE + kk * 32) >> 4), kIdesc, 1u);
                             tc_commit(empty0 + 8 * ss);
                         }
                         tc_commit(tfull0 + 8 * buf);
                     }
                 }
-                // every MMA issued above has completed once this barrier flips
+                // every MMA this thread issued has completed once the barrier flips (all three issuers)
                 tc_commit(done_bar);
                 const long long t0 = clock64();
                 while (!bar_try(done_bar, 0) && clock64() - t0 < kSpinCycles) {}
