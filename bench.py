@@ -209,6 +209,11 @@ def run_ours(args):
     # (ctx_now positions): 2 (K,V) * 16 heads * 32 dims * 2 B = 2048 B per position, plus q/out
     attn_bytes = float((ctx_now * 2048).sum() + per * (512 * 2 + 512 * 4))
     attn_gbs = attn_bytes / (prof["attention"] * 1e-3) / 1e9
+    # DRAM bytes per algorithmic byte of this kernel, from one ncu capture (dram__bytes_read.sum +
+    # dram__bytes_write.sum = 189.98 MB for 186.91 MB algorithmic, 256 sessions at context 353,
+    # profiles/k_attn_decode_256sessions.md); the full launch is too large to capture, so its
+    # traffic is that ratio times its algorithmic bytes (the kernel streams each byte once).
+    ATTN_DRAM_PER_ALGO_BYTE = 189.981184 / 186.908672
 
     # ---- CPU baseline (rank 0, N=1 only): the oracle on the host cores, bounded sample ----
     cpu = None
@@ -257,7 +262,8 @@ def run_ours(args):
                 "peak": peaks["hbm_gbs"],
                 "unit": "GB/s",
                 "frac": round(attn_gbs / peaks["hbm_gbs"], 4),
-                "traffic": None,
+                "traffic": int(attn_bytes * ATTN_DRAM_PER_ALGO_BYTE),
+                "traffic_source": "ncu dram bytes at 256 sessions scaled by algorithmic bytes",
                 "peak_kind": peak_kind,
                 "algorithmic_bytes_per_launch": int(attn_bytes),
                 "launch_ms": round(prof["attention"], 4),
