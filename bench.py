@@ -414,6 +414,69 @@ def run_matmul_sweep(args):
             W.close()
 
 
+def run_attention_sweep(args):
+    """Isolated batched attention over a paged f16 KV cache (one layer), through the
+    t2sx_kvcache_* entry points: decode = 256 sequences with prefixes uniform in [200, 1500] and one
+    query each; prefill = the same 256 sequences with 256-token prompts, causal, empty prefix.
+    K/V ~ N(0,1)/sqrt(32) and q ~ N(0,1), stored f16, seed 3.  One JSON line per case."""
+    import torch
+    import t2sx
+    import build as t2sx_build
+    t2sx_build.build()
+    torch.cuda.set_device(0)
+    peaks, peak_kind = load_peaks()
+    rng = np.random.default_rng(3)
+    n, max_len = 256, 1500
+    lens = rng.integers(200, 1501, size=n).astype(np.int32)
+    cache = t2sx.KVCache(n, max_len)
+    scale = np.float32(1.0 / np.sqrt(32.0))
+    for s_ in range(n):
+        L = int(lens[s_])
+        k = (rng.standard_normal((L, 16, 32), dtype=np.float32) * scale).astype(np.float16).view(np.uint16)
+        v = (rng.standard_normal((L, 16, 32), dtype=np.float32) * scale).astype(np.float16).view(np.uint16)
+        cache.write(s_, 0, k, v)
+    stream = torch.cuda.current_stream()
+
+    def timed(fn):
+        for _ in range(3):
+            fn()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / args.steps
+
+    seqs = np.arange(n, dtype=np.int32)
+    q = torch.randn((n, 512), generator=torch.Generator().manual_seed(3)).to(torch.float16).cuda()
+    out = torch.empty((n, 512), dtype=torch.float32, device="cuda")
+    ms = timed(lambda: cache.attn_decode(seqs, lens, q.data_ptr(), out.data_ptr(), stream=stream.cuda_stream))
+    byts = float(lens.astype(np.int64).sum() * 2048 + n * (512 * 2 + 512 * 4))
+    gbs = byts / (ms * 1e-3) / 1e9
+    print(json.dumps({"sweep": "attention", "case": "decode", "sequences": n, "prefix": "uniform [200,1500]",
+                      "sum_prefix": int(lens.sum()), "us": round(ms * 1e3, 2), "bytes": int(byts),
+                      "achieved_gbs": round(gbs, 1), "peak_gbs": peaks["hbm_gbs"], "frac": round(gbs / peaks["hbm_gbs"], 4),
+                      "peak_kind": peak_kind, "l2": "K/V %.0f MB > L2" % (byts / 1e6)}))
+    # causal prefill: 256 sequences x 256 new tokens over an empty prefix (positions 0..255 rewritten)
+    T = 256
+    for s_ in range(n):
+        k = (rng.standard_normal((T, 16, 32), dtype=np.float32) * scale).astype(np.float16).view(np.uint16)
+        v = (rng.standard_normal((T, 16, 32), dtype=np.float32) * scale).astype(np.float16).view(np.uint16)
+        cache.write(s_, 0, k, v)
+    pseqs = np.repeat(np.arange(n, dtype=np.int32), T)
+    plens = np.tile(np.arange(1, T + 1, dtype=np.int32), n)
+    pq = torch.randn((n * T, 512), generator=torch.Generator().manual_seed(4)).to(torch.float16).cuda()
+    pout = torch.empty((n * T, 512), dtype=torch.float32, device="cuda")
+    ms = timed(lambda: cache.attn_prefill(pseqs, plens, pq.data_ptr(), pout.data_ptr(), stream=stream.cuda_stream))
+    flops = float(n * 16 * 4 * 32 * (T * (T + 1) // 2))
+    print(json.dumps({"sweep": "attention", "case": "prefill", "sequences": n, "new_tokens": T, "prefix": 0,
+                      "us": round(ms * 1e3, 2), "flops": int(flops), "gflops": round(flops / (ms * 1e-3) / 1e9, 1),
+                      "unique_kv_bytes": n * T * 2048,
+                      "note": "one sequential softmax lane per (query, head): CUDA cores, not tensor cores"}))
+    cache.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -426,7 +489,7 @@ def main():
     ap.add_argument("--cpu-sessions", type=int, default=8)
     ap.add_argument("--cpu-steps", type=int, default=20)
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--sweep", choices=["matmul"], default=None,
+    ap.add_argument("--sweep", choices=["matmul", "attention"], default=None,
                     help="isolated kernel sweep instead of the decode workload (--steps = timed iterations)")
     ap.add_argument("--formats", default="q8_0,q4_0,q4_k,f16")
     ap.add_argument("--rows", default="1,8,16,64,256,2048")
@@ -435,6 +498,8 @@ def main():
         raise SystemExit("--warmup must be >= 3")
     if args.sweep == "matmul":
         run_matmul_sweep(args)
+    elif args.sweep == "attention":
+        run_attention_sweep(args)
     elif args.impl == "reference":
         run_reference(args)
     else:

@@ -56,6 +56,11 @@ SIGNATURES = {
     "t2sx_weight_free": (None, [_P]),
     "t2sx_matmul": (C.c_int, [_P, _P, _I64, _P, _P, _P]),
     "t2sx_matmul_noalloc": (C.c_int, [_P, _P, _I64, _P, _P, _P]),
+    "t2sx_kvcache_create": (C.c_int, [_I, _I, _I, _P]),
+    "t2sx_kvcache_free": (None, [_P]),
+    "t2sx_kvcache_write": (C.c_int, [_P, _I, _I, _I, _P, _P]),
+    "t2sx_kvcache_attn_decode": (C.c_int, [_P, _I, _P, _P, _P, _P, _P]),
+    "t2sx_kvcache_attn_prefill": (C.c_int, [_P, _I, _P, _P, _P, _P, _P]),
 }
 NOALLOC_MAX_ELEMS = 1 << 21
 
@@ -305,6 +310,43 @@ class Weight:
     def close(self):
         if self.h:
             lib().t2sx_weight_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class KVCache:
+    """One-layer paged f16 KV cache for the isolated attention entry points."""
+
+    def __init__(self, n_seqs: int, max_len: int, device: int = 0):
+        h = C.c_void_p()
+        _ck(lib().t2sx_kvcache_create(device, n_seqs, max_len, C.byref(h)))
+        self.h, self.n_seqs, self.max_len = h, n_seqs, max_len
+
+    def write(self, seq: int, pos0: int, k16: np.ndarray, v16: np.ndarray):
+        """k16, v16: f16 bits (uint16) [len][16][32]."""
+        k16 = np.ascontiguousarray(k16, dtype=np.uint16)
+        v16 = np.ascontiguousarray(v16, dtype=np.uint16)
+        _ck(lib().t2sx_kvcache_write(self.h, seq, pos0, k16.shape[0], _p(k16), _p(v16)))
+
+    def _attn(self, fn, seqs, lens, q_ptr: int, out_ptr: int, stream: int):
+        seqs = np.ascontiguousarray(seqs, dtype=np.int32)
+        lens = np.ascontiguousarray(lens, dtype=np.int32)
+        _ck(fn(self.h, len(seqs), _p(seqs), _p(lens), C.c_void_p(q_ptr), C.c_void_p(out_ptr), C.c_void_p(stream)))
+
+    def attn_decode(self, seqs, lens, q_ptr: int, out_ptr: int, stream: int = 0):
+        self._attn(lib().t2sx_kvcache_attn_decode, seqs, lens, q_ptr, out_ptr, stream)
+
+    def attn_prefill(self, seqs, lens, q_ptr: int, out_ptr: int, stream: int = 0):
+        self._attn(lib().t2sx_kvcache_attn_prefill, seqs, lens, q_ptr, out_ptr, stream)
+
+    def close(self):
+        if self.h:
+            lib().t2sx_kvcache_free(self.h)
             self.h = None
 
     def __del__(self):

@@ -170,6 +170,28 @@ T2SX_API int t2sx_matmul(t2sx_weight* w, const float* x_dev, int64_t M, const fl
 T2SX_API int t2sx_matmul_noalloc(t2sx_weight* w, const float* x_dev, int64_t M, const float* bias_dev,
                                  float* y_dev, void* stream);
 
+/* ---- isolated batched attention over a paged f16 KV cache (one layer) ----
+ * The attention step of t2s_attention_block_forward (src/t2s/block.cpp:575-608) on a stand-alone
+ * cache, with the decode and prefill kernels of the step: softmax(q . k^T / sqrt(32)) . v per head
+ * over positions [0, len) of a sequence.  The reference has no such entry point (its attention
+ * only runs inside the layer graph); this one serves the batched-attention checks and sweep.
+ * Calls are ordered on the stream they are given; do not overlap calls on different streams. */
+typedef struct t2sx_kvcache t2sx_kvcache;
+/* n_seqs sequences of up to max_len positions, pages zero-filled. */
+T2SX_API int t2sx_kvcache_create(int32_t device, int32_t n_seqs, int32_t max_len, t2sx_kvcache** out);
+T2SX_API void t2sx_kvcache_free(t2sx_kvcache* c);
+/* Positions [pos0, pos0 + len) of sequence seq := k, v (host, f16 bits [len][16 heads][32]). */
+T2SX_API int t2sx_kvcache_write(t2sx_kvcache* c, int32_t seq, int32_t pos0, int32_t len, const uint16_t* k,
+                                const uint16_t* v);
+/* Row r (q_dev f16 [n][512]) attends to positions [0, lens[r]) of sequence seqs[r] (host arrays);
+ * out_dev f32 [n][512].  decode: the decode kernel (32 position lanes per head, butterfly merge);
+ * prefill: the prefill kernel (one sequential lane per head) -- causal prefill rows give each
+ * query its own prefix length. */
+T2SX_API int t2sx_kvcache_attn_decode(t2sx_kvcache* c, int32_t n, const int32_t* seqs, const int32_t* lens,
+                                      const uint16_t* q_dev, float* out_dev, void* stream);
+T2SX_API int t2sx_kvcache_attn_prefill(t2sx_kvcache* c, int32_t n, const int32_t* seqs, const int32_t* lens,
+                                       const uint16_t* q_dev, float* out_dev, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -451,6 +451,21 @@ void orc_attn_prefill(const float* q, const uint16_t* k, const uint16_t* v, int 
     attn_prefill_head(qh, k, v, L, 32, out);
 }
 
+// Batched attention rows (the per-head functions above, positions strided by 16 heads x 32 dims).
+// Used for batched-attention shapes (SURVEY config 3: attention over a paged f16 cache).
+void orc_attn_rows(int n, const int* seqs, const int* lens, const uint16_t* q16, const uint16_t* k,
+                   const uint16_t* v, int max_len, int mode, float* out) {
+#pragma omp parallel for schedule(dynamic, 4)
+    for (int64_t rh = 0; rh < (int64_t)n * 16; ++rh) {
+        const int r = (int)(rh / 16), h = (int)(rh % 16);
+        float qh[32];
+        for (int d = 0; d < 32; ++d) qh[d] = h2f(q16[(size_t)r * 512 + h * 32 + d]);
+        const size_t base = ((size_t)seqs[r] * max_len) * 512 + (size_t)h * 32;
+        if (mode == 0) attn_decode_head(qh, k + base, v + base, lens[r], 512, out + (size_t)r * 512 + h * 32);
+        else attn_prefill_head(qh, k + base, v + base, lens[r], 512, out + (size_t)r * 512 + h * 32);
+    }
+}
+
 float orc_expf(float x) { return t2s_expf(x); }
 uint16_t orc_f32_to_f16(float x) { return f2h(x); }
 float orc_f16_to_f32(uint16_t h) { return h2f(h); }

@@ -308,3 +308,24 @@ def test_sampler_matches_float64_restatement(orc, top_k, top_p, temp):
     assert agree >= n - 1   # float32 vs float64 rounding can move a near-tie
     s2, g2 = m.sample(logits, noise=None)
     assert np.array_equal(s2, greedy) and np.array_equal(g2, greedy)
+
+
+def test_attn_rows_matches_per_head_calls(orc):
+    """The batched oracle attention (used for the batched-attention parity tests) is the per-head
+    decode / prefill restatement applied row by row."""
+    rng = np.random.default_rng(0)
+    S, Lm = 3, 150
+    k = (rng.standard_normal((S, Lm, 16, 32)) / np.sqrt(32)).astype(np.float16).view(np.uint16)
+    v = (rng.standard_normal((S, Lm, 16, 32)) / np.sqrt(32)).astype(np.float16).view(np.uint16)
+    q = rng.standard_normal((4, 512)).astype(np.float16)
+    seqs, lens = [0, 2, 1, 2], [150, 37, 1, 100]
+    for mode, fn in ((0, "orc_attn_decode"), (1, "orc_attn_prefill")):
+        out = orc.attn_rows(seqs, lens, q.view(np.uint16), k, v, mode)
+        for r in range(4):
+            for h in range(16):
+                kk = np.ascontiguousarray(k[seqs[r], :, h, :])
+                vv = np.ascontiguousarray(v[seqs[r], :, h, :])
+                qq = np.ascontiguousarray(q[r, h * 32:(h + 1) * 32].astype(np.float32))
+                o = np.empty(32, np.float32)
+                getattr(orc.lib(), fn)(orc.ptr(qq), orc.ptr(kk), orc.ptr(vv), lens[r], orc.ptr(o))
+                assert np.array_equal(o.view(np.uint32), out[r, h * 32:(h + 1) * 32].view(np.uint32)), (mode, r, h)
