@@ -6,7 +6,7 @@
  * the prefill and the autoregressive decode step on one CUDA device.  Plain pointers and sizes
  * only; every function returns a status (T2SX_OK == 0) and t2sx_last_error() describes the
  * last failure of the calling thread.  Citations name the reference interface each entry point
- * replaces (include/gpt_sovits/t2s.h, src/t2s/*.cpp).
+ * replaces (include/gpt_sovits/t2s.h and the sources under src/t2s).
  *
  * Threading: a session is a single-owner object (as t2s_session is); different sessions may be
  * driven from different host threads.  All device work of a session runs on its own stream.

@@ -49,7 +49,7 @@ def lib():
             "orc_embed_prefill": (I, [P, P, P, I, P, I, P]),
             "orc_prefill": (I, [P, I, P, I, I, I, P, P, P]),
             "orc_decode_step": (I, [P, I, P, P, P, F, I, P, P]),
-            "orc_slot_n_pos": (I, [P, I]), "orc_read_kv": (I, [P, I, I, I, P]),
+            "orc_slot_n_pos": (I, [P, I]), "orc_slot_release": (I, [P, I]), "orc_read_kv": (I, [P, I, I, I, P]),
             "orc_sample": (I, [P, I, P, P, P, I, F, F, F, I, P, P]),
             "orc_decode_step2": (I, [P, I, P, P, P, P, I, F, F, F, I, P, P, P]),
         }
@@ -193,6 +193,10 @@ class Session:
         if rc != 0:
             raise RuntimeError("oracle decode rejected")
         return sampled, greedy
+
+    def release(self, slot):
+        if lib().orc_slot_release(self.h, slot) != 0:
+            raise RuntimeError("oracle release rejected")
 
     def n_pos(self, slot):
         return lib().orc_slot_n_pos(self.h, slot)

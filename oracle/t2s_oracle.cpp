@@ -616,6 +616,14 @@ void* orc_session_new(void* model, int n_slots, int capacity) {
     return s;
 }
 void orc_session_free(void* sess) { delete (Session*)sess; }
+int orc_slot_release(void* sess, int slot) {
+    Session* S = (Session*)sess;
+    if (slot < 0 || slot >= S->n_slots) return -1;
+    S->n_pos[slot] = 0;
+    S->audio_off[slot] = 0;
+    return 0;
+}
+
 int orc_slot_n_pos(void* sess, int slot) { return ((Session*)sess)->n_pos[slot]; }
 
 static void matmul_rows(const Tensor* W, const Tensor* bias, const float* x, int64_t M, float* y) {

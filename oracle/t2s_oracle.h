@@ -74,6 +74,8 @@ int      orc_decode_step2(void* sess, int n, const int32_t* slots, const int32_t
                           float temperature, float rp, int eos_mask, int32_t* sampled_out,
                           int32_t* greedy_out, float* logits_out);
 int      orc_slot_n_pos(void* sess, int slot);
+// t2s_session_slot_release (session.cpp:224-240): the slot becomes idle (n_pos = 0).
+int      orc_slot_release(void* sess, int slot);
 // Sampler chain (block.cpp:52-348) on n rows of logits f32 [n][vocab]; seen f32 [n][vocab] or
 // null; noise f32 [n][vocab] Exp(1) samples indexed by sorted position, or null (greedy).
 int      orc_sample(void* model, int n, const float* logits, const float* seen, const float* noise,

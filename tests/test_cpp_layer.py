@@ -1,0 +1,110 @@
+"""The C++ session layer (include/gpt_sovits/t2s_cuda.h) as a C++ host uses it.
+
+tests/cpp/t2s_decode_loop.cpp is the reference's decode loop (test_t2s_infer.cpp:204-421 shape:
+prefill through flex plans, persistent decode graph steps, a mixed prefill/decode plan) written
+against that header; it is compiled with g++ and linked to libt2sx.so.  On a GPU its tokens must
+equal the oracle's; illegal slot transitions must abort, as GGML_ASSERT does in the reference
+(the reference death-tests them in test_t2s_session.cpp:1008-1031).
+"""
+import json
+import os
+import shutil
+import signal
+import subprocess
+
+import numpy as np
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+PKG = os.path.join(ROOT, "gpt-sovits.cpp_b200")
+SRC = os.path.join(ROOT, "tests", "cpp", "t2s_decode_loop.cpp")
+
+
+def _compile(tmp_path):
+    gxx = shutil.which("g++")
+    if gxx is None:
+        pytest.fail("g++ is required to build the C++ host program")
+    exe = str(tmp_path / "t2s_decode_loop")
+    cmd = [gxx, "-std=c++17", "-O2", "-Wall", "-Wextra", "-Werror", "-I", os.path.join(ROOT, "include"), SRC,
+           "-L", PKG, "-lt2sx", f"-Wl,-rpath,{PKG}", "-o", exe]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    return exe
+
+
+def test_cpp_layer_compiles_and_links(t2sx_mod, tmp_path):
+    """The header compiles warning-free under -Wall -Wextra -Werror and links against the library."""
+    exe = _compile(tmp_path)
+    assert os.path.exists(exe)
+
+
+def _write_inputs(path, prompts):
+    with open(path, "wb") as f:
+        np.array([len(prompts)], dtype=np.int32).tofile(f)
+        for ph, bert, sem in prompts:
+            np.array([ph.size, sem.size], dtype=np.int32).tofile(f)
+            ph.astype(np.int32).tofile(f)
+            bert.astype(np.float32).tofile(f)
+            sem.astype(np.int32).tofile(f)
+
+
+def _case(tmp_path):
+    import synth
+    path = synth.ensure_gguf("q4_k", seed=5, n_layer=2)
+    specs = [(40, 30, 101), (25, 50, 102), (60, 20, 103)]   # two sessions, then the refill of slot 0
+    prompts = [synth.session_inputs(seed, tt, tp) for tt, tp, seed in specs]
+    inp = str(tmp_path / "inputs.bin")
+    _write_inputs(inp, prompts)
+    return path, prompts, inp
+
+
+def _oracle(orc, path, prompts, n_steps):
+    m = orc.Model(path)
+    n = len(prompts) - 1
+    cap = max(p[0].size + p[2].size for p in prompts) + 2 * n_steps + 2
+    s = orc.Session(m, n, cap)
+    first = []
+    for i in range(n):
+        ph, bert, sem = prompts[i]
+        tok, _, _ = s.prefill(i, m.embed_prefill(ph, bert, sem), sem.size, eos_mask=True)
+        first.append(tok)
+    steps, cur = [], list(first)
+    for _ in range(n_steps):
+        out, _ = s.decode(np.arange(n), cur, eos_mask=True)
+        steps.append([int(t) for t in out]); cur = list(out)
+    # mixed plan: slot 0 released and refilled, the other slots decode one step
+    s.release(0)
+    out, _ = s.decode(np.arange(1, n), cur[1:], eos_mask=True)
+    ph, bert, sem = prompts[n]
+    refill, _, _ = s.prefill(0, m.embed_prefill(ph, bert, sem), sem.size, eos_mask=True)
+    mixed = [refill] + [int(t) for t in out]
+    cur = list(mixed)
+    for _ in range(n_steps):
+        out, _ = s.decode(np.arange(n), cur, eos_mask=True)
+        steps.append([int(t) for t in out]); cur = list(out)
+    s.close(); m.close()
+    return {"first": [int(t) for t in first], "mixed": mixed, "steps": steps}
+
+
+@pytest.mark.gpu
+def test_cpp_decode_loop_matches_oracle(t2sx_mod, orc, tmp_path):
+    exe = _compile(tmp_path)
+    path, prompts, inp = _case(tmp_path)
+    n_steps = 6
+    r = subprocess.run([exe, path, inp, str(n_steps)], capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stderr
+    got = json.loads(r.stdout)
+    want = _oracle(orc, path, prompts, n_steps)
+    assert got == want
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("mode,msg", [("release_bad", "slot id out of range"),
+                                      ("decode_idle", "decode of an idle slot"),
+                                      ("plan_idle", "an active slot left idle in a decoding plan")])
+def test_cpp_illegal_transitions_abort(t2sx_mod, tmp_path, mode, msg):
+    exe = _compile(tmp_path)
+    path, _, inp = _case(tmp_path)
+    r = subprocess.run([exe, path, inp, "2", mode], capture_output=True, text=True, timeout=600)
+    assert r.returncode == -signal.SIGABRT, (r.returncode, r.stderr)
+    assert msg in r.stderr
