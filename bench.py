@@ -134,6 +134,11 @@ def run_ours(args):
     per = hi - lo
     lengths_all = session_prompts(args.workload, total_sessions)
     mine = lengths_all[lo:hi]
+    # rank 0 writes the synthetic GGUF (once per cache directory); the others wait for it
+    if rank == 0:
+        path = synth.ensure_gguf(w["wtype"], w["seed"], n_layer=24)
+    if world > 1:
+        dist.barrier()
     path = synth.ensure_gguf(w["wtype"], w["seed"], n_layer=24)
 
     W, K = args.warmup, args.steps

@@ -97,7 +97,9 @@ def write_gguf(path: str, wtype: int, seed: int, n_layer: int = 24, d=512, ff=20
                vocab=1025, phone_vocab=732, eos=1024) -> str:
     import gguf
     rng = np.random.default_rng(seed)
-    tmp = path + ".tmp"
+    # one temporary name per process: several ranks may generate the same file at once; the
+    # final rename is atomic and any of the identical results may win
+    tmp = f"{path}.tmp.{os.getpid()}"
     writer = gguf.GGUFWriter(tmp, "t2s")
     for k, v in [("t2s.embedding_dim", d), ("t2s.hidden_dim", d), ("t2s.head", n_head),
                  ("t2s.linear_units", ff), ("t2s.n_layer", n_layer), ("t2s.vocab_size", vocab),
