@@ -384,6 +384,15 @@ __global__ void __launch_bounds__(128) k_mm_small(DevW W, ActQ A, int M, const f
     if (use_tail) tail_if_last(tail, y, M, W.N);
 }
 
+int narrow_min_rows() {
+    static const int v = [] {
+        const char* e = getenv("T2SX_NARROW_MIN_ROWS");
+        const int r = e ? atoi(e) : 8;
+        return r > 0 ? r : 8;
+    }();
+    return v;
+}
+
 int tc_min_rows() {
     static const int v = [] {
         const char* e = getenv("T2SX_TC_MIN_ROWS");
@@ -397,6 +406,8 @@ void matmul(const DevW& W, const ActQ& a, int M, const float* bias, int relu, fl
     const bool quant = W.type == W_Q8_0 || W.type == W_Q4_0 || W.type == W_Q4_K;
     if (quant && M >= tc_min_rows() && matmul_tc(W, a, M, bias, relu, y, e.qkv, st)) return;
     if (quant && M > kSmallM && matmul_mma(W, a, M, bias, relu, y, e.qkv, st)) return;
+    if (quant && M >= narrow_min_rows() && !(e.tail && M <= kSmallM) && matmul_mma_narrow(W, a, M, bias, relu, y, e.qkv, st))
+        return;
     QKVStore qkv{};
     if (e.qkv) qkv = *e.qkv;
     Tail tail{};

@@ -115,6 +115,12 @@ bool matmul_tc(const DevW& W, const ActQ& a, int M, const float* bias, int relu,
                cudaStream_t st);
 // Rows from which matmul() takes the tcgen05 path (T2SX_TC_MIN_ROWS overrides).
 int tc_min_rows();
+// mma.sync path with 32-weight-row tiles for M <= 32 (enough CTAs when there are few rows).
+bool matmul_mma_narrow(const DevW& W, const ActQ& a, int M, const float* bias, int relu, float* y, const QKVStore* qkv,
+                       cudaStream_t st);
+// Rows from which matmul() takes the narrow mma.sync path instead of the per-row kernel
+// (T2SX_NARROW_MIN_ROWS overrides).
+int narrow_min_rows();
 // Tensor-core path (mma.sync s8) for M > 32; false if the shape is not supported.
 bool matmul_mma(const DevW& W, const ActQ& a, int M, const float* bias, int relu, float* y, const QKVStore* qkv,
                 cudaStream_t st);

@@ -42,13 +42,16 @@ __device__ __forceinline__ int lds32(const uint8_t* p) { return *reinterpret_cas
 // exact int -> float for |i| < 2^22 (block dots of Q8_0 / Q4_0 are below 2^19)
 __device__ __forceinline__ float i2f_small(int i) { return __fsub_rn(__int_as_float(0x4B400000 + i), 12582912.0f); }
 
-constexpr int BN = 128;          // weight rows per CTA
 constexpr int KB = 4;            // 32-element blocks per stage
 constexpr int XROW = KB * 32 + 16;   // smem bytes per activation row (int8, padded)
 
-template <int WT, int MT_>
+template <int WT, int MT_, int WN_, int NSTG_ = 2>
 struct Cfg {
+    static constexpr int NSTG = NSTG_;                            // cp.async ring depth (stages)
     static constexpr int MT = MT_;                                // m8 tiles per warp
+    static constexpr int WN = WN_;                                // warps along the weight rows
+    static constexpr int NT = 64 * WN;                            // threads (WN x 2 warps)
+    static constexpr int BN = 32 * WN;                            // weight rows per CTA
     static constexpr int BM = 2 * 8 * MT;                         // activation rows per CTA
     static constexpr int WROW = (WT == W_Q8_0) ? KB * 32 + 16 : KB * 16 + 16;  // weight bytes per row
     static constexpr int W_BYTES = BN * WROW;
@@ -57,7 +60,7 @@ struct Cfg {
     static constexpr int DX_BYTES = BM * KB * 4;                  // f32 [m][KB] (Q4_K: bs32 int [m][KB])
     static constexpr int K_EXTRA = (WT == W_Q4_K) ? (BN * 16 + BN * 8 + BM * 4) : 0;  // scm, d+dmin, dx8k
     static constexpr int STAGE = W_BYTES + X_BYTES + DW_BYTES + DX_BYTES + K_EXTRA;
-    static constexpr int SMEM = 2 * STAGE;
+    static constexpr int SMEM = NSTG * STAGE;
 };
 
 __device__ __forceinline__ size_t kv_off_m(const KVView& kv, int page, int layer, int which, int head, int pos_in_page) {
@@ -76,15 +79,16 @@ __device__ __forceinline__ void qkv_store_m(const QKVStore& e, int m, int n, flo
     e.kv.pool[kv_off_m(e.kv, page, e.layer, which, j / kHeadDim, pos % kPage) + (j % kHeadDim)] = h;
 }
 
-template <int WT, int MT_>
-__global__ void __launch_bounds__(256) k_mm_mma(DevW W, ActQ A, int M, const float* __restrict__ bias, int relu,
+template <int WT, int MT_, int WN_, int NSTG_>
+__global__ void __launch_bounds__(64 * WN_) k_mm_mma(DevW W, ActQ A, int M, const float* __restrict__ bias, int relu,
                                                 float* __restrict__ y, QKVStore qkv, int use_qkv) {
-    using C = Cfg<WT, MT_>;
-    constexpr int MT = C::MT, BM = C::BM, WROW = C::WROW;
+    using C = Cfg<WT, MT_, WN_, NSTG_>;
+    constexpr int NSTG = C::NSTG;
+    constexpr int MT = C::MT, BM = C::BM, WROW = C::WROW, BN = C::BN, NT = C::NT;
     extern __shared__ __align__(16) uint8_t smem[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int g = lane >> 2, t = lane & 3;
-    const int wn = warp & 3, wm = warp >> 2;
+    const int wn = warp % C::WN, wm = warp / C::WN;
     const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
     const int N = W.N, K = W.K;
     const int nb32 = K / 32, nsb = K / 256;
@@ -106,26 +110,26 @@ __global__ void __launch_bounds__(256) k_mm_mma(DevW W, ActQ A, int M, const flo
         const int kb0 = stg * KB;
         uint8_t* w = sW(buf);
         if (WT == W_Q8_0) {
-            for (int i = tid; i < BN * 8; i += 256) {
+            for (int i = tid; i < BN * 8; i += NT) {
                 const int row = i >> 3, c = i & 7, n = n0 + row;
                 const bool ok = n < N;
                 cp_async16(w + row * WROW + c * 16, ok ? (const void*)(W.q8 + (size_t)n * K + kb0 * 32 + c * 16) : (const void*)W.q8, ok);
             }
         } else if (WT == W_Q4_0) {
-            for (int i = tid; i < BN * 4; i += 256) {
+            for (int i = tid; i < BN * 4; i += NT) {
                 const int row = i >> 2, c = i & 3, n = n0 + row;
                 const bool ok = n < N;
                 cp_async16(w + row * WROW + c * 16, ok ? (const void*)(W.q4 + ((size_t)n * nb32 + kb0 + c) * 16) : (const void*)W.q4, ok);
             }
         } else {  // Q4_K: half a super-block (64 nibble bytes) per row per stage
             const int sb = kb0 >> 3, half = (kb0 >> 2) & 1;
-            for (int i = tid; i < BN * 4; i += 256) {
+            for (int i = tid; i < BN * 4; i += NT) {
                 const int row = i >> 2, c = i & 3, n = n0 + row;
                 const bool ok = n < N;
                 cp_async16(w + row * WROW + c * 16,
                            ok ? (const void*)(W.q4 + ((size_t)n * nsb + sb) * 128 + half * 64 + c * 16) : (const void*)W.q4, ok);
             }
-            for (int i = tid; i < BN; i += 256) {
+            for (int i = tid; i < BN; i += NT) {
                 const int n = n0 + i;
                 const bool ok = n < N;
                 cp_async16(sScm(buf) + i * 16, ok ? (const void*)(W.scm + ((size_t)n * nsb + sb) * 16) : (const void*)W.scm, ok);
@@ -134,19 +138,19 @@ __global__ void __launch_bounds__(256) k_mm_mma(DevW W, ActQ A, int M, const flo
             }
         }
         if (WT != W_Q4_K) {
-            for (int i = tid; i < BN; i += 256) {
+            for (int i = tid; i < BN; i += NT) {
                 const int n = n0 + i;
                 const bool ok = n < N;
                 cp_async16(sDw(buf) + i * KB, ok ? (const void*)(W.d + (size_t)n * nb32 + kb0) : (const void*)W.d, ok);
             }
         }
         uint8_t* x = sX(buf);
-        for (int i = tid; i < BM * 8; i += 256) {
+        for (int i = tid; i < BM * 8; i += NT) {
             const int row = i >> 3, c = i & 7, m = m0 + row;
             const bool ok = m < M;
             cp_async16(x + row * XROW + c * 16, ok ? (const void*)(A.q + (size_t)m * K + kb0 * 32 + c * 16) : (const void*)A.q, ok);
         }
-        for (int i = tid; i < BM; i += 256) {
+        for (int i = tid; i < BM; i += NT) {
             const int m = m0 + i;
             const bool ok = m < M;
             if (WT == W_Q4_K) {
@@ -168,16 +172,23 @@ __global__ void __launch_bounds__(256) k_mm_mma(DevW W, ActQ A, int M, const flo
 #pragma unroll
             for (int e = 0; e < 4; ++e) { acc[i][j][e] = 0.0f; accm[i][j][e] = 0.0f; sa[i][j][e] = 0; sm[i][j][e] = 0; }
 
-    load_stage(0, 0);
+    // ring of NSTG stages: stage s lives in buffer s % NSTG; every iteration commits one group
+    // (empty past the end) so that waiting for all but the newest NSTG - 2 groups means stage stg
+    // has landed
+#pragma unroll
+    for (int s0 = 0; s0 < NSTG - 1; ++s0) {
+        if (s0 < nstage) load_stage(s0, s0);
+        else cp_commit();
+    }
     for (int stg = 0; stg < nstage; ++stg) {
-        const int buf = stg & 1;
-        if (stg + 1 < nstage) {
-            load_stage(stg + 1, buf ^ 1);
-            cp_wait<1>();
-        } else {
-            cp_wait<0>();
+        const int buf = stg % NSTG;
+        cp_wait<NSTG - 2>();
+        __syncthreads();   // stage stg visible to all; buffer (stg - 1) % NSTG no longer read
+        {
+            const int nxt = stg + NSTG - 1;
+            if (nxt < nstage) load_stage(nxt, nxt % NSTG);
+            else cp_commit();
         }
-        __syncthreads();
         const uint8_t* w = sW(buf);
         const uint8_t* x = sX(buf);
 #pragma unroll
@@ -285,7 +296,6 @@ __global__ void __launch_bounds__(256) k_mm_mma(DevW W, ActQ A, int M, const flo
                 }
             }
         }
-        __syncthreads();
     }
 #pragma unroll
     for (int i = 0; i < 2; ++i)
@@ -305,31 +315,47 @@ __global__ void __launch_bounds__(256) k_mm_mma(DevW W, ActQ A, int M, const flo
             }
 }
 
-template <int WT, int MT>
+template <int WT, int MT, int WN = 4, int NSTG = 2>
 static void launch_mma(const DevW& W, const ActQ& a, int M, const float* bias, int relu, float* y, const QKVStore* qkv,
                        cudaStream_t st) {
-    using C = Cfg<WT, MT>;
+    using C = Cfg<WT, MT, WN, NSTG>;
     static bool configured = false;   // the attribute is per function; set once per process
     if (!configured) {
-        if (cudaFuncSetAttribute(k_mm_mma<WT, MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess)
+        if (cudaFuncSetAttribute(k_mm_mma<WT, MT, WN, NSTG>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess)
             return;   // the launch below then fails and the caller's launch check reports it
         configured = true;
     }
-    dim3 grid((W.N + BN - 1) / BN, (M + C::BM - 1) / C::BM);
+    dim3 grid((W.N + C::BN - 1) / C::BN, (M + C::BM - 1) / C::BM);
     QKVStore q{};
     if (qkv) q = *qkv;
-    launch_k((k_mm_mma<WT, MT>), grid, dim3(256), C::SMEM, st, W, a, M, bias, relu, y, q, qkv ? 1 : 0);
+    launch_k((k_mm_mma<WT, MT, WN, NSTG>), grid, dim3(C::NT), C::SMEM, st, W, a, M, bias, relu, y, q, qkv ? 1 : 0);
 }
 
 bool matmul_mma(const DevW& W, const ActQ& a, int M, const float* bias, int relu, float* y, const QKVStore* qkv,
                 cudaStream_t st) {
     if (W.K % (32 * KB)) return false;
     // 64-row activation tiles when they still give two CTAs per SM, else 32-row tiles
-    const bool wide = (long)((W.N + BN - 1) / BN) * ((M + 63) / 64) >= 2 * 148;
+    const bool wide = (long)((W.N + 127) / 128) * ((M + 63) / 64) >= 2 * 148;
     switch (W.type) {
         case W_Q8_0: wide ? launch_mma<W_Q8_0, 4>(W, a, M, bias, relu, y, qkv, st) : launch_mma<W_Q8_0, 2>(W, a, M, bias, relu, y, qkv, st); return true;
         case W_Q4_0: wide ? launch_mma<W_Q4_0, 4>(W, a, M, bias, relu, y, qkv, st) : launch_mma<W_Q4_0, 2>(W, a, M, bias, relu, y, qkv, st); return true;
         case W_Q4_K: launch_mma<W_Q4_K, 2>(W, a, M, bias, relu, y, qkv, st); return true;
+    }
+    return false;
+}
+
+// Narrow tiles (32 weight rows x 16 or 32 activation rows, 2 warps per CTA) for few activation
+// rows: the whole matmul then spreads over N/32 CTAs, and the activation tile is staged once per
+// CTA in shared memory instead of being re-read per weight row.  With few CTAs per SM the K loop
+// is latency-bound, so the ring keeps 5 stages (640 elements of K) in flight.
+bool matmul_mma_narrow(const DevW& W, const ActQ& a, int M, const float* bias, int relu, float* y, const QKVStore* qkv,
+                       cudaStream_t st) {
+    if (W.K % (32 * KB) || M > 32) return false;
+    const bool m16 = M <= 16;
+    switch (W.type) {
+        case W_Q8_0: m16 ? launch_mma<W_Q8_0, 1, 1, 6>(W, a, M, bias, relu, y, qkv, st) : launch_mma<W_Q8_0, 2, 1, 6>(W, a, M, bias, relu, y, qkv, st); return true;
+        case W_Q4_0: m16 ? launch_mma<W_Q4_0, 1, 1, 6>(W, a, M, bias, relu, y, qkv, st) : launch_mma<W_Q4_0, 2, 1, 6>(W, a, M, bias, relu, y, qkv, st); return true;
+        case W_Q4_K: m16 ? launch_mma<W_Q4_K, 1, 1, 6>(W, a, M, bias, relu, y, qkv, st) : launch_mma<W_Q4_K, 2, 1, 6>(W, a, M, bias, relu, y, qkv, st); return true;
     }
     return false;
 }

@@ -41,7 +41,7 @@ def same_bits(a, b):
 
 @pytest.mark.parametrize("fmt", ["q8_0", "q4_0", "q4_k", "f16", "f32"])
 @pytest.mark.parametrize("NK", [(1536, 512), (512, 2048), (1025, 512)])
-@pytest.mark.parametrize("M", [1, 7, 32, 33, 64, 65, 130, 255, 2048])
+@pytest.mark.parametrize("M", [1, 7, 8, 16, 17, 32, 33, 64, 65, 130, 255, 2048])
 def test_matmul_bit_exact(t2sx_mod, orc, fmt, NK, M):
     _need_gpu()
     if fmt in ("f16", "f32") and M > 33:
