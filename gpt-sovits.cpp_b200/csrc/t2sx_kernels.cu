@@ -5,6 +5,7 @@
 // order per reduction; see t2sx_math.cuh.  Built with --fmad=false.
 #include "t2sx_kernels.cuh"
 #include "t2sx_math.cuh"
+#include "t2sx_kv.cuh"
 
 #include <cstdlib>
 
@@ -157,10 +158,6 @@ __device__ __forceinline__ float epi(float acc, const float* bias, int n, int re
 }
 
 constexpr int kSmallM = 32;
-
-__device__ __forceinline__ size_t kv_off(const KVView& kv, int page, int layer, int which, int head, int pos_in_page) {
-    return (((((size_t)page * kv.n_layer + layer) * 2 + which) * kHeads + head) * kPage + pos_in_page) * kHeadDim;
-}
 
 // QKV projection output element (row m, column n) -> Q as f16 for attention, K / V as f16 into
 // the row's cache page (ggml_set_rows into an F16 cache, block.cpp:557-573).
@@ -489,32 +486,6 @@ void embed_decode(int T, const int32_t* row_slot, const int32_t* token_in, const
     if (T > 0)
         launch_k(k_embed_decode, dim3((T + 3) / 4), dim3(128), 0, st, T, row_slot, token_in, n_pos, audio_off, emb16, emb32, emb_rows, pe,
                                                     pe_rows, alpha, rows, x, qtype, qo);
-}
-
-__device__ __forceinline__ void unpack_row32(const uint4 (&u4)[4], float* out) {
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-        const uint32_t w[4] = {u4[c].x, u4[c].y, u4[c].z, u4[c].w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            out[c * 8 + 2 * e] = h2f((uint16_t)(w[e] & 0xffffu));
-            out[c * 8 + 2 * e + 1] = h2f((uint16_t)(w[e] >> 16));
-        }
-    }
-}
-
-__device__ __forceinline__ void load_row32(const uint16_t* p, float* out) {
-    const uint4* p4 = reinterpret_cast<const uint4*>(p);
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-        const uint4 u = p4[c];
-        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            out[c * 8 + 2 * e] = h2f((uint16_t)(w[e] & 0xffffu));
-            out[c * 8 + 2 * e + 1] = h2f((uint16_t)(w[e] >> 16));
-        }
-    }
 }
 
 // Decode attention: one warp per (row, head), eight heads of a row per CTA.  Position lane

@@ -1,0 +1,41 @@
+// Paged KV cache addressing and f16 row loads shared by the attention and matmul kernels.
+#pragma once
+#include "t2sx_kernels.cuh"
+#include "t2sx_math.cuh"
+
+namespace t2sx {
+
+// Element offset of (page, layer, K|V, head, position in page, dim 0) in the page pool.
+__device__ __forceinline__ size_t kv_off(const KVView& kv, int page, int layer, int which, int head, int pos_in_page) {
+    return (((((size_t)page * kv.n_layer + layer) * 2 + which) * kHeads + head) * kPage + pos_in_page) * kHeadDim;
+}
+
+// 32 f16 values (four 16-byte chunks, in order) -> f32
+__device__ __forceinline__ void unpack_row32(const uint4 (&u4)[4], float* out) {
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        const uint32_t w[4] = {u4[c].x, u4[c].y, u4[c].z, u4[c].w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            out[c * 8 + 2 * e] = h2f((uint16_t)(w[e] & 0xffffu));
+            out[c * 8 + 2 * e + 1] = h2f((uint16_t)(w[e] >> 16));
+        }
+    }
+}
+
+// 32 consecutive f16 values at p (16-byte aligned) -> f32
+__device__ __forceinline__ void load_row32(const uint16_t* p, float* out) {
+    const uint4* p4 = reinterpret_cast<const uint4*>(p);
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        const uint4 u = p4[c];
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            out[c * 8 + 2 * e] = h2f((uint16_t)(w[e] & 0xffffu));
+            out[c * 8 + 2 * e + 1] = h2f((uint16_t)(w[e] >> 16));
+        }
+    }
+}
+
+}  // namespace t2sx

@@ -13,6 +13,7 @@
 // (high nibble), i.e. exactly the a0/a2 (and a1/a3) register pairs of one 32-bit load.
 #include "t2sx_kernels.cuh"
 #include "t2sx_math.cuh"
+#include "t2sx_kv.cuh"
 
 namespace t2sx {
 
@@ -63,10 +64,6 @@ struct Cfg {
     static constexpr int SMEM = NSTG * STAGE;
 };
 
-__device__ __forceinline__ size_t kv_off_m(const KVView& kv, int page, int layer, int which, int head, int pos_in_page) {
-    return (((((size_t)page * kv.n_layer + layer) * 2 + which) * kHeads + head) * kPage + pos_in_page) * kHeadDim;
-}
-
 // QKV projection output element -> Q as f16, K / V as f16 into the row's cache page.
 __device__ __forceinline__ void qkv_store_m(const QKVStore& e, int m, int n, float v) {
     const uint16_t h = f2h(v);
@@ -76,7 +73,7 @@ __device__ __forceinline__ void qkv_store_m(const QKVStore& e, int m, int n, flo
     if (pos < 0 || pos >= e.rows.cap[s]) return;
     const int page = e.kv.ptab[(size_t)s * e.kv.max_pages + pos / kPage];
     const int which = (n - kD) / kD, j = (n - kD) % kD;
-    e.kv.pool[kv_off_m(e.kv, page, e.layer, which, j / kHeadDim, pos % kPage) + (j % kHeadDim)] = h;
+    e.kv.pool[kv_off(e.kv, page, e.layer, which, j / kHeadDim, pos % kPage) + (j % kHeadDim)] = h;
 }
 
 template <int WT, int MT_, int WN_, int NSTG_>

@@ -30,6 +30,7 @@
 // in the row error flag when it has one.
 #include "t2sx_kernels.cuh"
 #include "t2sx_math.cuh"
+#include "t2sx_kv.cuh"
 
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -215,9 +216,6 @@ __device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
 // exact int -> float for |i| < 2^22 (block dots of Q8_0 / Q4_0 are below 2^19)
 __device__ __forceinline__ float i2f_small(int i) { return __fsub_rn(__int_as_float(0x4B400000 + i), 12582912.0f); }
 
-__device__ __forceinline__ size_t kv_off(const KVView& kv, int page, int layer, int which, int head, int pos_in_page) {
-    return (((((size_t)page * kv.n_layer + layer) * 2 + which) * kHeads + head) * kPage + pos_in_page) * kHeadDim;
-}
 __device__ __forceinline__ void qkv_store(const QKVStore& e, int m, int n, float v) {
     const uint16_t h = f2h(v);
     if (n < kD) { e.q16[(size_t)m * kD + n] = h; return; }
