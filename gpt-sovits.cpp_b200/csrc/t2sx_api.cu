@@ -625,13 +625,8 @@ static void run_layers(t2sx_session* s, Work& w, int T, bool decode, int final_q
         Epi e_qkv;
         e_qkv.qkv = &qs;
         matmul(L.qkv, act_for(w, w.x), T, L.qkv_b, 0, nullptr, s->st, e_qkv);
-        if (decode) {
-            attention_decode(T, w.q16, rows, kv, l, kAttnScale, w.attn, L.out.type, act_of(w), s->st);
-        } else {
-            attention_prefill(T, w.q16, rows, kv, l, kAttnScale, w.attn, s->st);
-            ActQ a = act_of(w);
-            quantize_act(L.out.type, w.attn, T, kD, a, s->st);
-        }
+        // decode and prefill rows alike: the row attends to positions [0, L) of its slot
+        attention_decode(T, w.q16, rows, kv, l, kAttnScale, w.attn, L.out.type, act_of(w), s->st);
         if (small) {
             Tail t1;
             t1.kind = 1; t1.resid = w.x; t1.g = L.ln1_w; t1.beta = L.ln1_b; t1.eps = 1e-5f; t1.y_out = w.ln1;

@@ -614,38 +614,6 @@ void attention_decode(int T, const uint16_t* q16, Rows rows, KVView kv, int laye
     }
 }
 
-// Prefill attention: one thread per (row, head) folds its prefix sequentially.
-__global__ void __launch_bounds__(128) k_attn_prefill(int T, const uint16_t* __restrict__ q16, Rows rows, KVView kv,
-                                                      int layer, float scale, float* __restrict__ out) {
-    pdl_trigger();
-    pdl_wait();
-    const int idx = blockIdx.x * blockDim.x + threadIdx.x;
-    if (idx >= T * kHeads) return;
-    const int r = idx / kHeads, h = idx % kHeads;
-    const int s = rows.slot[r];
-    const int L = rows.L[r];
-    float q[kHeadDim];
-    load_row32(q16 + (size_t)r * kD + h * kHeadDim, q);
-    AttnState st;
-    st_empty(st);
-    const int32_t* pt = kv.ptab + (size_t)s * kv.max_pages;
-    for (int i = 0; i < L; ++i) {
-        const int page = pt[i / kPage];
-        float k[kHeadDim], v[kHeadDim];
-        load_row32(kv.pool + kv_off(kv, page, layer, 0, h, i % kPage), k);
-        load_row32(kv.pool + kv_off(kv, page, layer, 1, h, i % kPage), v);
-        st_update(st, __fmul_rn(dot32(q, k), scale), v);
-    }
-    const float inv = __fdiv_rn(1.0f, st.l);
-#pragma unroll
-    for (int d = 0; d < kHeadDim; ++d) out[(size_t)r * kD + h * kHeadDim + d] = __fmul_rn(st.o[d], inv);
-}
-
-void attention_prefill(int T, const uint16_t* q16, Rows rows, KVView kv, int layer, float scale, float* out,
-                       cudaStream_t st) {
-    if (T > 0) launch_k(k_attn_prefill, dim3((T * kHeads + 127) / 128), dim3(128), 0, st, T, q16, rows, kv, layer, scale, out);
-}
-
 // y = LN(a + b) * g + beta, one warp per row (ln_row_warp); the row is also written in the next
 // matmul's dot type when qtype >= 0.
 __global__ void k_residual_ln(int T, const float* __restrict__ a, const float* __restrict__ b,

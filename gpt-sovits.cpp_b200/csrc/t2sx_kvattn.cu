@@ -1,9 +1,9 @@
 // Isolated batched attention over a paged f16 KV cache (one layer).
 //
 // The reference computes attention inside t2s_attention_block_forward (src/t2s/block.cpp:575-608)
-// on its session cache; these entry points run the same two kernels the decode step and the
-// prefill use (k_attn_decode, k_attn_prefill) on a stand-alone cache, so the attention can be
-// checked and measured on its own at batched-attention shapes (many sequences, long prefixes).
+// on its session cache; these entry points run the attention kernel of the decode step and the
+// prefill (k_attn_decode) on a stand-alone cache, so the attention can be checked and measured on
+// its own at batched-attention shapes (many sequences, long prefixes, causal prefill rows).
 // Pages have the session layout with one layer: element (page, kv, head, pos, dim) at
 // (((page * 2 + kv) * 16 + head) * 64 + pos) * 32 + dim; sequence s owns pages
 // [s * pages_per_seq, (s + 1) * pages_per_seq).
@@ -156,7 +156,7 @@ static int kv_rows(t2sx_kvcache* c, int32_t n, const int32_t* seqs, const int32_
 }
 
 static int kv_attn(t2sx_kvcache* c, int32_t n, const int32_t* seqs, const int32_t* lens, const uint16_t* q, float* out,
-                   void* stream, bool prefill) {
+                   void* stream) {
     if (!c || n <= 0 || !seqs || !lens || !q || !out) return t2sx_set_error(T2SX_ERR_INVALID, "attention: bad arguments");
     KCK(cudaSetDevice(c->device));
     cudaStream_t st = (cudaStream_t)stream;
@@ -166,18 +166,18 @@ static int kv_attn(t2sx_kvcache* c, int32_t n, const int32_t* seqs, const int32_
     KVView kv;
     kv.pool = c->pool; kv.ptab = c->ptab; kv.max_pages = c->pages_per_seq; kv.n_layer = 1;
     const float scale = 1.0f / sqrtf((float)kHeadDim);
-    if (prefill) attention_prefill(n, q, rows, kv, 0, scale, out, st);
-    else attention_decode(n, q, rows, kv, 0, scale, out, -1, ActQ(), st);
+    attention_decode(n, q, rows, kv, 0, scale, out, -1, ActQ(), st);
     KCK(cudaGetLastError());
     return T2SX_OK;
 }
 
 extern "C" int t2sx_kvcache_attn_decode(t2sx_kvcache* c, int32_t n, const int32_t* seqs, const int32_t* lens,
                                         const uint16_t* q, float* out, void* stream) {
-    return kv_attn(c, n, seqs, lens, q, out, stream, false);
+    return kv_attn(c, n, seqs, lens, q, out, stream);
 }
 
 extern "C" int t2sx_kvcache_attn_prefill(t2sx_kvcache* c, int32_t n, const int32_t* seqs, const int32_t* lens,
                                          const uint16_t* q, float* out, void* stream) {
-    return kv_attn(c, n, seqs, lens, q, out, stream, true);
+    // the same computation: causal prefill rows differ only in their prefix lengths
+    return kv_attn(c, n, seqs, lens, q, out, stream);
 }

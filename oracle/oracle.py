@@ -39,8 +39,8 @@ def lib():
             "orc_quantize_q8_0": (None, [P, I64, P]), "orc_quantize_q8_K": (None, [P, I64, P]),
             "orc_dequantize": (None, [I, P, I64, P]),
             "orc_matmul": (I, [I, P, I64, I64, P, I64, P]),
-            "orc_attn_decode": (None, [P, P, P, I, P]), "orc_attn_prefill": (None, [P, P, P, I, P]),
-            "orc_attn_rows": (None, [I, P, P, P, P, P, I, I, P]),
+            "orc_attn_decode": (None, [P, P, P, I, P]),
+            "orc_attn_rows": (None, [I, P, P, P, P, P, I, P]),
             "orc_layernorm": (None, [P, P, P, I, F, P]), "orc_pe_row": (None, [I, I, P]),
             "orc_model_load": (P, [C.c_char_p]), "orc_model_free": (None, [P]),
             "orc_model_info": (I, [P, P, P]),
@@ -77,16 +77,16 @@ def matmul(wtype: int, w_bytes: np.ndarray, N: int, K: int, x: np.ndarray) -> np
     return y
 
 
-def attn_rows(seqs, lens, q16: np.ndarray, k16: np.ndarray, v16: np.ndarray, mode: int) -> np.ndarray:
+def attn_rows(seqs, lens, q16: np.ndarray, k16: np.ndarray, v16: np.ndarray) -> np.ndarray:
     """Batched attention rows; k16/v16 f16 bits [n_seqs][max_len][16][32], q16 f16 bits [n][512].
-    mode 0 = decode lane order, 1 = prefill order.  Returns f32 [n][512]."""
+    Returns f32 [n][512]."""
     seqs = np.ascontiguousarray(seqs, dtype=np.int32)
     lens = np.ascontiguousarray(lens, dtype=np.int32)
     q16 = np.ascontiguousarray(q16, dtype=np.uint16)
     k16 = np.ascontiguousarray(k16, dtype=np.uint16)
     v16 = np.ascontiguousarray(v16, dtype=np.uint16)
     out = np.empty((len(seqs), 512), dtype=np.float32)
-    lib().orc_attn_rows(len(seqs), ptr(seqs), ptr(lens), ptr(q16), ptr(k16), ptr(v16), k16.shape[1], mode, ptr(out))
+    lib().orc_attn_rows(len(seqs), ptr(seqs), ptr(lens), ptr(q16), ptr(k16), ptr(v16), k16.shape[1], ptr(out))
     return out
 
 

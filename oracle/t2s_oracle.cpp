@@ -28,8 +28,8 @@
 //               strided sequential sums combined by an xor butterfly.
 //   flash_attn  K/V rounded to f16 by set_rows, Q rounded to f16; score = 32-term dot (4
 //               sequential fma chains of 8, summed pairwise) * (1/sqrt(32)); softmax-weighted V
-//               accumulated in f32 with the online (running-max) update.  Decode: 32 position
-//               lanes (lane = pos mod 32) merged by an xor butterfly; prefill: one sequential lane.
+//               accumulated in f32 with the online (running-max) update.  Every row (decode and
+//               prefill): 32 position lanes (lane = pos mod 32) merged by an xor butterfly.
 //               ggml's F16-V kernel keeps its VKQ accumulator in f16; this order keeps f32.
 //   exp         own Cody-Waite + degree-7 Taylor polynomial (t2s_expf below), identical on GPU.
 #include "t2s_oracle.h"
@@ -428,41 +428,22 @@ static void attn_decode_head(const float* q, const uint16_t* k, const uint16_t* 
     for (int d = 0; d < 32; ++d) out[d] = R.o[d] * inv;
 }
 
-static void attn_prefill_head(const float* q, const uint16_t* k, const uint16_t* v, int L,
-                              int64_t stride, float* out) {
-    AttnState st;
-    st_empty(st);
-    for (int i = 0; i < L; ++i) {
-        const float s = dot32(q, k + i * stride) * kAttnScale;
-        st_update(st, s, v + i * stride);
-    }
-    const float inv = 1.0f / st.l;
-    for (int d = 0; d < 32; ++d) out[d] = st.o[d] * inv;
-}
-
 void orc_attn_decode(const float* q, const uint16_t* k, const uint16_t* v, int L, float* out) {
     float qh[32];
     for (int d = 0; d < 32; ++d) qh[d] = h2f(f2h(q[d]));
     attn_decode_head(qh, k, v, L, 32, out);
 }
-void orc_attn_prefill(const float* q, const uint16_t* k, const uint16_t* v, int L, float* out) {
-    float qh[32];
-    for (int d = 0; d < 32; ++d) qh[d] = h2f(f2h(q[d]));
-    attn_prefill_head(qh, k, v, L, 32, out);
-}
-
 // Batched attention rows (the per-head functions above, positions strided by 16 heads x 32 dims).
 // Used for batched-attention shapes (SURVEY config 3: attention over a paged f16 cache).
 void orc_attn_rows(int n, const int* seqs, const int* lens, const uint16_t* q16, const uint16_t* k,
-                   const uint16_t* v, int max_len, int mode, float* out) {
+                   const uint16_t* v, int max_len, float* out) {
 #pragma omp parallel for schedule(dynamic, 4)
     for (int64_t rh = 0; rh < (int64_t)n * 16; ++rh) {
         const int r = (int)(rh / 16), h = (int)(rh % 16);
         float qh[32];
         for (int d = 0; d < 32; ++d) qh[d] = h2f(q16[(size_t)r * 512 + h * 32 + d]);
         const size_t base = ((size_t)seqs[r] * max_len) * 512 + (size_t)h * 32;
-        if (mode == 0) attn_decode_head(qh, k + base, v + base, lens[r], 512, out + (size_t)r * 512 + h * 32);
-        else attn_prefill_head(qh, k + base, v + base, lens[r], 512, out + (size_t)r * 512 + h * 32);
+        attn_decode_head(qh, k + base, v + base, lens[r], 512, out + (size_t)r * 512 + h * 32);
     }
 }
 
@@ -636,9 +617,9 @@ static void matmul_rows(const Tensor* W, const Tensor* bias, const float* x, int
 }
 
 // Rows of one forward pass: row r belongs to slot[r], writes KV position pos[r], attends to
-// prefix [0, L[r]) of its slot, using the decode (128 lanes) or prefill (sequential) order.
+// prefix [0, L[r]) of its slot (32 position lanes per head, butterfly merge).
 static void forward_rows(Session* S, int64_t T, const int* slot, const int* pos, const int* L,
-                         bool decode_order, float* x /* [T][d], in/out */) {
+                         float* x /* [T][d], in/out */) {
     Model* m = S->m;
     const int d = (int)m->hp[1], nl = (int)m->hp[4], F = (int)m->hp[3], H = (int)m->hp[2];
     const int hd = d / H;
@@ -660,8 +641,7 @@ static void forward_rows(Session* S, int64_t T, const int* slot, const int* pos,
             for (int i = 0; i < hd; ++i) qh[i] = h2f(f2h(qkv[t * 3 * d + hh * hd + i]));
             const uint16_t* kb = &S->K[(size_t)slot[t] * nl + li][hh * hd];
             const uint16_t* vb = &S->V[(size_t)slot[t] * nl + li][hh * hd];
-            if (decode_order) attn_decode_head(qh, kb, vb, L[t], d, &attn[t * d + hh * hd]);
-            else attn_prefill_head(qh, kb, vb, L[t], d, &attn[t * d + hh * hd]);
+            attn_decode_head(qh, kb, vb, L[t], d, &attn[t * d + hh * hd]);
         }
         matmul_rows(Lw.out_w, Lw.out_b, attn.data(), T, o.data());
         for (int64_t i = 0; i < T * d; ++i) r[i] = x[i] + o[i];
@@ -788,7 +768,7 @@ int orc_prefill(void* sess, int slot, const float* x, int nq, int T_prompt, int 
 #ifdef _OPENMP
     if (g_threads > 0) omp_set_num_threads(g_threads);
 #endif
-    forward_rows(S, nq, sl.data(), pos.data(), L.data(), false, xs.data());
+    forward_rows(S, nq, sl.data(), pos.data(), L.data(), xs.data());
     if (y_out) memcpy(y_out, xs.data(), sizeof(float) * xs.size());
     std::vector<float> logits(m->hp[5]);
     matmul_rows(m->lm_head, nullptr, &xs[(size_t)(nq - 1) * d], 1, logits.data());
@@ -821,7 +801,7 @@ static int decode_forward(Session* S, int n, const int32_t* slots, const int32_t
         for (int k = 0; k < d; ++k) x[(size_t)i * d + k] = e[k] + S->pe[(size_t)pe_pos * d + k] * alpha;
         sl[i] = s; pos[i] = S->n_pos[s]; L[i] = S->n_pos[s] + 1;
     }
-    forward_rows(S, n, sl.data(), pos.data(), L.data(), true, x.data());
+    forward_rows(S, n, sl.data(), pos.data(), L.data(), x.data());
     logits.assign((size_t)n * V, 0.0f);
     matmul_rows(m->lm_head, nullptr, x.data(), n, logits.data());
     for (int i = 0; i < n; ++i) S->n_pos[slots[i]] += 1;

@@ -37,12 +37,11 @@ int      orc_matmul(int wtype, const void* w, int64_t N, int64_t K,
                     const float* x, int64_t M, float* y);
 // One head of attention.  q f32[32]; k,v f16 [L][32]; out f32[32].
 void     orc_attn_decode(const float* q, const uint16_t* k, const uint16_t* v, int L, float* out);
-void     orc_attn_prefill(const float* q, const uint16_t* k, const uint16_t* v, int L, float* out);
 // Batched rows over per-sequence caches k, v: f16 bits [n_seqs][max_len][16][32].  Row r: q f16
 // bits [n][512], every head attends to positions [0, lens[r]) of sequence seqs[r]; out f32 [n][512].
-// mode 0: the decode lane order (32 lanes + butterfly), mode 1: the prefill order (one lane).
+// 32 position lanes merged by the xor butterfly, as for every attention row.
 void     orc_attn_rows(int n, const int* seqs, const int* lens, const uint16_t* q16, const uint16_t* k,
-                       const uint16_t* v, int max_len, int mode, float* out);
+                       const uint16_t* v, int max_len, float* out);
 void     orc_layernorm(const float* x, const float* g, const float* b, int n, float eps, float* y);
 void     orc_pe_row(int pos, int d_model, float* out);
 

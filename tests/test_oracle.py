@@ -148,7 +148,7 @@ def test_attention_orders_match_float64(orc):
         s = (k.astype(np.float64) @ qh) * float(np.float32(1) / np.sqrt(np.float32(32)))
         p = np.exp(s - s.max())
         ref = (p / p.sum()) @ v.astype(np.float64)
-        for fn in (L.orc_attn_decode, L.orc_attn_prefill):
+        for fn in (L.orc_attn_decode,):
             out = np.zeros(32, dtype=np.float32)
             fn(orc.ptr(q), orc.ptr(k.view(np.uint16)), orc.ptr(v.view(np.uint16)), n, orc.ptr(out))
             assert np.abs(out - ref).max() < 2e-6 * max(1, np.abs(ref).max()), (n, fn)
@@ -312,15 +312,15 @@ def test_sampler_matches_float64_restatement(orc, top_k, top_p, temp):
 
 def test_attn_rows_matches_per_head_calls(orc):
     """The batched oracle attention (used for the batched-attention parity tests) is the per-head
-    decode / prefill restatement applied row by row."""
+    restatement applied row by row."""
     rng = np.random.default_rng(0)
     S, Lm = 3, 150
     k = (rng.standard_normal((S, Lm, 16, 32)) / np.sqrt(32)).astype(np.float16).view(np.uint16)
     v = (rng.standard_normal((S, Lm, 16, 32)) / np.sqrt(32)).astype(np.float16).view(np.uint16)
     q = rng.standard_normal((4, 512)).astype(np.float16)
     seqs, lens = [0, 2, 1, 2], [150, 37, 1, 100]
-    for mode, fn in ((0, "orc_attn_decode"), (1, "orc_attn_prefill")):
-        out = orc.attn_rows(seqs, lens, q.view(np.uint16), k, v, mode)
+    for fn in ("orc_attn_decode",):
+        out = orc.attn_rows(seqs, lens, q.view(np.uint16), k, v)
         for r in range(4):
             for h in range(16):
                 kk = np.ascontiguousarray(k[seqs[r], :, h, :])
@@ -328,4 +328,4 @@ def test_attn_rows_matches_per_head_calls(orc):
                 qq = np.ascontiguousarray(q[r, h * 32:(h + 1) * 32].astype(np.float32))
                 o = np.empty(32, np.float32)
                 getattr(orc.lib(), fn)(orc.ptr(qq), orc.ptr(kk), orc.ptr(vv), lens[r], orc.ptr(o))
-                assert np.array_equal(o.view(np.uint32), out[r, h * 32:(h + 1) * 32].view(np.uint32)), (mode, r, h)
+                assert np.array_equal(o.view(np.uint32), out[r, h * 32:(h + 1) * 32].view(np.uint32)), (r, h)
