@@ -521,36 +521,54 @@ __global__ void __launch_bounds__(32 * HPC) k_attn_decode(const uint16_t* __rest
             st_update(st, __fmul_rn(dot32(q, k), scale), v);
         }
     }
-    // PIPE (small batches, latency-bound): the K/V rows of the lane's next position are in
-    // flight while the current one is folded (fold order unchanged; costs registers)
-    uint4 kr[4], vr[4];
-    int i = PIPE ? lane : L;
-    if (i < L) {
-        const int page = pt[i / kPage];
-        const uint4* kp = reinterpret_cast<const uint4*>(kv.pool + kv_off(kv, page, layer, 0, h, i % kPage));
-        const uint4* vp = reinterpret_cast<const uint4*>(kv.pool + kv_off(kv, page, layer, 1, h, i % kPage));
+    if (PIPE) {
+        // Small batches (latency-bound): each lane keeps D of its positions in flight with
+        // cp.async into its own slots of a shared-memory ring ([slot][16-byte chunk][thread], so
+        // a warp's reads of one chunk are bank-conflict free); the fold order is unchanged.  All
+        // lanes of a warp read the same page at a step (positions lane + 32k lie in page k / 2),
+        // so the row's page numbers are staged in shared memory first.
+        constexpr int NT = 32 * HPC;
+        constexpr int D = 16 / HPC;
+        extern __shared__ __align__(16) uint8_t dsm[];
+        int32_t* s_pt = reinterpret_cast<int32_t*>(dsm + D * 8 * NT * 16);
+        const int np = (L + kPage - 1) / kPage;
+        for (int j = threadIdx.x; j < np; j += NT) s_pt[j] = pt[j];
+        __syncthreads();
+        const int nk = (L - lane + kAttnLanes - 1) / kAttnLanes;   // this lane's positions
+        auto issue = [&](int k) {
+            if (k < nk) {
+                const int i = lane + kAttnLanes * k;
+                const int page = s_pt[k >> 1];
+                const uint16_t* kp = kv.pool + kv_off(kv, page, layer, 0, h, i % kPage);
+                const uint16_t* vp = kv.pool + kv_off(kv, page, layer, 1, h, i % kPage);
+                uint8_t* dst = dsm + (size_t)(k % D) * 8 * NT * 16 + threadIdx.x * 16;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) { kr[c] = kp[c]; vr[c] = vp[c]; }
-    }
-    int next_page = (i + kAttnLanes < L) ? pt[(i + kAttnLanes) / kPage] : 0;
-    while (i < L) {
-        const int in = i + kAttnLanes;
-        uint4 kn[4], vn[4];
-        if (in < L) {
-            const uint4* kp = reinterpret_cast<const uint4*>(kv.pool + kv_off(kv, next_page, layer, 0, h, in % kPage));
-            const uint4* vp = reinterpret_cast<const uint4*>(kv.pool + kv_off(kv, next_page, layer, 1, h, in % kPage));
+                for (int c = 0; c < 4; ++c) {
+                    cp_async16(dst + c * NT * 16, kp + 8 * c, true);
+                    cp_async16(dst + (4 + c) * NT * 16, vp + 8 * c, true);
+                }
+            }
+            cp_commit();
+        };
 #pragma unroll
-            for (int c = 0; c < 4; ++c) { kn[c] = kp[c]; vn[c] = vp[c]; }
-            next_page = (in + kAttnLanes < L) ? pt[(in + kAttnLanes) / kPage] : 0;
+        for (int k = 0; k < D - 1; ++k) issue(k);
+        for (int k = 0; k < nk; ++k) {
+            asm volatile("" ::: "memory");   // the previous step's reads of that slot stay before the refill
+            issue(k + D - 1);   // into the slot read in the previous step
+            cp_wait<D - 1>();
+            const uint8_t* src = dsm + (size_t)(k % D) * 8 * NT * 16 + threadIdx.x * 16;
+            uint4 kr[4], vr[4];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                kr[c] = *reinterpret_cast<const uint4*>(src + c * NT * 16);
+                vr[c] = *reinterpret_cast<const uint4*>(src + (4 + c) * NT * 16);
+            }
+            float k32[kHeadDim], v32[kHeadDim];
+            unpack_row32(kr, k32);
+            unpack_row32(vr, v32);
+            st_update(st, __fmul_rn(dot32(q, k32), scale), v32);
         }
-        float k[kHeadDim], v[kHeadDim];
-        unpack_row32(kr, k);
-        unpack_row32(vr, v);
-        const float sc = __fmul_rn(dot32(q, k), scale);
-        st_update(st, sc, v);
-#pragma unroll
-        for (int c = 0; c < 4; ++c) { kr[c] = kn[c]; vr[c] = vn[c]; }
-        i = in;
+        cp_wait<0>();
     }
 #pragma unroll
     for (int off = 16; off >= 1; off >>= 1) {
@@ -599,16 +617,28 @@ __global__ void __launch_bounds__(32 * HPC) k_attn_decode(const uint16_t* __rest
     }
 }
 
+// Dynamic shared memory of the small-batch (PIPE) attention variant: the cp.async ring plus the
+// row's page numbers; the kernel's limit is raised once.
+template <int HPC>
+static size_t attn_pipe_smem(const KVView& kv) {
+    static bool configured = false;
+    if (!configured) {
+        cudaFuncSetAttribute(k_attn_decode<HPC, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        configured = true;
+    }
+    return (size_t)(16 / HPC) * 8 * (32 * HPC) * 16 + (size_t)kv.max_pages * 4;
+}
+
 void attention_decode(int T, const uint16_t* q16, Rows rows, KVView kv, int layer, float scale, float* out, int qtype,
                       ActQ qo, cudaStream_t st) {
     if (T <= 0) return;
     // a Q8_K output block spans eight heads, so that format needs eight heads per CTA; otherwise
     // small batches spread the heads over more CTAs
     if (qtype == W_Q4_K) {
-        if (T < 64) launch_k((k_attn_decode<8, true>), dim3(dim3(T, kHeads / 8)), dim3(256), 0, st, q16, rows, kv, layer, scale, out, qtype, qo);
+        if (T < 64) launch_k((k_attn_decode<8, true>), dim3(dim3(T, kHeads / 8)), dim3(256), attn_pipe_smem<8>(kv), st, q16, rows, kv, layer, scale, out, qtype, qo);
         else launch_k((k_attn_decode<8, false>), dim3(dim3(T, kHeads / 8)), dim3(256), 0, st, q16, rows, kv, layer, scale, out, qtype, qo);
     } else if (T < 64) {
-        launch_k((k_attn_decode<2, true>), dim3(dim3(T, kHeads / 2)), dim3(64), 0, st, q16, rows, kv, layer, scale, out, qtype, qo);
+        launch_k((k_attn_decode<2, true>), dim3(dim3(T, kHeads / 2)), dim3(64), attn_pipe_smem<2>(kv), st, q16, rows, kv, layer, scale, out, qtype, qo);
     } else {
         launch_k((k_attn_decode<4, false>), dim3(dim3(T, kHeads / 4)), dim3(128), 0, st, q16, rows, kv, layer, scale, out, qtype, qo);
     }

@@ -10,6 +10,22 @@ __device__ __forceinline__ size_t kv_off(const KVView& kv, int page, int layer, 
     return (((((size_t)page * kv.n_layer + layer) * 2 + which) * kHeads + head) * kPage + pos_in_page) * kHeadDim;
 }
 
+// cp.async copies global -> shared (16 or 4 bytes; a false `valid` copies nothing and zero-fills),
+// grouped per thread by commit; wait until at most N of this thread's groups are pending.
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool valid) {
+    const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+    const int n = valid ? 16 : 0;
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(s), "l"(gmem), "r"(n));
+}
+__device__ __forceinline__ void cp_async4(void* smem, const void* gmem, bool valid) {
+    const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+    const int n = valid ? 4 : 0;
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(s), "l"(gmem), "r"(n));
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N>
+__device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
+
 // 32 f16 values (four 16-byte chunks, in order) -> f32
 __device__ __forceinline__ void unpack_row32(const uint4 (&u4)[4], float* out) {
 #pragma unroll
