@@ -10,6 +10,7 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <memory>
@@ -607,12 +608,22 @@ static ActQ act_for(Work& w, const float* f32_input) {
 // rows and, when final_qtype >= 0, the activation buffer holds them in that dot type.  For one or
 // two rows the residual + LayerNorm runs in the last CTA of the preceding matmul; otherwise it is
 // its own kernel.
+// Rows up to which the residual + LayerNorm runs as the last CTA's tail of the preceding matmul
+// (T2SX_LN_TAIL_ROWS overrides; 0 = always a separate kernel).
+static int tail_rows() {
+    static const int v = [] {
+        const char* e = getenv("T2SX_LN_TAIL_ROWS");
+        return e ? atoi(e) : 2;
+    }();
+    return v;
+}
+
 static void run_layers(t2sx_session* s, Work& w, int T, bool decode, int final_qtype) {
     const t2sx_model* m = s->m;
     Rows rows = rows_of(s, w);
     KVView kv = kv_of(s);
-    // last-CTA LayerNorm tails pay off only for one or two rows (the tail runs on one CTA)
-    const bool small = T <= 2;
+    // last-CTA LayerNorm tails: at most tail_rows() rows (the tail runs on one CTA)
+    const bool small = T <= tail_rows();
     const int nl = s->n_layer;
     for (int l = 0; l < nl; ++l) {
         const LayerD& L = m->layers[l];
