@@ -348,6 +348,12 @@ struct t2sx_model {
     const uint16_t* audio16 = nullptr; const float* audio32 = nullptr; int audio_rows = 0;
     const uint16_t* text16 = nullptr; const float* text32 = nullptr; int text_rows = 0;
     float alpha_text = 1.0f, alpha_audio = 1.0f;
+    // extract-latent: Conv1d(768, 768, k=2, s=2) as a 768 x 1536 weight, the codebook as an
+    // n_codes x 768 weight, and 0.5 * ||E_c||^2 per code
+    DevW ssl_w, codebook;
+    const float* ssl_b = nullptr;
+    const float* code_half_norm = nullptr;
+    int n_codes = 0;
 };
 
 static const float* fptr(char* base, size_t off) { return (const float*)(base + off); }
@@ -421,6 +427,31 @@ extern "C" int t2sx_model_load(const char* path, int32_t device, t2sx_model** ou
         return rc;
     for (const char* n : {"extract_latent.ssl_proj_w", "extract_latent.ssl_proj_b", "extract_latent.codebook"})
         if (!g.t.count(n)) return fail(T2SX_ERR_FORMAT, "tensor '%s' not found in GGUF", n);
+    // extract-latent (block.cpp:140-189): kernel {2, 768, 768} = 768 rows of [ic][k], codebook
+    // {768, n_codes} kept f32 (convert_t2s_to_gguf.py keeps it un-quantised)
+    const GTensor* sw = &g.t.at("extract_latent.ssl_proj_w");
+    const GTensor* sbias = &g.t.at("extract_latent.ssl_proj_b");
+    const GTensor* cb = &g.t.at("extract_latent.codebook");
+    if (sw->ne[0] != 2 || sw->ne[1] != 768 || sw->ne[2] != 768 || sbias->ne[0] != 768 || sbias->ne[1] != 1 ||
+        cb->ne[0] != 768 || cb->type != W_F32 || cb->ne[1] < 1)
+        return fail(T2SX_ERR_FORMAT, "extract_latent tensors have unexpected shapes or types");
+    WOff swo, cbo;
+    if (!repack_weight(sw->type, sw->data, 768, 1536, ar, swo) || !repack_weight(W_F32, cb->data, cb->ne[1], 768, ar, cbo))
+        return fail(T2SX_ERR_FORMAT, "extract_latent weight type %d unsupported", sw->type);
+    size_t sbo;
+    if ((rc = add_f32(sbias, sbo))) return rc;
+    size_t hno;
+    {
+        // ggml_sqr, ggml_sum_rows (sequential double sum of the f32 squares), ggml_scale(0.5)
+        std::vector<float> hn((size_t)cb->ne[1]);
+        const float* E = (const float*)cb->data;
+        for (int64_t c = 0; c < cb->ne[1]; ++c) {
+            double sum = 0.0;
+            for (int d = 0; d < 768; ++d) { const float e = E[c * 768 + d]; sum += (double)(e * e); }
+            hn[c] = (float)sum * 0.5f;
+        }
+        hno = ar.add(as_bytes(hn));
+    }
     WOff lmo, bwo;
     size_t bbo;
     if ((rc = add_w(lm, lmo)) || (rc = add_w(bw, bwo)) || (rc = add_f32(bb, bbo))) return rc;
@@ -457,6 +488,11 @@ extern "C" int t2sx_model_load(const char* path, int32_t device, t2sx_model** ou
     if (ae->type == W_F16) m->audio16 = (const uint16_t*)(base + aeo); else m->audio32 = (const float*)(base + aeo);
     m->text_rows = (int)te->ne[1];
     m->audio_rows = (int)ae->ne[1];
+    m->ssl_w = resolve(swo, base);
+    m->codebook = resolve(cbo, base);
+    m->ssl_b = fptr(base, sbo);
+    m->code_half_norm = fptr(base, hno);
+    m->n_codes = (int)cb->ne[1];
     *out = m.release();
     return T2SX_OK;
 }
@@ -1300,5 +1336,51 @@ extern "C" int t2sx_matmul(t2sx_weight* w, const float* x, int64_t M, const floa
     quantize_act(w->w.type, x, (int)M, (int)K, a, st);
     matmul(w->w, a, (int)M, bias, 0, y, st);
     CK(cudaGetLastError());
+    return T2SX_OK;
+}
+
+// ============================================================================================
+// extract-latent (t2s_session_compute_ref_emb's code extraction, session.cpp:881-1044;
+// sovits_extract_latent_block_forward, block.cpp:140-189)
+// ============================================================================================
+extern "C" int t2sx_extract_latent(t2sx_session* s, const float* hubert, int32_t T, int32_t* codes_out) {
+    if (!s || !hubert || !codes_out || T < 2 || T > (1 << 20)) return fail(T2SX_ERR_INVALID, "t2sx_extract_latent: bad arguments");
+    const t2sx_model* m = s->m;
+    CK(cudaSetDevice(m->device));
+    const int C = 768, K = 2 * C, NC = m->n_codes;
+    const int To = (T - 2) / 2 + 1;
+    // one scratch allocation: frames, im2col rows, their dot-type copy, conv output, scores, codes
+    auto al = [](size_t n) { return (n + 255) & ~(size_t)255; };
+    const size_t bx = al((size_t)T * C * 4), bc = al((size_t)To * K * 4), bq = al((size_t)To * K * 2) + al((size_t)To * (K / 32) * 8),
+                 bs = al((size_t)To * C * 4), bsc = al((size_t)To * NC * 4), bk = al((size_t)To * 4);
+    char* mem = nullptr;
+    CK(cudaMalloc(&mem, bx + bc + bq + bs + bsc + bk));
+    float* x = (float*)mem;
+    float* cols = (float*)(mem + bx);
+    char* qbuf = mem + bx + bc;
+    float* ssl = (float*)(mem + bx + bc + bq);
+    float* score = (float*)(mem + bx + bc + bq + bs);
+    int32_t* codes = (int32_t*)(mem + bx + bc + bq + bs + bsc);
+    ActQ a;
+    a.q = (int8_t*)qbuf;
+    a.h = (uint16_t*)qbuf;
+    a.d = (float*)(qbuf + al((size_t)To * K * 2));
+    a.bs = (int32_t*)(qbuf + al((size_t)To * K * 2) + al((size_t)To * (K / 32) * 4));
+    a.f = cols;
+    cudaError_t e = cudaMemcpyAsync(x, hubert, (size_t)T * C * 4, cudaMemcpyHostToDevice, s->st);
+    if (e == cudaSuccess) {
+        im2col_k2s2(To, C, x, cols, s->st);
+        if (m->ssl_w.type != W_F32) quantize_act(m->ssl_w.type, cols, To, K, a, s->st);
+        matmul(m->ssl_w, a, To, m->ssl_b, 0, ssl, s->st);
+        ActQ af;
+        af.f = ssl;   // the codebook is f32: the conv output is read as it is
+        matmul(m->codebook, af, To, nullptr, 0, score, s->st);
+        code_argmax(To, NC, score, m->code_half_norm, codes, s->st);
+        e = cudaGetLastError();
+        if (e == cudaSuccess) e = cudaMemcpyAsync(codes_out, codes, (size_t)To * 4, cudaMemcpyDeviceToHost, s->st);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(s->st);
+    }
+    cudaFree(mem);
+    if (e != cudaSuccess) return fail(T2SX_ERR_CUDA, "t2sx_extract_latent: %s", cudaGetErrorString(e));
     return T2SX_OK;
 }

@@ -929,3 +929,53 @@ void embed_prefill_rows(int T_text, int T_prompt, const int32_t* phones, const i
 }
 
 }  // namespace t2sx
+
+namespace t2sx {
+
+// ============================================================================================
+// extract-latent (sovits_extract_latent_block_forward, src/t2s/block.cpp:140-189)
+// ============================================================================================
+
+// im2col of the width-2, stride-2 Conv1d: cols[t][ic * 2 + k] = x[2t + k][ic] (ggml_im2col order,
+// kernel tap fastest)
+__global__ void k_im2col_k2s2(int To, int C, const float* __restrict__ x, float* __restrict__ cols) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (int64_t)To * C * 2) return;
+    const int64_t t = i / (2 * C);
+    const int j = (int)(i % (2 * C)), ic = j >> 1, k = j & 1;
+    cols[i] = x[(2 * t + k) * C + ic];
+}
+
+// codes[t] = first index c of the max of score[t][c] - half_norm[c] (ggml_sub, ggml_argmax); one
+// warp per frame: lanes scan c = lane, lane + 32, ... keeping their first maximum, then the
+// warp keeps the larger value and, on equal values, the smaller index.
+__global__ void k_code_argmax(int To, int NC, const float* __restrict__ score, const float* __restrict__ half_norm,
+                              int32_t* __restrict__ codes) {
+    const int lane = threadIdx.x & 31;
+    const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    if (t >= To) return;
+    float bv = __int_as_float(0xff800000);
+    int bi = 0x7fffffff;
+    for (int c = lane; c < NC; c += 32) {
+        const float v = __fsub_rn(score[(size_t)t * NC + c], half_norm[c]);
+        if (v > bv || bi == 0x7fffffff) { bv = v; bi = c; }
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+        if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+    }
+    if (lane == 0) codes[t] = bi;
+}
+
+void im2col_k2s2(int To, int C, const float* x, float* cols, cudaStream_t st) {
+    const int64_t n = (int64_t)To * C * 2;
+    if (n > 0) k_im2col_k2s2<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(To, C, x, cols);
+}
+
+void code_argmax(int To, int NC, const float* score, const float* half_norm, int32_t* codes, cudaStream_t st) {
+    if (To > 0) k_code_argmax<<<(To + 3) / 4, 128, 0, st>>>(To, NC, score, half_norm, codes);
+}
+
+}  // namespace t2sx

@@ -147,6 +147,9 @@ void sample_full(int T, const float* logits, int V, const int32_t* row_slot, con
                  int32_t* tok_out, int32_t* greedy_out, cudaStream_t st);
 void advance(int T, const int32_t* row_slot, const int32_t* tok, int32_t* token_in, int32_t* n_pos, uint8_t* seen,
              int V, int32_t* ring, int ring_len, int32_t* ring_step, cudaStream_t st);
+// extract-latent: im2col of the width-2 stride-2 Conv1d (cols [To][2C]) and the nearest-code pick
+void im2col_k2s2(int To, int C, const float* x, float* cols, cudaStream_t st);
+void code_argmax(int To, int NC, const float* score, const float* half_norm, int32_t* codes, cudaStream_t st);
 void gather_rows(int n, const float* src, const int32_t* idx, int ld, float* dst, cudaStream_t st);
 void embed_prefill_rows(int T_text, int T_prompt, const int32_t* phones, const int32_t* sem, const float* bert_proj,
                         const uint16_t* text16, const float* text32, const uint16_t* audio16, const float* audio32,

@@ -61,6 +61,7 @@ SIGNATURES = {
     "t2sx_kvcache_write": (C.c_int, [_P, _I, _I, _I, _P, _P]),
     "t2sx_kvcache_attn_decode": (C.c_int, [_P, _I, _P, _P, _P, _P, _P]),
     "t2sx_kvcache_attn_prefill": (C.c_int, [_P, _I, _P, _P, _P, _P, _P]),
+    "t2sx_extract_latent": (C.c_int, [_P, _P, _I, _P]),
 }
 NOALLOC_MAX_ELEMS = 1 << 21
 
@@ -193,6 +194,14 @@ class Session:
         x = np.empty((T, self.model.d), dtype=np.float32)
         _ck(lib().t2sx_embed_prefill(self.h, _p(phones), _p(bert), phones.size, _p(sem), sem.size, _p(x), 0))
         return x
+
+    def extract_latent(self, hubert: np.ndarray) -> np.ndarray:
+        """Prompt semantic codes of HuBERT frames f32 [T][768] (T >= 2): int32 [(T - 2) // 2 + 1]."""
+        hubert = np.ascontiguousarray(hubert, dtype=np.float32)
+        T = hubert.shape[0]
+        out = np.empty((T - 2) // 2 + 1, dtype=np.int32)
+        _ck(lib().t2sx_extract_latent(self.h, _p(hubert), T, _p(out)))
+        return out
 
     def prefill(self, slots, n_query, t_prompt, x=None, x_dev_ptr: int | None = None):
         slots = np.ascontiguousarray(np.atleast_1d(slots), dtype=np.int32)

@@ -95,6 +95,9 @@ struct t2s_session {
     uint32_t slot_size = 0;
     t2s_sampler_config sampler_cfg;
     int64_t ref_T_prompt = 0;        // prompt audio tokens of the session's reference (as in t2s.h)
+    int64_t ref_T_ref = 0;           // reference text tokens
+    std::vector<int32_t> ref_tokens, ref_codes;   // reference phonemes, prompt codes (from HuBERT)
+    std::vector<float> ref_bert;                  // reference BERT features [T_ref][1024]
     // persistent decode path (t2s.h:477-488): caller fills token_id, reads sampled / greedy
     std::vector<int32_t> token_id;   // {n_batch}, slot order
     std::vector<int32_t> sampled;    // {n_batch}
@@ -159,6 +162,49 @@ inline bool t2s_embed_input(t2s_session & session, const int32_t * phones, const
         return false;
     }
     return true;
+}
+
+// ---- reference prompt (t2s.h:432-467) ----
+// t2s_session_compute_ref_emb: the prompt semantic codes are extracted from the HuBERT frames
+// ({768, T_hub} in ggml order = [T_hub][768]) on the device (Conv1d k=2 s=2 + nearest code), and
+// the reference text is kept; t2s_embed_with_ref then builds the prefill rows
+// [reference text | input text | reference prompt] and sets ref_T_prompt.
+inline bool t2s_session_compute_ref_emb(t2s_session & session, const t2s_model & model, const int32_t * ref_token,
+                                        int64_t T_ref, const float * ref_bert, const float * hubert_data, int64_t T_hub) {
+    T2S_CUDA_ASSERT(session.handle != nullptr && model.handle != nullptr, "session or model not initialised");
+    T2S_CUDA_ASSERT(ref_token != nullptr && ref_bert != nullptr && hubert_data != nullptr, "null input");
+    T2S_CUDA_ASSERT(T_ref > 0 && T_hub > 0, "empty reference");
+    if (T_hub < 2) {
+        std::fprintf(stderr, "t2s_session_compute_ref_emb: at least 2 HuBERT frames are needed\n");
+        return false;
+    }
+    std::vector<int32_t> codes((size_t)((T_hub - 2) / 2 + 1));
+    if (t2sx_extract_latent(session.handle, hubert_data, (int32_t)T_hub, codes.data()) != T2SX_OK) {
+        std::fprintf(stderr, "t2s_session_compute_ref_emb: %s\n", t2sx_last_error());
+        return false;
+    }
+    session.ref_codes = std::move(codes);
+    session.ref_tokens.assign(ref_token, ref_token + T_ref);
+    session.ref_bert.assign(ref_bert, ref_bert + T_ref * 1024);
+    session.ref_T_ref = T_ref;
+    session.ref_T_prompt = (int64_t)session.ref_codes.size();
+    return true;
+}
+inline int64_t t2s_session_get_ref_T_ref(const t2s_session & session) { return session.ref_T_ref; }
+inline int64_t t2s_session_get_ref_T_prompt(const t2s_session & session) { return session.ref_T_prompt; }
+
+// Prefill rows f32 [T_ref + T_in + T_prompt][d_model] (host) for an input text after the reference.
+inline bool t2s_embed_with_ref(t2s_session & session, const t2s_model & model, const int32_t * phones,
+                               const float * bert, int T_in, std::vector<float> & x_out) {
+    T2S_CUDA_ASSERT(session.ref_T_ref > 0, "t2s_session_compute_ref_emb was not called");
+    const int T_text = (int)session.ref_T_ref + T_in;
+    std::vector<int32_t> ph(session.ref_tokens);
+    ph.insert(ph.end(), phones, phones + T_in);
+    std::vector<float> bt(session.ref_bert);
+    bt.insert(bt.end(), bert, bert + (size_t)T_in * 1024);
+    x_out.assign((size_t)(T_text + session.ref_T_prompt) * model.hparams.embedding_dim, 0.0f);
+    return t2s_embed_input(session, ph.data(), bt.data(), T_text, session.ref_codes.data(), (int)session.ref_T_prompt,
+                           x_out.data());
 }
 
 // ---- flex plans (t2s.h:496-582) ----

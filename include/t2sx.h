@@ -90,6 +90,13 @@ T2SX_API int t2sx_session_device_bytes(const t2sx_session* s, uint64_t* bytes);
 T2SX_API int t2sx_embed_prefill(t2sx_session* s, const int32_t* phones, const float* bert, int32_t T_text,
                        const int32_t* sem, int32_t T_prompt, float* x_out, int32_t x_out_on_device);
 
+/* Prompt semantic codes from HuBERT frames (the code extraction of t2s_session_compute_ref_emb,
+ * session.cpp:881-1044; sovits_extract_latent_block_forward, block.cpp:140-189): Conv1d(768, 768,
+ * kernel 2, stride 2) over the frames plus bias, then the nearest codebook entry,
+ * argmax_c(x . E_c - ||E_c||^2 / 2).  hubert: f32 [T][768] (host), T >= 2; codes_out: int32
+ * [(T - 2) / 2 + 1] (host). */
+T2SX_API int t2sx_extract_latent(t2sx_session* s, const float* hubert, int32_t T, int32_t* codes_out);
+
 /* Prefill of n idle slots in one pass (t2s_session_build_flex_graph + t2s_session_flex_advance
  * with prefill-only plans, session.cpp:461-859): slot[i] receives n_query[i] rows of x (rows of
  * all slots concatenated in the given order, f32 [sum n_query][d]; host pointer, or device

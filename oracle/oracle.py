@@ -49,7 +49,8 @@ def lib():
             "orc_embed_prefill": (I, [P, P, P, I, P, I, P]),
             "orc_prefill": (I, [P, I, P, I, I, I, P, P, P]),
             "orc_decode_step": (I, [P, I, P, P, P, F, I, P, P]),
-            "orc_slot_n_pos": (I, [P, I]), "orc_slot_release": (I, [P, I]), "orc_read_kv": (I, [P, I, I, I, P]),
+            "orc_slot_n_pos": (I, [P, I]), "orc_slot_release": (I, [P, I]),
+            "orc_extract_latent": (I, [P, P, I, P]), "orc_read_kv": (I, [P, I, I, I, P]),
             "orc_sample": (I, [P, I, P, P, P, I, F, F, F, I, P, P]),
             "orc_decode_step2": (I, [P, I, P, P, P, P, I, F, F, F, I, P, P, P]),
         }
@@ -124,6 +125,15 @@ class Model:
         rc = lib().orc_embed_prefill(self.h, ptr(phones), ptr(bert), phones.size, ptr(sem), sem.size, ptr(x))
         assert rc == 0
         return x
+
+    def extract_latent(self, hubert: np.ndarray) -> np.ndarray:
+        """Prompt semantic codes of HuBERT frames f32 [T][768]."""
+        hubert = np.ascontiguousarray(hubert, dtype=np.float32)
+        T = hubert.shape[0]
+        out = np.empty((T - 2) // 2 + 1, dtype=np.int32)
+        n = lib().orc_extract_latent(self.h, ptr(hubert), T, ptr(out))
+        assert n == out.size, n
+        return out
 
     def sample(self, logits, seen=None, noise=None, top_k=15, top_p=1.0, temperature=1.0, rep_penalty=1.0,
                eos_mask=True):

@@ -476,6 +476,7 @@ struct Model {
     };
     std::vector<Layer> layers;
     const Tensor *text_emb, *bert_w, *bert_b, *text_alpha, *audio_emb, *audio_alpha, *lm_head;
+    const Tensor *ssl_w = nullptr, *ssl_b = nullptr, *codebook = nullptr;   // extract-latent
 };
 
 struct Rd {
@@ -552,6 +553,8 @@ void* orc_model_load(const char* path) {
     m->text_emb = get("encoder.text_embedding"); m->bert_w = get("encoder.bert_proj_w"); m->bert_b = get("encoder.bert_proj_b");
     m->text_alpha = get("encoder.text_pos_alpha"); m->audio_emb = get("encoder.audio_embedding");
     m->audio_alpha = get("encoder.audio_pos_alpha"); m->lm_head = get("sampler.lm_head_w");
+    m->ssl_w = get("extract_latent.ssl_proj_w"); m->ssl_b = get("extract_latent.ssl_proj_b");
+    m->codebook = get("extract_latent.codebook");
     if (!m->text_emb || !m->bert_w || !m->bert_b || !m->text_alpha || !m->audio_emb || !m->audio_alpha || !m->lm_head) { delete m; return nullptr; }
     return m;
 }
@@ -836,6 +839,45 @@ int orc_read_kv(void* sess, int slot, int layer, int which, uint16_t* out) {
     const auto& src = which ? S->V[(size_t)slot * nl + layer] : S->K[(size_t)slot * nl + layer];
     memcpy(out, src.data(), sizeof(uint16_t) * (size_t)S->n_pos[slot] * d);
     return S->n_pos[slot];
+}
+
+// Extract-latent (sovits_extract_latent_block_forward, src/t2s/block.cpp:140-189): prompt semantic
+// codes from HuBERT frames.  ggml_conv_1d(k = 2, s = 2, p = 0) is im2col in f16 (frames rounded to
+// f16, row j = ic * 2 + k of output frame t is x[2t + k][ic]) times the f16 kernel rows
+// [oc][ic][k]: the F16 matmul with 1536-long rows; then + bias; then score = codebook (F32
+// matmul) - 0.5 * ||E_c||^2 with ||E_c||^2 = sum of the f32 squares in a sequential double sum
+// (ggml_sqr, ggml_sum_rows, ggml_scale, ggml_sub); code = first index of the max (ggml_argmax).
+int orc_extract_latent(void* model, const float* hubert, int T, int32_t* codes_out) {
+    Model* m = (Model*)model;
+    if (!m->ssl_w || !m->ssl_b || !m->codebook || T < 2) return -1;
+    const int C = 768, K = 2 * C, NC = (int)m->codebook->ne[1];
+    if (m->ssl_w->ne[0] != 2 || m->ssl_w->ne[1] != C || m->ssl_w->ne[2] != C || m->codebook->ne[0] != C) return -1;
+    const int To = (T - 2) / 2 + 1;
+    std::vector<float> cols((size_t)To * K), ssl((size_t)To * C), score((size_t)To * NC);
+    for (int t = 0; t < To; ++t)
+        for (int ic = 0; ic < C; ++ic)
+            for (int k = 0; k < 2; ++k) cols[(size_t)t * K + ic * 2 + k] = hubert[(size_t)(2 * t + k) * C + ic];
+    orc_matmul(m->ssl_w->type, m->ssl_w->data, C, K, cols.data(), To, ssl.data());
+    const float* b = fdata(m->ssl_b);
+    for (int t = 0; t < To; ++t) for (int o = 0; o < C; ++o) ssl[(size_t)t * C + o] = ssl[(size_t)t * C + o] + b[o];
+    orc_matmul(m->codebook->type, m->codebook->data, NC, C, ssl.data(), To, score.data());
+    const float* E = fdata(m->codebook);
+    std::vector<float> half_norm(NC);
+    for (int c = 0; c < NC; ++c) {
+        double sum = 0.0;
+        for (int d = 0; d < C; ++d) { const float e = E[(size_t)c * C + d]; sum += (double)(e * e); }
+        half_norm[c] = (float)sum * 0.5f;
+    }
+    for (int t = 0; t < To; ++t) {
+        int best = 0;
+        float bv = score[(size_t)t * NC] - half_norm[0];
+        for (int c = 1; c < NC; ++c) {
+            const float v = score[(size_t)t * NC + c] - half_norm[c];
+            if (v > bv) { bv = v; best = c; }
+        }
+        codes_out[t] = best;
+    }
+    return To;
 }
 
 int orc_embed_prefill(void* model, const int32_t* phones, const float* bert, int T_text, const int32_t* sem, int T_prompt,

@@ -73,6 +73,9 @@ int      orc_decode_step2(void* sess, int n, const int32_t* slots, const int32_t
                           float temperature, float rp, int eos_mask, int32_t* sampled_out,
                           int32_t* greedy_out, float* logits_out);
 int      orc_slot_n_pos(void* sess, int slot);
+// Extract-latent codes of HuBERT frames f32 [T][768]: writes (T - 2) / 2 + 1 codes, returns that
+// count (-1 on a missing tensor or T < 2).
+int      orc_extract_latent(void* model, const float* hubert, int T, int32_t* codes_out);
 // t2s_session_slot_release (session.cpp:224-240): the slot becomes idle (n_pos = 0).
 int      orc_slot_release(void* sess, int slot);
 // Sampler chain (block.cpp:52-348) on n rows of logits f32 [n][vocab]; seen f32 [n][vocab] or

@@ -4,6 +4,10 @@
 // released and prefilled again while the other slots decode), then more decode steps.
 //
 // usage: t2s_decode_loop MODEL.gguf INPUTS.bin N_STEPS [release_bad|decode_idle|plan_idle]
+//        t2s_decode_loop MODEL.gguf INPUTS.bin N_STEPS ref HUBERT.bin
+// ref: prompt 0 is the reference text, HUBERT.bin (int32 T_hub, f32 [T_hub][768]) its audio
+// features; t2s_session_compute_ref_emb extracts the prompt codes, prompt 1's text is embedded
+// after the reference, slot 0 is prefilled and decoded; prints the codes and the tokens.
 // INPUTS.bin: int32 n, then per prompt: int32 T_text, int32 T_prompt, int32 phones[T_text],
 // f32 bert[T_text][1024], int32 sem[T_prompt]; the last prompt refills slot 0 in the mixed plan.
 // Prints one JSON object with the sampled tokens.
@@ -82,11 +86,47 @@ int main(int argc, char** argv) {
     int slot_size = 0;
     for (auto& p : prompts) slot_size = std::max(slot_size, p.T_text + p.T_prompt);
     slot_size += 2 * n_steps + 2;
+    if (!std::strcmp(mode, "ref")) slot_size *= 3;   // reference text + input text + prompt codes
     t2s_session session;
     t2s_sampler_config cfg;
     cfg.repetition_penalty = 1.0f;
     if (!t2s_session_init(session, model, (uint32_t)n, (uint32_t)slot_size, cfg, /*eos_mask=*/true)) return 1;
 
+    if (!std::strcmp(mode, "ref")) {
+        if (argc < 6) return 2;
+        FILE* f = std::fopen(argv[5], "rb");
+        int32_t T_hub = 0;
+        if (!f || std::fread(&T_hub, 4, 1, f) != 1) return 2;
+        std::vector<float> hub((size_t)T_hub * 768);
+        const bool ok = std::fread(hub.data(), 4, hub.size(), f) == hub.size();
+        std::fclose(f);
+        if (!ok) return 2;
+        const Prompt& ref = prompts[0];
+        if (!t2s_session_compute_ref_emb(session, model, ref.phones.data(), ref.T_text, ref.bert.data(), hub.data(),
+                                         T_hub))
+            return 8;
+        if (t2s_session_get_ref_T_ref(session) != ref.T_text) return 9;
+        std::vector<float> x;
+        if (!t2s_embed_with_ref(session, model, prompts[1].phones.data(), prompts[1].bert.data(), prompts[1].T_text, x))
+            return 3;
+        t2s_batch_plan plan;
+        plan.n_query.assign(session.n_batch, 0);
+        plan.n_query[0] = (int)(x.size() / model.hparams.embedding_dim);
+        t2s_flex_graph g = t2s_session_build_flex_graph(session, model, plan);
+        if (!g.built) return 4;
+        std::memcpy(g.x_prefill.data(), x.data(), x.size() * sizeof(float));
+        t2s_session_flex_advance(session, plan, g);
+        if (!t2s_flex_graph_compute(session, g)) return 5;
+        const int tok = g.sampled[0];
+        t2s_flex_graph_free(g);
+        std::printf("{\"codes\": [");
+        for (size_t i = 0; i < session.ref_codes.size(); ++i) std::printf("%s%d", i ? ", " : "", session.ref_codes[i]);
+        std::printf("], \"T_prompt\": %lld, \"tokens\": [", (long long)t2s_session_get_ref_T_prompt(session));
+        std::printf("%d]}\n", tok);
+        t2s_session_free(session);
+        t2s_model_free(model);
+        return 0;
+    }
     if (!std::strcmp(mode, "release_bad")) t2s_session_slot_release(session, n);   // aborts
     if (!std::strcmp(mode, "decode_idle")) {                                        // aborts
         t2s_session_build_decode_graph(session, model);

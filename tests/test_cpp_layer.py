@@ -108,3 +108,36 @@ def test_cpp_illegal_transitions_abort(t2sx_mod, tmp_path, mode, msg):
     r = subprocess.run([exe, path, inp, "2", mode], capture_output=True, text=True, timeout=600)
     assert r.returncode == -signal.SIGABRT, (r.returncode, r.stderr)
     assert msg in r.stderr
+
+
+@pytest.mark.gpu
+def test_cpp_compute_ref_emb_matches_oracle(t2sx_mod, orc, tmp_path):
+    """t2s_session_compute_ref_emb: prompt codes extracted from HuBERT frames on the device, the
+    input text embedded after the reference text (session.cpp:881-1044 flow), first token of the
+    prefill; codes and token equal the oracle's."""
+    exe = _compile(tmp_path)
+    path, prompts, inp = _case(tmp_path)
+    rng = np.random.default_rng(21)
+    T_hub = 57
+    hub = rng.standard_normal((T_hub, 768), dtype=np.float32)
+    hub_path = str(tmp_path / "hubert.bin")
+    with open(hub_path, "wb") as f:
+        np.array([T_hub], np.int32).tofile(f)
+        hub.tofile(f)
+    r = subprocess.run([exe, path, inp, "2", "ref", hub_path], capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, (r.returncode, r.stderr)
+    got = json.loads(r.stdout)
+
+    m = orc.Model(path)
+    codes = m.extract_latent(hub)
+    ref_ph, ref_bert, _ = prompts[0]
+    in_ph, in_bert, _ = prompts[1]
+    ph = np.concatenate([ref_ph, in_ph])
+    bert = np.concatenate([ref_bert, in_bert])
+    n = len(prompts) - 1
+    s = orc.Session(m, n, ph.size + codes.size + 8)
+    tok, _, _ = s.prefill(0, m.embed_prefill(ph, bert, codes), codes.size, eos_mask=True)
+    s.close(); m.close()
+    assert got["codes"] == [int(c) for c in codes]
+    assert got["T_prompt"] == codes.size
+    assert got["tokens"] == [int(tok)]

@@ -337,3 +337,25 @@ def test_kvcache_edge_lengths_and_errors(t2sx_mod, orc):
     with pytest.raises(t2sx_mod.T2SXError):
         c.write(0, 190, k[0, :20], v[0, :20])   # past max_len
     c.close()
+
+
+@pytest.mark.parametrize("fmt", ["q8_0", "f32"])
+def test_extract_latent_bit_exact(t2sx_mod, orc, fmt):
+    """Prompt codes from HuBERT frames (Conv1d k=2 s=2 + nearest codebook entry), GPU against the
+    oracle, for even and odd frame counts from the minimum of 2 frames up."""
+    _need_gpu()
+    import synth
+    path = synth.ensure_gguf(fmt, seed=6, n_layer=2)
+    m_gpu = t2sx_mod.Model(path)
+    s = t2sx_mod.Session(m_gpu, 1, 64)
+    m_orc = orc.Model(path)
+    rng = np.random.default_rng(11)
+    for T in (2, 3, 64, 101, 999):
+        h = rng.standard_normal((T, 768), dtype=np.float32)
+        got = s.extract_latent(h)
+        want = m_orc.extract_latent(h)
+        assert got.shape == ((T - 2) // 2 + 1,)
+        assert np.array_equal(got, want), (fmt, T, int((got != want).sum()))
+    with pytest.raises(t2sx_mod.T2SXError):
+        s.extract_latent(np.zeros((1, 768), np.float32))
+    s.close(); m_gpu.close(); m_orc.close()

@@ -329,3 +329,32 @@ def test_attn_rows_matches_per_head_calls(orc):
                 o = np.empty(32, np.float32)
                 getattr(orc.lib(), fn)(orc.ptr(qq), orc.ptr(kk), orc.ptr(vv), lens[r], orc.ptr(o))
                 assert np.array_equal(o.view(np.uint32), out[r, h * 32:(h + 1) * 32].view(np.uint32)), (r, h)
+
+
+def test_extract_latent_matches_float64(orc):
+    """Oracle extract-latent against an independent float64 restatement of the reference graph
+    (block.cpp:140-189: Conv1d k=2 s=2 on f16-rounded frames and kernel, + bias, nearest code by
+    x.E - ||E||^2/2): scores agree closely and every code with a clear margin is identical."""
+    import synth
+    import gguf
+    path = synth.ensure_gguf("q8_0", seed=5, n_layer=2)
+    r = gguf.GGUFReader(path)
+    t = {x.name: x for x in r.tensors}
+    w = np.asarray(t["extract_latent.ssl_proj_w"].data).astype(np.float64).reshape(768, 768, 2)   # [oc][ic][k]
+    b = np.asarray(t["extract_latent.ssl_proj_b"].data).astype(np.float64)
+    E = np.asarray(t["extract_latent.codebook"].data).astype(np.float64).reshape(-1, 768)
+    rng = np.random.default_rng(4)
+    h = rng.standard_normal((121, 768)).astype(np.float32)
+    hq = h.astype(np.float16).astype(np.float64)
+    To = (121 - 2) // 2 + 1
+    x = np.stack([hq[2 * i:2 * i + 2] for i in range(To)])          # [t][k][ic]
+    ssl = np.einsum("tki,oik->to", x, w) + b
+    score = ssl @ E.T - 0.5 * (E * E).sum(1)
+    want = score.argmax(1)
+    m = orc.Model(path)
+    got = m.extract_latent(h)
+    m.close()
+    top2 = np.sort(score, 1)[:, -2:]
+    clear = (top2[:, 1] - top2[:, 0]) > 1e-3 * np.abs(top2[:, 1]).clip(1)
+    assert clear.sum() > To // 2
+    assert np.array_equal(got[clear], want[clear])
