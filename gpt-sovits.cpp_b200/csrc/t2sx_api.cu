@@ -7,6 +7,7 @@
 
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -885,25 +886,27 @@ static int check_err_flag(t2sx_session* s) {
 static void run_sampler(t2sx_session* s, int T, const float* logits, const int32_t* row_slot, const uint8_t* seen,
                         int32_t* tok, int32_t* greedy);
 
-extern "C" int t2sx_prefill(t2sx_session* s, int32_t n, const int32_t* slots, const int32_t* n_query, const int32_t* t_prompt,
-                            const float* x, int32_t x_on_device, int32_t* tokens_out) {
-    if (!s || n <= 0 || !slots || !n_query || !t_prompt || !x) return fail(T2SX_ERR_INVALID, "t2sx_prefill: bad arguments");
-    std::vector<char> used(s->n_slots, 0);
-    int64_t total = 0;
+// Rows of one prefill pass at most (the prefill work buffers are sized for this many).
+static const int64_t kChunk = 32768;
+
+// Validates the prefill part of a plan (t2s_session_flex_advance checks, session.cpp:461-540).
+static int check_prefill(t2sx_session* s, int32_t n, const int32_t* slots, const int32_t* n_query, const int32_t* t_prompt,
+                         std::vector<char>& used, const char* who) {
     for (int i = 0; i < n; ++i) {
         const int sl = slots[i];
-        if (sl < 0 || sl >= s->n_slots || used[sl]) return fail(T2SX_ERR_INVALID, "t2sx_prefill: bad or repeated slot %d", sl);
+        if (sl < 0 || sl >= s->n_slots || used[sl]) return fail(T2SX_ERR_INVALID, "%s: bad or repeated slot %d", who, sl);
         used[sl] = 1;
-        if (s->n_pos_h[sl] != 0) return fail(T2SX_ERR_STATE, "t2sx_prefill: slot %d is not idle (n_pos=%d)", sl, s->n_pos_h[sl]);
-        if (n_query[i] <= 0 || n_query[i] > s->slot_size) return fail(T2SX_ERR_INVALID, "t2sx_prefill: n_query %d out of range", n_query[i]);
+        if (s->n_pos_h[sl] != 0) return fail(T2SX_ERR_STATE, "%s: slot %d is not idle (n_pos=%d)", who, sl, s->n_pos_h[sl]);
+        if (n_query[i] <= 0 || n_query[i] > s->slot_size) return fail(T2SX_ERR_INVALID, "%s: n_query %d out of range", who, n_query[i]);
         if (t_prompt[i] < 0 || n_query[i] < t_prompt[i])
-            return fail(T2SX_ERR_INVALID, "t2sx_prefill: n_query < ref_T_prompt (audio_offset would be negative)");
-        if ((int64_t)s->free_pages.size() < (int64_t)(i + 1) * s->pages_per_slot) return fail(T2SX_ERR_OOM, "t2sx_prefill: out of KV pages");
-        total += n_query[i];
+            return fail(T2SX_ERR_INVALID, "%s: n_query < ref_T_prompt (audio_offset would be negative)", who);
+        if ((int64_t)s->free_pages.size() < (int64_t)(i + 1) * s->pages_per_slot) return fail(T2SX_ERR_OOM, "%s: out of KV pages", who);
     }
-    const t2sx_model* m = s->m;
-    CK(cudaSetDevice(m->device));
-    // assign pages (a slot holds slot_size positions)
+    return T2SX_OK;
+}
+
+// Gives each slot its pages from the free list (a slot holds slot_size positions).
+static int assign_pages(t2sx_session* s, int32_t n, const int32_t* slots) {
     for (int i = 0; i < n; ++i) {
         const int sl = slots[i];
         for (int p = 0; p < s->pages_per_slot; ++p) {
@@ -916,11 +919,40 @@ extern "C" int t2sx_prefill(t2sx_session* s, int32_t n, const int32_t* slots, co
         CK(cudaMemcpyAsync(s->cap + sl, &cap, 4, cudaMemcpyHostToDevice, s->st));
     }
     CK(cudaStreamSynchronize(s->st));
+    return T2SX_OK;
+}
+
+// Slot state after its prefill: n_pos = n_query, audio_offset = n_query - T_prompt, the first
+// token as the next input and as the only seen token.
+static int finish_prefill(t2sx_session* s, int sl, int nq, int tp, int32_t tok) {
+    s->n_pos_h[sl] = nq;
+    s->audio_off_h[sl] = nq - tp;
+    CK(cudaMemcpyAsync(s->n_pos + sl, &s->n_pos_h[sl], 4, cudaMemcpyHostToDevice, s->st));
+    CK(cudaMemcpyAsync(s->audio_off + sl, &s->audio_off_h[sl], 4, cudaMemcpyHostToDevice, s->st));
+    CK(cudaMemcpyAsync(s->token_in + sl, &tok, 4, cudaMemcpyHostToDevice, s->st));
+    if (s->seen) {
+        CK(cudaMemsetAsync(s->seen + (size_t)sl * s->V, 0, s->V, s->st));
+        const uint8_t one = 1;
+        CK(cudaMemcpyAsync(s->seen + (size_t)sl * s->V + tok, &one, 1, cudaMemcpyHostToDevice, s->st));
+    }
+    return T2SX_OK;
+}
+
+extern "C" int t2sx_prefill(t2sx_session* s, int32_t n, const int32_t* slots, const int32_t* n_query, const int32_t* t_prompt,
+                            const float* x, int32_t x_on_device, int32_t* tokens_out) {
+    if (!s || n <= 0 || !slots || !n_query || !t_prompt || !x) return fail(T2SX_ERR_INVALID, "t2sx_prefill: bad arguments");
+    std::vector<char> used(s->n_slots, 0);
+    {
+        const int rc0 = check_prefill(s, n, slots, n_query, t_prompt, used, "t2sx_prefill");
+        if (rc0) return rc0;
+    }
+    const t2sx_model* m = s->m;
+    CK(cudaSetDevice(m->device));
+    int rc;
+    if ((rc = assign_pages(s, n, slots))) return rc;
     // process slots in chunks of at most kChunk rows
-    const int64_t kChunk = 32768;
     std::vector<int32_t> toks(n, 0);
     int64_t xoff = 0;
-    int rc;
     for (int i0 = 0; i0 < n;) {
         int i1 = i0;
         int64_t rows = 0;
@@ -966,17 +998,7 @@ extern "C" int t2sx_prefill(t2sx_session* s, int32_t n, const int32_t* slots, co
     }
     if ((rc = check_err_flag(s))) return rc;
     for (int i = 0; i < n; ++i) {
-        const int sl = slots[i];
-        s->n_pos_h[sl] = n_query[i];
-        s->audio_off_h[sl] = n_query[i] - t_prompt[i];
-        CK(cudaMemcpyAsync(s->n_pos + sl, &s->n_pos_h[sl], 4, cudaMemcpyHostToDevice, s->st));
-        CK(cudaMemcpyAsync(s->audio_off + sl, &s->audio_off_h[sl], 4, cudaMemcpyHostToDevice, s->st));
-        CK(cudaMemcpyAsync(s->token_in + sl, &toks[i], 4, cudaMemcpyHostToDevice, s->st));
-        if (s->seen) {
-            CK(cudaMemsetAsync(s->seen + (size_t)sl * s->V, 0, s->V, s->st));
-            const uint8_t one = 1;
-            CK(cudaMemcpyAsync(s->seen + (size_t)sl * s->V + toks[i], &one, 1, cudaMemcpyHostToDevice, s->st));
-        }
+        if ((rc = finish_prefill(s, slots[i], n_query[i], t_prompt[i], toks[i]))) return rc;
         if (tokens_out) tokens_out[i] = toks[i];
     }
     CK(cudaStreamSynchronize(s->st));
@@ -1150,6 +1172,98 @@ extern "C" int t2sx_decode_step_host(t2sx_session* s, const int32_t* tokens_in, 
     if (tokens_out) CK(cudaMemcpyAsync(tokens_out, s->dec.tok, T * 4, cudaMemcpyDeviceToHost, s->st));
     CK(cudaStreamSynchronize(s->st));
     CK(cudaEventElapsedTime(&s->last_ms, s->ev0, s->ev1));
+    return T2SX_OK;
+}
+
+// One pass over a mixed plan (the flex graph of session.cpp:461-859 with decode and prefill slots):
+// rows [0, n_dec) are one decode step of the listed slots, then each prefill slot's n_query rows.
+// The layers run once over all rows; the sampler picks a token for every decode row and for the
+// last row of every prefill slot.  Per-row arithmetic is the one of t2sx_decode_step_host and
+// t2sx_prefill, so the tokens equal those of the two separate passes.
+extern "C" int t2sx_flex_step(t2sx_session* s, int32_t n_dec, const int32_t* dec_slots, const int32_t* dec_tokens,
+                              int32_t n_pre, const int32_t* pre_slots, const int32_t* n_query, const int32_t* t_prompt,
+                              const float* x, int32_t* tokens_out) {
+    if (!s || n_dec < 0 || n_pre < 0 || n_dec + n_pre == 0 || (n_dec && (!dec_slots || !dec_tokens)) ||
+        (n_pre && (!pre_slots || !n_query || !t_prompt || !x)))
+        return fail(T2SX_ERR_INVALID, "t2sx_flex_step: bad arguments");
+    const t2sx_model* m = s->m;
+    std::vector<char> used(s->n_slots, 0);
+    int64_t T64 = n_dec;
+    for (int i = 0; i < n_dec; ++i) {
+        const int sl = dec_slots[i];
+        if (sl < 0 || sl >= s->n_slots || used[sl]) return fail(T2SX_ERR_INVALID, "t2sx_flex_step: bad or repeated slot %d", sl);
+        used[sl] = 1;
+        if (s->n_pos_h[sl] == 0) return fail(T2SX_ERR_STATE, "t2sx_flex_step: decode of an idle slot %d", sl);
+        if (s->n_pos_h[sl] + 1 > s->slot_size)
+            return fail(T2SX_ERR_BOUNDS, "t2sx_flex_step: slot %d would exceed slot_size %d", sl, s->slot_size);
+        if (dec_tokens[i] < 0 || dec_tokens[i] >= m->audio_rows) return fail(T2SX_ERR_INVALID, "token id %d out of range", dec_tokens[i]);
+    }
+    int rc;
+    if ((rc = check_prefill(s, n_pre, pre_slots, n_query, t_prompt, used, "t2sx_flex_step"))) return rc;
+    for (int i = 0; i < n_pre; ++i) T64 += n_query[i];
+    if (T64 > kChunk) return fail(T2SX_ERR_INVALID, "t2sx_flex_step: %lld rows in one pass (at most %lld)", (long long)T64, (long long)kChunk);
+    const int T = (int)T64, ns = n_dec + n_pre;
+    CK(cudaSetDevice(m->device));
+    {
+        const cudaError_t stale = cudaGetLastError();
+        if (stale != cudaSuccess) return fail(T2SX_ERR_CUDA, "pending CUDA error before the pass: %s", cudaGetErrorString(stale));
+    }
+    if ((rc = assign_pages(s, n_pre, pre_slots))) return rc;
+    if ((rc = work_alloc(s->pre, T, s->V, s->ff))) return rc;
+    Work& w = s->pre;
+    std::vector<int32_t> rs(T), rp(T), rl(T), last(ns), samp(ns);
+    int r = 0;
+    for (int i = 0; i < n_dec; ++i, ++r) {
+        rs[r] = dec_slots[i]; rp[r] = s->n_pos_h[dec_slots[i]]; rl[r] = rp[r] + 1;
+        last[i] = r; samp[i] = dec_slots[i];
+    }
+    for (int i = 0; i < n_pre; ++i) {
+        const int T_text = n_query[i] - t_prompt[i];
+        for (int j = 0; j < n_query[i]; ++j, ++r) {
+            rs[r] = pre_slots[i]; rp[r] = j; rl[r] = (j < T_text) ? T_text : (j + 1);
+        }
+        last[n_dec + i] = r - 1; samp[n_dec + i] = pre_slots[i];
+    }
+    CK(cudaMemcpyAsync(w.row_slot, rs.data(), T * 4, cudaMemcpyHostToDevice, s->st));
+    CK(cudaMemcpyAsync(w.row_pos, rp.data(), T * 4, cudaMemcpyHostToDevice, s->st));
+    CK(cudaMemcpyAsync(w.row_L, rl.data(), T * 4, cudaMemcpyHostToDevice, s->st));
+    CK(cudaMemcpyAsync(w.lastrow, last.data(), ns * 4, cudaMemcpyHostToDevice, s->st));
+    if (n_pre) CK(cudaMemcpyAsync(w.x + (size_t)n_dec * kD, x, (size_t)(T - n_dec) * kD * 4, cudaMemcpyHostToDevice, s->st));
+    if (n_dec) {
+        CK(cudaMemcpyAsync(s->scratch_i, dec_tokens, n_dec * 4, cudaMemcpyHostToDevice, s->st));
+        k_scatter_tokens<<<(n_dec + 255) / 256, 256, 0, s->st>>>(n_dec, w.row_slot, s->scratch_i, s->token_in);
+        embed_decode(n_dec, w.row_slot, s->token_in, s->n_pos, s->audio_off, m->audio16, m->audio32, m->audio_rows, s->pe,
+                     s->slot_size, m->alpha_audio, rows_of(s, w), w.x, m->layers[0].qkv.type, act_of(w), s->st);
+    }
+    {
+        ActQ a0 = act_of(w);
+        quantize_act(m->layers[0].qkv.type, w.x, T, kD, a0, s->st);
+    }
+    run_layers(s, w, T, false, -1);
+    gather_rows(ns, w.x, w.lastrow, kD, w.xl, s->st);
+    ActQ a = act_for(w, w.xl);
+    quantize_act(m->lm_head.type, w.xl, ns, kD, a, s->st);
+    matmul(m->lm_head, a, ns, nullptr, 0, w.logits, s->st);
+    // the prefill rows sample with an empty seen set, as in t2sx_prefill
+    for (int i = 0; s->seen && i < n_pre; ++i) CK(cudaMemsetAsync(s->seen + (size_t)pre_slots[i] * s->V, 0, s->V, s->st));
+    CK(cudaMemcpyAsync(w.row_slot, samp.data(), ns * 4, cudaMemcpyHostToDevice, s->st));
+    run_sampler(s, ns, w.logits, w.row_slot, s->seen, w.tok, w.greedy);
+    // decode rows: token_in, n_pos + 1 and the seen set, as in the decode step
+    if (n_dec) advance(n_dec, w.row_slot, w.tok, s->token_in, s->n_pos, s->seen, s->V, nullptr, 0, s->ring_step, s->st);
+    CK(cudaGetLastError());
+    std::vector<int32_t> toks(ns, 0);
+    CK(cudaMemcpyAsync(toks.data(), w.tok, ns * 4, cudaMemcpyDeviceToHost, s->st));
+    CK(cudaStreamSynchronize(s->st));
+    s->last_rows = ns;
+    s->last_logits = w.logits;
+    s->last_greedy = w.greedy;
+    if ((rc = check_err_flag(s))) return rc;
+    for (int i = 0; i < n_dec; ++i) s->n_pos_h[dec_slots[i]] += 1;
+    for (int i = 0; i < n_pre; ++i)
+        if ((rc = finish_prefill(s, pre_slots[i], n_query[i], t_prompt[i], toks[n_dec + i]))) return rc;
+    CK(cudaStreamSynchronize(s->st));
+    if (tokens_out) std::copy(toks.begin(), toks.end(), tokens_out);
+    if (n_pre) rebuild_active(s);
     return T2SX_OK;
 }
 

@@ -39,6 +39,7 @@ SIGNATURES = {
     "t2sx_session_device_bytes": (C.c_int, [_P, _P]),
     "t2sx_embed_prefill": (C.c_int, [_P, _P, _P, _I, _P, _I, _P, _I]),
     "t2sx_prefill": (C.c_int, [_P, _I, _P, _P, _P, _P, _I, _P]),
+    "t2sx_flex_step": (C.c_int, [_P, _I, _P, _P, _I, _P, _P, _P, _P, _P]),
     "t2sx_decode": (C.c_int, [_P, _I, _P]),
     "t2sx_decode_async": (C.c_int, [_P, _I]),
     "t2sx_synchronize": (C.c_int, [_P]),
@@ -214,6 +215,27 @@ class Session:
             x = np.ascontiguousarray(x, dtype=np.float32)
             assert x.shape == (int(nq.sum()), self.model.d)
             _ck(lib().t2sx_prefill(self.h, slots.size, _p(slots), _p(nq), _p(tp), _p(x), 0, _p(toks)))
+        return toks
+
+    def flex_step(self, dec_slots, dec_tokens, pre_slots=(), n_query=(), t_prompt=(), x=None):
+        """One pass over a mixed plan: a decode step of dec_slots (input tokens dec_tokens) and the
+        prefill of pre_slots (rows x f32 [sum n_query][d]); returns the decode slots' tokens then the
+        prefill slots' first tokens."""
+        ds = np.ascontiguousarray(np.atleast_1d(dec_slots), dtype=np.int32)
+        dt = np.ascontiguousarray(np.atleast_1d(dec_tokens), dtype=np.int32)
+        ps = np.ascontiguousarray(np.atleast_1d(pre_slots), dtype=np.int32)
+        nq = np.ascontiguousarray(np.atleast_1d(n_query), dtype=np.int32)
+        tp = np.ascontiguousarray(np.atleast_1d(t_prompt), dtype=np.int32)
+        assert ds.size == dt.size and ps.size == nq.size == tp.size
+        xp = None
+        if ps.size:
+            x = np.ascontiguousarray(x, dtype=np.float32)
+            assert x.shape == (int(nq.sum()), self.model.d)
+            xp = _p(x)
+        toks = np.zeros(ds.size + ps.size, dtype=np.int32)
+        _ck(lib().t2sx_flex_step(self.h, ds.size, _p(ds) if ds.size else None, _p(dt) if dt.size else None, ps.size,
+                                 _p(ps) if ps.size else None, _p(nq) if ps.size else None,
+                                 _p(tp) if ps.size else None, xp, _p(toks)))
         return toks
 
     # ---- decode ------------------------------------------------------------------------------

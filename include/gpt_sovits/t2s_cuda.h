@@ -293,7 +293,28 @@ inline bool t2s_flex_graph_compute(t2s_session & session, t2s_flex_graph & graph
     graph.advanced = false;
     std::vector<std::pair<int, int>> out;   // (slot, token) / greedy
     std::vector<std::pair<int, int>> outg;
-    if (graph.n_decode > 0) {
+    int64_t rows = graph.n_decode;
+    for (int v : graph.prefill_nq) rows += v;
+    if (rows <= 32768) {   // the whole plan in one pass
+        const int nd = graph.n_decode, np = (int)graph.prefill_slots.size();
+        std::vector<int32_t> ds(graph.decode_slots.begin(), graph.decode_slots.begin() + nd);
+        std::vector<int32_t> dt(graph.decode_token_ids.begin(), graph.decode_token_ids.begin() + nd);
+        std::vector<int32_t> ps(graph.prefill_slots.begin(), graph.prefill_slots.end());
+        std::vector<int32_t> nq(graph.prefill_nq.begin(), graph.prefill_nq.end()), tp(np, (int32_t)session.ref_T_prompt);
+        std::vector<int32_t> tok(nd + np), gr(nd + np);
+        if (t2sx_flex_step(session.handle, nd, ds.data(), dt.data(), np, ps.data(), nq.data(), tp.data(),
+                           np ? graph.x_prefill.data() : nullptr, tok.data()) != T2SX_OK) {
+            std::fprintf(stderr, "t2s_flex_graph_compute: %s\n", t2sx_last_error());
+            return false;
+        }
+        int32_t nr = 0;
+        t2sx_read_greedy(session.handle, gr.data(), nd + np, &nr);
+        for (int k = 0; k < nd + np; ++k) {
+            const int sl = k < nd ? ds[k] : ps[k - nd];
+            out.push_back({sl, tok[k]});
+            outg.push_back({sl, gr[k]});
+        }
+    } else if (graph.n_decode > 0) {
         std::vector<int32_t> tok(graph.n_decode), gr(graph.n_decode);
         if (t2sx_decode_step_host(session.handle, graph.decode_token_ids.data(), tok.data()) != T2SX_OK) {
             std::fprintf(stderr, "t2s_flex_graph_compute (decode): %s\n", t2sx_last_error());
@@ -303,7 +324,7 @@ inline bool t2s_flex_graph_compute(t2s_session & session, t2s_flex_graph & graph
         t2sx_read_greedy(session.handle, gr.data(), graph.n_decode, &rows);
         for (int k = 0; k < graph.n_decode; ++k) { out.push_back({graph.decode_slots[k], tok[k]}); outg.push_back({graph.decode_slots[k], gr[k]}); }
     }
-    if (!graph.prefill_slots.empty()) {
+    if (rows > 32768 && !graph.prefill_slots.empty()) {
         const int n = (int)graph.prefill_slots.size();
         std::vector<int32_t> slots(graph.prefill_slots.begin(), graph.prefill_slots.end());
         std::vector<int32_t> nq(graph.prefill_nq.begin(), graph.prefill_nq.end()), tp(n, (int32_t)session.ref_T_prompt);

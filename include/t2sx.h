@@ -127,6 +127,19 @@ T2SX_API int t2sx_active_slots(t2sx_session* s, int32_t* slots, int32_t* n);
 /* Logits f32 [rows][vocab] of the last pass (decode: one row per active slot; prefill: one
  * row per prefilled slot), before the repetition penalty. */
 T2SX_API int t2sx_read_logits(t2sx_session* s, float* out, int32_t max_rows, int32_t* rows);
+/* One pass over a mixed plan (t2s_session_build_flex_graph + t2s_session_flex_advance +
+ * graph compute with decode and prefill slots, session.cpp:461-859): one decode step of the
+ * n_dec active slots dec_slots[] with input tokens dec_tokens[], and the prefill of the n_pre idle
+ * slots pre_slots[] (n_query, t_prompt and x as in t2sx_prefill; x is host f32
+ * [sum n_query][d]), through the layers once.  tokens_out (host, may be NULL) receives n_dec +
+ * n_pre tokens: the decode slots' in argument order, then the prefill slots' first tokens.  Noise
+ * rows (t2sx_set_exp_noise) follow the same order.  The tokens equal those of
+ * t2sx_decode_step_host and t2sx_prefill run separately.  At most 32768 rows per pass; an idle
+ * decode slot, a busy prefill slot or a repeated slot -> T2SX_ERR_STATE / T2SX_ERR_INVALID before
+ * any device work. */
+T2SX_API int t2sx_flex_step(t2sx_session* s, int32_t n_dec, const int32_t* dec_slots, const int32_t* dec_tokens,
+                            int32_t n_pre, const int32_t* pre_slots, const int32_t* n_query, const int32_t* t_prompt,
+                            const float* x, int32_t* tokens_out);
 /* Cached f16 K (which=0) or V (which=1) of one slot and layer: out [n_pos][d] (uint16 bits). */
 T2SX_API int t2sx_read_kv(t2sx_session* s, int32_t slot, int32_t layer, int32_t which, uint16_t* out);
 /* Seen-token mask used by the repetition penalty (t2s_session_get_seen_mask, t2s.h:487): set

@@ -359,3 +359,98 @@ def test_extract_latent_bit_exact(t2sx_mod, orc, fmt):
     with pytest.raises(t2sx_mod.T2SXError):
         s.extract_latent(np.zeros((1, 768), np.float32))
     s.close(); m_gpu.close(); m_orc.close()
+
+
+@pytest.mark.parametrize("rp", [1.0, 1.35])
+def test_flex_step_mixed_plan_bit_exact(t2sx_mod, orc, rp):
+    """t2sx_flex_step (session.cpp:461-859 with decode and prefill slots in one plan): a decode of a
+    subset of the active slots, then a released slot prefilled in the same pass as the others'
+    decode step, then ordinary decode steps.  Tokens, logits and the refilled slot's KV equal the
+    oracle's separate decode and prefill; the repetition penalty applies to the decode rows only."""
+    _need_gpu()
+    import synth
+    path = synth.ensure_gguf("q4_k", 7, n_layer=2)
+    m_gpu, m_orc = t2sx_mod.Model(path), orc.Model(path)
+    lengths = [(30, 20, 41), (12, 40, 42), (50, 5, 43)]
+    refill = (25, 25, 44)
+    n, cap, V = len(lengths), 160, m_orc.vocab
+    s_gpu = t2sx_mod.Session(m_gpu, n, cap, eos_mask=True, repetition_penalty=rp)
+    s_orc = orc.Session(m_orc, n, cap)
+    seen = np.zeros((n, V), dtype=np.float32)
+    xs, nq, tps, cur = [], [], [], np.zeros(n, np.int32)
+    for i, (tt, tp, seed) in enumerate(lengths):
+        ph, bert, sem = synth.session_inputs(seed, tt, tp)
+        x = m_orc.embed_prefill(ph, bert, sem)
+        xs.append(x); nq.append(tt + tp); tps.append(tp)
+        cur[i] = s_orc.prefill(i, x, tp, eos_mask=True)[0]
+    assert np.array_equal(s_gpu.prefill(np.arange(n), nq, tps, np.concatenate(xs)), cur)
+    seen[np.arange(n), cur] = 1.0
+
+    def orc_decode(slots, toks, want_logits=False):
+        slots = np.asarray(slots, np.int32)
+        out, lg = s_orc.decode(slots, toks, seen=seen[slots] if rp != 1.0 else None, rep_penalty=rp,
+                               eos_mask=True, want_logits=want_logits)
+        seen[slots, out] = 1.0
+        return out, lg
+
+    for _ in range(3):
+        got = s_gpu.decode_step_host(cur)
+        cur, _ = orc_decode(np.arange(n), cur)
+        assert np.array_equal(got, cur)
+    # decode of a subset (slot 1 waits)
+    got = s_gpu.flex_step([2, 0], cur[[2, 0]])
+    ref, lg = orc_decode([2, 0], cur[[2, 0]], want_logits=True)
+    assert np.array_equal(got, ref)
+    assert same_bits(s_gpu.read_logits(2), lg)
+    cur[[2, 0]] = ref
+    assert s_gpu.slot_n_pos(1) == nq[1] + 3 and s_gpu.slot_n_pos(0) == nq[0] + 4
+    # slot 1 released and prefilled again while slots 0 and 2 decode, in one pass
+    s_gpu.slot_release(1); s_orc.release(1)
+    tt, tp, seed = refill
+    ph, bert, sem = synth.session_inputs(seed, tt, tp)
+    x = m_orc.embed_prefill(ph, bert, sem)
+    got = s_gpu.flex_step([0, 2], cur[[0, 2]], [1], [tt + tp], [tp], x)
+    lg_gpu = s_gpu.read_logits(3)
+    ref, lg = orc_decode([0, 2], cur[[0, 2]], want_logits=True)
+    tok1, lg1, _ = s_orc.prefill(1, x, tp, eos_mask=True, want_logits=True)
+    assert list(got) == list(ref) + [tok1]
+    assert same_bits(lg_gpu[:2], lg) and same_bits(lg_gpu[2], lg1)
+    assert s_gpu.slot_n_pos(1) == tt + tp and s_gpu.slot_audio_offset(1) == tt
+    for which in (0, 1):
+        assert np.array_equal(s_gpu.read_kv(1, m_orc.n_layer - 1, which), s_orc.read_kv(1, m_orc.n_layer - 1, which))
+    cur[[0, 2]] = ref
+    cur[1] = tok1
+    seen[1] = 0.0
+    seen[1, tok1] = 1.0
+    for _ in range(4):
+        got = s_gpu.decode_step_host(cur)
+        cur, _ = orc_decode(np.arange(n), cur)
+        assert np.array_equal(got, cur)
+    s_gpu.close(); s_orc.close(); m_gpu.close(); m_orc.close()
+
+
+def test_flex_step_errors(t2sx_mod):
+    """Plans the reference rejects (session.cpp:461-540) fail before any device work."""
+    _need_gpu()
+    import synth
+    T = t2sx_mod
+    path = synth.ensure_gguf("q8_0", 7, n_layer=2)
+    m = T.Model(path)
+    s = T.Session(m, 3, 64, eos_mask=True)
+    x = np.random.default_rng(0).standard_normal((10, 512), dtype=np.float32)
+    s.prefill([0], [10], [4], x)
+    for args, code in [(([1], [5]), T.ERR_STATE),                          # decode of an idle slot
+                       (([0], [5], [0], [10], [4], x), T.ERR_INVALID),     # slot both decoded and prefilled
+                       (([0], [5], [1], [10], [4], x), None),              # legal
+                       (([0], [5], [1], [10], [4], x), T.ERR_STATE),       # slot 1 is busy now
+                       (([0], [5], [2], [3], [4], x[:3]), T.ERR_INVALID),  # n_query < ref_T_prompt
+                       (([0, 0], [5, 5]), T.ERR_INVALID),                  # repeated slot
+                       (([0], [m.vocab + 5]), T.ERR_INVALID)]:             # token out of range
+        if code is None:
+            s.flex_step(*args)
+            continue
+        with pytest.raises(T.T2SXError) as e:
+            s.flex_step(*args)
+        assert e.value.code == code, args
+    assert s.slot_n_pos(0) == 11 and s.slot_n_pos(1) == 10 and s.slot_n_pos(2) == 0
+    s.close(); m.close()
