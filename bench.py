@@ -490,6 +490,37 @@ def run_attention_sweep(args):
                       "unique_kv_bytes": n * T * 2048,
                       "note": "32 position lanes per (query, head) with the online softmax: CUDA cores, not tensor cores"}))
     cache.close()
+    # decode rows of one fixed context each: time against context gives the per-launch cost that
+    # does not scale with the prefix (row start-up, merge, output)
+    nf = 2048
+    ctxs = [int(c) for c in args.attn_ctx.split(",") if c]
+    if ctxs:
+        cmax = max(ctxs)
+        cache = t2sx.KVCache(nf, cmax)
+        k = (rng.standard_normal((cmax, 16, 32), dtype=np.float32) * scale).astype(np.float16).view(np.uint16)
+        v = (rng.standard_normal((cmax, 16, 32), dtype=np.float32) * scale).astype(np.float16).view(np.uint16)
+        for s_ in range(nf):
+            cache.write(s_, 0, k, v)
+        fseqs = np.arange(nf, dtype=np.int32)
+        fq = torch.randn((nf, 512), generator=torch.Generator().manual_seed(5)).to(torch.float16).cuda()
+        fout = torch.empty((nf, 512), dtype=torch.float32, device="cuda")
+        for c in ctxs:
+            flens = np.full(nf, c, dtype=np.int32)
+            ms = timed(lambda: cache.attn_decode(fseqs, flens, fq.data_ptr(), fout.data_ptr(), stream=stream.cuda_stream))
+            byts = float(nf * c * 2048 + nf * (512 * 2 + 512 * 4))
+            gbs = byts / (ms * 1e-3) / 1e9
+            print(json.dumps({"sweep": "attention", "case": "decode_fixed", "sequences": nf, "prefix": c,
+                              "us": round(ms * 1e3, 2), "bytes": int(byts), "achieved_gbs": round(gbs, 1),
+                              "frac": round(gbs / peaks["hbm_gbs"], 4), "peak_kind": peak_kind}))
+        if cmax >= 1500:   # the same rows with ragged prefixes (uniform in [200, 1500])
+            flens = rng.integers(200, 1501, size=nf).astype(np.int32)
+            ms = timed(lambda: cache.attn_decode(fseqs, flens, fq.data_ptr(), fout.data_ptr(), stream=stream.cuda_stream))
+            byts = float(flens.astype(np.int64).sum() * 2048 + nf * (512 * 2 + 512 * 4))
+            gbs = byts / (ms * 1e-3) / 1e9
+            print(json.dumps({"sweep": "attention", "case": "decode_ragged", "sequences": nf, "prefix": "uniform [200,1500]",
+                              "us": round(ms * 1e3, 2), "bytes": int(byts), "achieved_gbs": round(gbs, 1),
+                              "frac": round(gbs / peaks["hbm_gbs"], 4), "peak_kind": peak_kind}))
+        cache.close()
 
 
 def main():
@@ -508,6 +539,8 @@ def main():
                     help="isolated kernel sweep instead of the decode workload (--steps = timed iterations)")
     ap.add_argument("--formats", default="q8_0,q4_0,q4_k,f16")
     ap.add_argument("--rows", default="1,8,16,64,256,2048")
+    ap.add_argument("--attn-ctx", default="",
+                    help="attention sweep: also time 2048 decode rows at each of these fixed prefixes")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")

@@ -488,6 +488,75 @@ void embed_decode(int T, const int32_t* row_slot, const int32_t* token_in, const
                                                     pe_rows, alpha, rows, x, qtype, qo);
 }
 
+// One round of the lane merge with partner lane ^ OFF: in holds 2N values (dims whose bits
+// above OFF match this lane), out receives the N whose bit OFF matches; m and l merge in full.
+template <int OFF, int N>
+__device__ __forceinline__ void attn_merge_round(AttnState& st, int lane, const float* in, float* out) {
+    const float mB = __shfl_xor_sync(0xffffffffu, st.m, OFF);
+    const float lB = __shfl_xor_sync(0xffffffffu, st.l, OFF);
+    float M, a, b, l;
+    bool empty;
+    st_merge_scalars(st.m, st.l, mB, lB, M, a, b, l, empty);
+    const bool hi = (lane & OFF) != 0;
+#pragma unroll
+    for (int u = 0; u < N; ++u) {
+        const float keep = hi ? in[N + u] : in[u];
+        const float send = hi ? in[u] : in[N + u];
+        const float oB = __shfl_xor_sync(0xffffffffu, send, OFF);
+        out[u] = empty ? 0.0f : __fadd_rn(__fmul_rn(keep, a), __fmul_rn(oB, b));
+    }
+    st.m = empty ? __int_as_float(0xff800000) : M;
+    st.l = l;
+}
+
+// Merge of a warp's 32 position lanes in xor-butterfly order (partners 16, 8, 4, 2, 1; the merge
+// is symmetric, so every lane ends with the same state and lane d owns output dim d), then the
+// output row in the out-projection's dot type (a Q8_0 block is one head, a Q8_K block the CTA's
+// eight heads: every warp of the CTA must call this for the same row), or f32 when qtype < 0.
+template <int HPC>
+__device__ __forceinline__ void attn_finish(AttnState& st, int r, int hg, int warp, int lane, float* __restrict__ out,
+                                            int qtype, const ActQ& qo, AbsMax* s_am, float* s_is) {
+    // The butterfly runs as a reduce-scatter: at the round with partner lane ^ off a lane keeps the
+    // half of its dims whose bit `off` equals its own and receives the partner's values for them,
+    // so after the five rounds lane d holds dim d.  Every kept value is the one the full butterfly
+    // computes at that lane (the partner holds the same dims, and m, l still follow the full
+    // butterfly), with 31 exchanged values per lane instead of 160.
+    float o16[16], o8[8], o4[4], o2[2], mine;
+    attn_merge_round<16, 16>(st, lane, st.o, o16);
+    attn_merge_round<8, 8>(st, lane, o16, o8);
+    attn_merge_round<4, 4>(st, lane, o8, o4);
+    attn_merge_round<2, 2>(st, lane, o4, o2);
+    attn_merge_round<1, 1>(st, lane, o2, &mine);
+    const float val = __fmul_rn(mine, __fdiv_rn(1.0f, st.l));
+    const int h = hg * HPC + warp;
+    const size_t e = (size_t)r * kD + h * kHeadDim + lane;
+    if (qtype == W_Q8_0 || qtype == W_Q4_0) {
+        qo.q[e] = (int8_t)q8_0_lane(val, qo.d + (size_t)r * (kD / 32) + h, lane);
+    } else if (qtype == W_Q4_K && HPC == 8) {
+        AbsMax am{0.0f, 0.0f, 0x7fffffff};
+        absmax_take(am, val, warp * kHeadDim + lane);
+        am = absmax_warp(am);
+        if (lane == 0) s_am[warp] = am;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            AbsMax all = s_am[0];
+            for (int w = 1; w < 8; ++w) absmax_merge(all, s_am[w]);
+            const float iscale = q8k_iscale(all);
+            *s_is = iscale;
+            qo.d[(size_t)r * (kD / 256) + hg] = q8k_d(iscale);
+        }
+        __syncthreads();
+        const int qv = q8k_q(*s_is, val);
+        qo.q[e] = (int8_t)qv;
+        const int sum = warp_sum_i(qv);
+        if (lane == 0) qo.bs[(size_t)r * (kD / 32) + h] = sum;
+    } else if (qtype == W_F16) {
+        qo.h[e] = f2h(val);
+    } else {
+        out[e] = val;
+    }
+}
+
 // Decode attention: one warp per (row, head), eight heads of a row per CTA.  Position lane
 // t = lane folds positions t, t+32, ... with the online update; the 32 lanes merge in the
 // order of an xor butterfly (partners 16, 8, 4, 2, 1).  The merge is symmetric, so every lane
@@ -570,51 +639,7 @@ __global__ void __launch_bounds__(32 * HPC) k_attn_decode(const uint16_t* __rest
         }
         cp_wait<0>();
     }
-#pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) {
-        const float mB = __shfl_xor_sync(0xffffffffu, st.m, off);
-        const float lB = __shfl_xor_sync(0xffffffffu, st.l, off);
-        float M, a, b, l;
-        bool empty;
-        st_merge_scalars(st.m, st.l, mB, lB, M, a, b, l, empty);
-#pragma unroll
-        for (int d = 0; d < kHeadDim; ++d) {
-            const float oB = __shfl_xor_sync(0xffffffffu, st.o[d], off);
-            st.o[d] = empty ? 0.0f : __fadd_rn(__fmul_rn(st.o[d], a), __fmul_rn(oB, b));
-        }
-        st.m = empty ? __int_as_float(0xff800000) : M;
-        st.l = l;
-    }
-    float mine = 0.0f;
-#pragma unroll
-    for (int d = 0; d < kHeadDim; ++d) if (d == lane) mine = st.o[d];
-    const float val = __fmul_rn(mine, __fdiv_rn(1.0f, st.l));
-    const size_t e = (size_t)r * kD + h * kHeadDim + lane;
-    if (qtype == W_Q8_0 || qtype == W_Q4_0) {
-        qo.q[e] = (int8_t)q8_0_lane(val, qo.d + (size_t)r * (kD / 32) + h, lane);
-    } else if (qtype == W_Q4_K && HPC == 8) {
-        AbsMax am{0.0f, 0.0f, 0x7fffffff};
-        absmax_take(am, val, warp * kHeadDim + lane);
-        am = absmax_warp(am);
-        if (lane == 0) s_am[warp] = am;
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            AbsMax all = s_am[0];
-            for (int w = 1; w < 8; ++w) absmax_merge(all, s_am[w]);
-            const float iscale = q8k_iscale(all);
-            s_is = iscale;
-            qo.d[(size_t)r * (kD / 256) + blockIdx.y] = q8k_d(iscale);
-        }
-        __syncthreads();
-        const int qv = q8k_q(s_is, val);
-        qo.q[e] = (int8_t)qv;
-        const int sum = warp_sum_i(qv);
-        if (lane == 0) qo.bs[(size_t)r * (kD / 32) + h] = sum;
-    } else if (qtype == W_F16) {
-        qo.h[e] = f2h(val);
-    } else {
-        out[e] = val;
-    }
+    attn_finish<HPC>(st, r, blockIdx.y, warp, lane, out, qtype, qo, s_am, &s_is);
 }
 
 // Dynamic shared memory of the small-batch (PIPE) attention variant: the cp.async ring plus the

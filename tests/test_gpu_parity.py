@@ -339,6 +339,34 @@ def test_kvcache_edge_lengths_and_errors(t2sx_mod, orc):
     c.close()
 
 
+def test_kvcache_long_prefixes_many_rows(t2sx_mod, orc):
+    """Many rows (the persistent kernel) with prefixes past 32 pages (2048 positions), where the
+    page numbers held one per lane are reloaded: lengths at and around 2048 and 4096."""
+    _need_gpu()
+    n_seqs, max_len = 4, 4500
+    rng, k, v = _kv_case(n_seqs, max_len, seed=33)
+    c = _kv_fill(t2sx_mod, k, v, np.full(n_seqs, max_len), chunks=3)
+    fixed = [2047, 2048, 2049, 2112, 4095, 4096, 4097, 4500, 1, 64, 65]
+    lens = np.concatenate([fixed, rng.integers(1, max_len + 1, size=80 - len(fixed))]).astype(np.int32)
+    seqs = rng.integers(0, n_seqs, size=lens.size).astype(np.int32)
+    q16 = rng.standard_normal((lens.size, 512), dtype=np.float32).astype(np.float16).view(np.uint16)
+    got = _kv_run(c, 0, seqs, lens, q16)
+    ref = orc.attn_rows(seqs, lens, q16, k, v)
+    c.close()
+    assert same_bits(got, ref), f"{int((got != ref).sum())} mismatches"
+
+
+def test_decode_many_sessions_q4_k_bit_exact(t2sx_mod, orc):
+    """72 sessions of a Q4_K model: the many-row decode path (tcgen05 matmuls, persistent
+    attention with the Q8_K output) against the oracle for 8 steps."""
+    _need_gpu()
+    import synth
+    path = synth.ensure_gguf("q4_k", 7, n_layer=2)
+    rng = np.random.default_rng(50)
+    lengths = [(int(rng.integers(5, 40)), int(rng.integers(3, 30)), 500 + i) for i in range(72)]
+    _run_pair(t2sx_mod, orc, path, lengths, steps=8)
+
+
 @pytest.mark.parametrize("fmt", ["q8_0", "f32"])
 def test_extract_latent_bit_exact(t2sx_mod, orc, fmt):
     """Prompt codes from HuBERT frames (Conv1d k=2 s=2 + nearest codebook entry), GPU against the
