@@ -35,6 +35,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <cstring>
 #include <mutex>
 
 namespace t2sx {
@@ -114,6 +115,20 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
 }
 
 // barrier of the 8 epilogue warps only (named barrier 1)
+// tensor store of one box from shared memory (x, y >= 0; x * element size a multiple of 16 bytes;
+// the parts of the box outside the tensor are not written), tracked per thread
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, int x, int y, const void* ssrc) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];\n" ::"l"((uint64_t)map), "r"(x),
+                 "r"(y), "r"(smem_u32(ssrc))
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;\n" ::: "memory"); }
+// this thread's tensor stores have read their shared-memory source
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;\n" ::: "memory"); }
+// this thread's tensor stores have completed
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;\n" ::: "memory"); }
+// shared-memory writes of this thread become visible to the tensor-store (async) proxy
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory"); }
 __device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, %0;\n" ::"n"(32 * EPI_WARPS) : "memory"); }
 // the same barrier, returning the OR of v over the 8 warps (one decision for all of them)
 __device__ __forceinline__ bool epi_sync_or(bool v) {
@@ -177,6 +192,12 @@ __device__ __forceinline__ void tmem_wait_ld_regs(int (&v)[NR]) {
 #pragma unroll
     for (int i = 0; i < NR; ++i) asm volatile("" : "+r"(v[i]));
 }
+template <int NR>
+__device__ __forceinline__ void tmem_wait_ld_regs2(int (&v)[NR], int (&w)[NR]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < NR; ++i) asm volatile("" : "+r"(v[i]), "+r"(w[i]));
+}
 // 32 consecutive TMEM columns of this thread's lane := c (four 8-column stores: the source of one
 // store is 8 consecutive registers, so this keeps the constant's register footprint at 8)
 __device__ __forceinline__ void tmem_st32_const(uint32_t taddr, int c) {
@@ -216,20 +237,10 @@ __device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
 // exact int -> float for |i| < 2^22 (block dots of Q8_0 / Q4_0 are below 2^19)
 __device__ __forceinline__ float i2f_small(int i) { return __fsub_rn(__int_as_float(0x4B400000 + i), 12582912.0f); }
 
-__device__ __forceinline__ void qkv_store(const QKVStore& e, int m, int n, float v) {
-    const uint16_t h = f2h(v);
-    if (n < kD) { e.q16[(size_t)m * kD + n] = h; return; }
-    const int pos = e.rows.pos[m];
-    const int s = e.rows.slot[m];
-    if (pos < 0 || pos >= e.rows.cap[s]) return;
-    const int page = e.kv.ptab[(size_t)s * e.kv.max_pages + pos / kPage];
-    const int which = (n - kD) / kD, j = (n - kD) % kD;
-    e.kv.pool[kv_off(e.kv, page, e.layer, which, j / kHeadDim, pos % kPage) + (j % kHeadDim)] = h;
-}
-
 __global__ void __launch_bounds__(THREADS, 1)
-k_mm_tc_q4k(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, DevW W, ActQ A, int M,
-            const float* __restrict__ bias, int relu, float* __restrict__ y, QKVStore qkv, int use_qkv) {
+k_mm_tc_q4k(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
+            const __grid_constant__ CUtensorMap tmY, DevW W, ActQ A, int M, const float* __restrict__ bias, int relu,
+            float* __restrict__ y, QKVStore qkv, int use_qkv, int tstore) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     float* out_tile = (float*)(smem + NS * STAGE);
@@ -242,6 +253,10 @@ k_mm_tc_q4k(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUt
                    tempty0 = tfull0 + 8 * NBUF, done_bar = tempty0 + 8 * NBUF;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (tid == 0) {   // the producer's first copies need both descriptors
+        asm volatile("prefetch.tensormap [%0];\n" ::"l"((uint64_t)&tmW) : "memory");
+        asm volatile("prefetch.tensormap [%0];\n" ::"l"((uint64_t)&tmX) : "memory");
+    }
     const int N = W.N, K = W.K, nsb = K / 256;
     const int tiles_n = (N + BM - 1) / BM, tiles_m = (M + BN - 1) / BN;
     const int n_tiles = tiles_n * tiles_m;
@@ -394,36 +409,56 @@ k_mm_tc_q4k(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUt
                 auto ld24 = [&](int (&v)[24], int q) { tmem_ld3x8(tb + q * 8, v); };
                 // each 8-column group is restored to the magic pattern as soon as it is in registers
                 auto reset8 = [&](int q) { tmem_st3x8_const(tb + q * 8, kMagic); };
-                int va[24], vb[24];
-                ld24(va, 0); tmem_wait_ld_regs(va); reset8(0);
-                ld24(vb, 1); fold8(va, 0); tmem_wait_ld_regs(vb); reset8(1);
-                ld24(va, 2); fold8(vb, 1); tmem_wait_ld_regs(va); reset8(2);
-                ld24(vb, 3); fold8(va, 2); tmem_wait_ld_regs(vb); reset8(3);
+                // two 8-column groups per TMEM round trip; the second pair loads while the first folds
+                int va[24], vb[24], vc[24], vd[24];
+                ld24(va, 0); ld24(vb, 1); tmem_wait_ld_regs2(va, vb); reset8(0); reset8(1);
+                ld24(vc, 2); ld24(vd, 3); fold8(va, 0); fold8(vb, 1); tmem_wait_ld_regs2(vc, vd); reset8(2); reset8(3);
                 // this warp's columns are read and reset: hand the buffer back
                 asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory");
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) bar_arrive(tempty0 + 8 * buf);
-                fold8(vb, 3);
+                fold8(vc, 2); fold8(vd, 3);
             }
-            // ---------------- output: registers -> smem tile -> coalesced global stores ----------------
-            epi_sync();   // the previous tile's copy-out has finished reading out_tile and kvb
+            // ---------------- output: registers -> smem tile -> global ----------------
+            // The tile is staged in shared memory (f16 for the QKV projection, else f32).  An f32
+            // tile or a Q tile then leaves as one tensor store issued by one thread, so the fold
+            // warps go on to the next tile while it drains (that thread waits until the store has
+            // read the tile before the tile is written again); K/V tiles go to each row's page
+            // slot with 16-byte stores.  Every epilogue warp takes the same abort decision at the
+            // first barrier.
+            const int et = tid - 32 * EPI_WARP0;   // 0..255
+            if (tstore && et == 0) bulk_wait_read();
+            aborted = epi_sync_or(aborted || *abort_flag);
+            const float nan_v = __int_as_float(0x7FC00000);
+            uint16_t* out_h = reinterpret_cast<uint16_t*>(out_tile);   // [BN][BM] f16 (QKV)
             {
+                // acc + accm is never -0 (both chains start at +0), so adding a zero bias changes no value
                 const int col = quarter * 32 + lane;
                 const float bn = (bias && nok) ? bias[n] : 0.0f;
+                const float2 bn2 = make_float2(bn, bn);
+                float2 v2[16];
 #pragma unroll
                 for (int c2 = 0; c2 < 16; ++c2) {
-                    const float2 v2 = add2(acc[c2], accm[c2]);
-                    float v[2] = {v2.x, v2.y};
+                    v2[c2] = add2(add2(acc[c2], accm[c2]), bn2);
+                    if (relu && !(v2[c2].x > 0.0f)) v2[c2].x = 0.0f;
+                    if (relu && !(v2[c2].y > 0.0f)) v2[c2].y = 0.0f;
+                    if (aborted) v2[c2] = make_float2(nan_v, nan_v);
+                }
+                if (use_qkv) {
 #pragma unroll
-                    for (int u = 0; u < 2; ++u) {
-                        if (bias) v[u] = __fadd_rn(v[u], bn);
-                        if (relu) v[u] = (v[u] > 0.0f) ? v[u] : 0.0f;
-                        out_tile[(cg * 32 + 2 * c2 + u) * BM + col] = v[u];
+                    for (int c2 = 0; c2 < 16; ++c2) {
+                        out_h[(cg * 32 + 2 * c2) * BM + col] = f2h(v2[c2].x);
+                        out_h[(cg * 32 + 2 * c2 + 1) * BM + col] = f2h(v2[c2].y);
+                    }
+                } else {
+#pragma unroll
+                    for (int c2 = 0; c2 < 16; ++c2) {
+                        out_tile[(cg * 32 + 2 * c2) * BM + col] = v2[c2].x;
+                        out_tile[(cg * 32 + 2 * c2 + 1) * BM + col] = v2[c2].y;
                     }
                 }
             }
-            const int et = tid - 32 * EPI_WARP0;   // 0..255
             if (use_qkv && et < BN) {
                 // K/V cache element offset of (page, layer, K, head 0, pos, dim 0) for this row, or -1
                 long long off = -1;
@@ -437,39 +472,24 @@ k_mm_tc_q4k(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUt
                 }
                 kvb[et] = off;
             }
-            // every epilogue warp takes the same abort decision here, so all leave the tile loop together
-            aborted = epi_sync_or(aborted || *abort_flag);
-            const float nan_v = __int_as_float(0x7FC00000);
-            if (use_qkv) {
-#pragma unroll 1
-                for (int i = et; i < BN * BM / 4; i += 32 * EPI_WARPS) {
-                    const int ml = i / (BM / 4), nl = (i % (BM / 4)) * 4;
-                    const int m = m0 + ml, nn = n0 + nl;
-                    if (m >= M || nn >= N) continue;
-                    const float4 v4 = aborted ? make_float4(nan_v, nan_v, nan_v, nan_v)
-                                              : *reinterpret_cast<const float4*>(out_tile + ml * BM + nl);
-                    uint2 h;
-                    h.x = (uint32_t)f2h(v4.x) | ((uint32_t)f2h(v4.y) << 16);
-                    h.y = (uint32_t)f2h(v4.z) | ((uint32_t)f2h(v4.w) << 16);
-                    if (nn < kD) {
-                        *reinterpret_cast<uint2*>(qkv.q16 + (size_t)m * kD + nn) = h;
-                    } else {
-                        const long long base = kvb[ml];
-                        if (base < 0) continue;
-                        const int j = nn - kD, which = j / kD, jj = j % kD;
-                        const size_t o = (size_t)base + ((size_t)(which * kHeads + jj / kHeadDim) * kPage) * kHeadDim + (jj % kHeadDim);
-                        *reinterpret_cast<uint2*>(qkv.kv.pool + o) = h;
-                    }
+            if (tstore) fence_proxy_async_smem();
+            epi_sync();
+            if (use_qkv && n0 >= kD) {
+                // K or V tile: 4 heads of 32 values per row; (row, head) chunks of 64 B to the row's page slot
+                const int ml = et >> 2, hh = et & 3;
+                const int m = m0 + ml;
+                const long long base = kvb[ml];
+                if (m < M && base >= 0) {
+                    const int j = n0 - kD + hh * kHeadDim, which = j / kD, head = (j % kD) / kHeadDim;
+                    uint4* dst = reinterpret_cast<uint4*>(qkv.kv.pool + (size_t)base + (size_t)(which * kHeads + head) * kPage * kHeadDim);
+                    const uint4* src = reinterpret_cast<const uint4*>(out_h + ml * BM + hh * kHeadDim);
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) dst[c] = src[c];
                 }
-            } else if ((N & 3) == 0) {
-#pragma unroll 1
-                for (int i = et; i < BN * BM / 4; i += 32 * EPI_WARPS) {
-                    const int ml = i / (BM / 4), nl = (i % (BM / 4)) * 4;
-                    const int m = m0 + ml, nn = n0 + nl;
-                    if (m >= M || nn >= N) continue;
-                    const float4 v4 = aborted ? make_float4(nan_v, nan_v, nan_v, nan_v)
-                                              : *reinterpret_cast<const float4*>(out_tile + ml * BM + nl);
-                    *reinterpret_cast<float4*>(y + (size_t)m * N + nn) = v4;
+            } else if (tstore) {
+                if (et == 0) {
+                    tma_store_2d(&tmY, n0, m0, out_tile);   // Q rows (f16) or y rows (f32)
+                    bulk_commit();
                 }
             } else {
 #pragma unroll 1
@@ -477,10 +497,11 @@ k_mm_tc_q4k(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUt
                     const int ml = i / BM, nl = i % BM;
                     const int m = m0 + ml, nn = n0 + nl;
                     if (m >= M || nn >= N) continue;
-                    y[(size_t)m * N + nn] = aborted ? nan_v : out_tile[i];
+                    y[(size_t)m * N + nn] = out_tile[i];
                 }
             }
         }
+        if (tstore && tid == 32 * EPI_WARP0) bulk_wait_all();   // the stores are complete before the CTA exits
     }
     __syncwarp();
     tc_fence_before();
@@ -510,6 +531,20 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
             fn = (PFN_cuTensorMapEncodeTiled_v12000)p;
     });
     return fn;
+}
+
+// row-major [rows][cols] of f32 or f16 (elem_bytes 4 or 2), boxes of BM columns x BN rows, no
+// swizzle: the staged output tile of the kernel.
+bool make_out_map(CUtensorMap* map, const void* base, int cols, int rows, int elem_bytes) {
+    auto fn = encode_fn();
+    if (!fn || ((uintptr_t)base & 15) || (((size_t)cols * elem_bytes) & 15)) return false;
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)cols * elem_bytes};
+    cuuint32_t box[2] = {(cuuint32_t)BM, (cuuint32_t)BN};
+    cuuint32_t es[2] = {1, 1};
+    return fn(map, elem_bytes == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, const_cast<void*>(base),
+              dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+              CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 // int8 [rows][K] row-major, boxes of 128 bytes of K x box_rows rows, 128-byte swizzle.
@@ -547,7 +582,14 @@ bool launch_q4k(const DevW& W, const ActQ& a, int M, const float* bias, int relu
     if (qkv) q = *qkv;
     const int tiles = ((W.N + BM - 1) / BM) * ((M + BN - 1) / BN);
     const int grid = tiles < n_sm ? tiles : n_sm;
-    launch_k(k_mm_tc_q4k, dim3(grid), dim3(THREADS), (size_t)SMEM, st, mw, mx, W, a, M, bias, relu, y, q, qkv ? 1 : 0);
+    // tensor stores of the output tile: Q rows of the QKV projection (f16 [M][512]), else y (f32
+    // [M][N]) when its rows are 16-byte aligned; otherwise the kernel stores element by element
+    CUtensorMap my;
+    std::memset(&my, 0, sizeof(my));
+    const int tstore = qkv ? (make_out_map(&my, qkv->q16, kD, M, 2) ? 1 : 0) : (make_out_map(&my, y, W.N, M, 4) ? 1 : 0);
+    if (qkv && !tstore) return false;
+    launch_k(k_mm_tc_q4k, dim3(grid), dim3(THREADS), (size_t)SMEM, st, mw, mx, my, W, a, M, bias, relu, y, q, qkv ? 1 : 0,
+             tstore);
     return true;
 }
 
