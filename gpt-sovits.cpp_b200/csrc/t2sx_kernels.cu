@@ -659,9 +659,14 @@ void attention_decode(int T, const uint16_t* q16, Rows rows, KVView kv, int laye
     if (T <= 0) return;
     // a Q8_K output block spans eight heads, so that format needs eight heads per CTA; otherwise
     // small batches spread the heads over more CTAs
-    if (qtype == W_Q4_K) {
-        if (T < 64) launch_k((k_attn_decode<8, true>), dim3(dim3(T, kHeads / 8)), dim3(256), attn_pipe_smem<8>(kv), st, q16, rows, kv, layer, scale, out, qtype, qo);
-        else launch_k((k_attn_decode<8, false>), dim3(dim3(T, kHeads / 8)), dim3(256), 0, st, q16, rows, kv, layer, scale, out, qtype, qo);
+    if (qtype == W_Q4_K && T < 64) {
+        launch_k((k_attn_decode<8, true>), dim3(dim3(T, kHeads / 8)), dim3(256), attn_pipe_smem<8>(kv), st, q16, rows, kv, layer, scale, out, qtype, qo);
+    } else if (qtype == W_Q4_K) {
+        // many rows: four heads per CTA with an f32 row, then the Q8_K conversion as its own pass
+        // (eight-head CTAs that convert in place wait on two CTA barriers per row: 8.65 -> 8.39 ms
+        // for the 2048-row decode step)
+        launch_k((k_attn_decode<4, false>), dim3(dim3(T, kHeads / 4)), dim3(128), 0, st, q16, rows, kv, layer, scale, out, -1, qo);
+        quantize_act(W_Q4_K, out, T, kD, qo, st);
     } else if (T < 64) {
         launch_k((k_attn_decode<2, true>), dim3(dim3(T, kHeads / 2)), dim3(64), attn_pipe_smem<2>(kv), st, q16, rows, kv, layer, scale, out, qtype, qo);
     } else {
