@@ -221,7 +221,7 @@ def run_ours(args):
     # attention of one layer at the last step: each session reads K and V of its whole prefix
     # (ctx_now positions): 2 (K,V) * 16 heads * 32 dims * 2 B = 2048 B per position, plus q/out
     attn_bytes = float((ctx_now * 2048).sum() + per * (512 * 2 + 512 * 4))
-    attn_gbs = attn_bytes / (prof["attention"] * 1e-3) / 1e9
+    attn_gbs = attn_bytes / (prof["attention_kernel"] * 1e-3) / 1e9
     # DRAM bytes per algorithmic byte of this kernel, from one ncu capture (dram__bytes_read.sum +
     # dram__bytes_write.sum = 189.98 MB for 186.91 MB algorithmic, 256 sessions at context 353,
     # profiles/k_attn_decode_256sessions.md); the full launch is too large to capture, so its
@@ -281,7 +281,7 @@ def run_ours(args):
                 "traffic_source": "ncu dram bytes at 256 sessions scaled by algorithmic bytes",
                 "peak_kind": peak_kind,
                 "algorithmic_bytes_per_launch": int(attn_bytes),
-                "launch_ms": round(prof["attention"], 4),
+                "launch_ms": round(prof["attention_kernel"], 4),
             },
             "kernel_ms": {k: round(v, 4) for k, v in prof.items()},
             "kernel_ms_at_start": {k: round(v, 4) for k, v in prof_start.items()},

@@ -1353,6 +1353,8 @@ extern "C" int t2sx_profile_step(t2sx_session* s, int32_t iters, float* ms) {
     if ((rc = timeit(4, [&] { matmul(L.down, a, T, L.down_b, 0, w.f, s->st); }))) return rc;
     if ((rc = timeit(6, [&] { residual_layernorm(T, w.ln1, w.f, L.ln2_w, L.ln2_b, 1e-5f, w.o, -1, a, s->st); }))) return rc;
     if ((rc = timeit(7, [&] { quantize_act(L.down.type, w.h, T, s->ff, a, s->st); }))) return rc;
+    // the attention kernel alone (f32 rows, no conversion for the out-projection)
+    if ((rc = timeit(8, [&] { attention_decode(T, w.q16, rows, kv, 0, kAttnScale, w.attn, -1, a, s->st); }))) return rc;
     CK(cudaGetLastError());
     return T2SX_OK;
 }

@@ -269,10 +269,10 @@ class Session:
         return n.value
 
     def profile_step(self, iters: int = 20):
-        ms = np.zeros(8, dtype=np.float32)
+        ms = np.zeros(9, dtype=np.float32)
         _ck(lib().t2sx_profile_step(self.h, iters, _p(ms)))
         return dict(zip(["attention", "mm_qkv", "mm_out", "mm_up", "mm_down", "mm_lm_head", "residual_ln",
-                         "quant_2048"], ms.tolist()))
+                         "quant_2048", "attention_kernel"], ms.tolist()))
 
     def read_logits(self, max_rows: int | None = None):
         max_rows = max_rows or self.n_slots

@@ -162,7 +162,8 @@ T2SX_API int t2sx_decode_graph_kernels(t2sx_session* s, int32_t* n);
 /* Average device ms of one launch of each decode-step kernel class, replayed on the state of
  * the last decode step: ms[0] attention (one layer), ms[1..5] matmuls qkv, out, ffn-up,
  * ffn-down, lm_head (with their bias/ReLU epilogues), ms[6] residual+LayerNorm,
- * ms[7] activation quantisation of the 2048-wide FFN rows.  ms must hold 8 floats. */
+ * ms[7] activation quantisation of the 2048-wide FFN rows, ms[8] the attention kernel alone
+ * (f32 rows; ms[0] adds the conversion for the out-projection).  ms must hold 9 floats. */
 T2SX_API int t2sx_profile_step(t2sx_session* s, int32_t iters, float* ms);
 
 /* ---- kernels on caller-provided device buffers (isolated measurements) ------------------- */
