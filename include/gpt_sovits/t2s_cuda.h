@@ -23,6 +23,7 @@
 #ifndef GPT_SOVITS_T2S_CUDA_H
 #define GPT_SOVITS_T2S_CUDA_H
 
+#include <cstddef>
 #include <cstdint>
 #include <cstdio>
 #include <cstdlib>
@@ -153,6 +154,9 @@ inline int t2s_session_slot_n_pos(const t2s_session & session, int slot_id) {
     return t2sx_session_slot_n_pos(session.handle, slot_id);
 }
 
+// Total KV entries (t2s_session_get_n_kv, t2s.h:431): always n_batch * slot_size.
+inline int t2s_session_get_n_kv(const t2s_session & session) { return (int)(session.n_batch * session.slot_size); }
+
 // Prefill input rows of one prompt (t2s_embed_input_forward / t2s_embed_ref_forward,
 // block.cpp:424-511): x_out f32 [T_text + T_prompt][d_model] (host).
 inline bool t2s_embed_input(t2s_session & session, const int32_t * phones, const float * bert, int T_text,
@@ -192,6 +196,29 @@ inline bool t2s_session_compute_ref_emb(t2s_session & session, const t2s_model &
 }
 inline int64_t t2s_session_get_ref_T_ref(const t2s_session & session) { return session.ref_T_ref; }
 inline int64_t t2s_session_get_ref_T_prompt(const t2s_session & session) { return session.ref_T_prompt; }
+
+// The reference's cached embeddings (t2s_session_get_ref_text_emb / get_ref_audio_emb,
+// t2s.h:458-461) as host rows f32 [T][d_model]: the reference text rows (text embedding + BERT
+// projection + positions 0..T_ref-1) and the prompt rows (code embedding + positions
+// 0..T_prompt-1).  Empty before t2s_session_compute_ref_emb.
+inline std::vector<float> t2s_session_get_ref_text_emb(t2s_session & session, const t2s_model & model) {
+    if (session.ref_T_ref <= 0) return {};
+    std::vector<float> x((size_t)(session.ref_T_ref + session.ref_T_prompt) * model.hparams.embedding_dim);
+    if (!t2s_embed_input(session, session.ref_tokens.data(), session.ref_bert.data(), (int)session.ref_T_ref,
+                         session.ref_codes.data(), (int)session.ref_T_prompt, x.data()))
+        return {};
+    x.resize((size_t)session.ref_T_ref * model.hparams.embedding_dim);
+    return x;
+}
+inline std::vector<float> t2s_session_get_ref_audio_emb(t2s_session & session, const t2s_model & model) {
+    if (session.ref_T_ref <= 0) return {};
+    const size_t d = model.hparams.embedding_dim;
+    std::vector<float> x((size_t)(session.ref_T_ref + session.ref_T_prompt) * d);
+    if (!t2s_embed_input(session, session.ref_tokens.data(), session.ref_bert.data(), (int)session.ref_T_ref,
+                         session.ref_codes.data(), (int)session.ref_T_prompt, x.data()))
+        return {};
+    return std::vector<float>(x.begin() + (ptrdiff_t)(session.ref_T_ref * d), x.end());
+}
 
 // Prefill rows f32 [T_ref + T_in + T_prompt][d_model] (host) for an input text after the reference.
 inline bool t2s_embed_with_ref(t2s_session & session, const t2s_model & model, const int32_t * phones,

@@ -4,7 +4,7 @@
 // released and prefilled again while the other slots decode), then more decode steps.
 //
 // usage: t2s_decode_loop MODEL.gguf INPUTS.bin N_STEPS [release_bad|decode_idle|plan_idle]
-//        t2s_decode_loop MODEL.gguf INPUTS.bin N_STEPS ref HUBERT.bin
+//        t2s_decode_loop MODEL.gguf INPUTS.bin N_STEPS ref HUBERT.bin [EMB_PREFIX]
 // ref: prompt 0 is the reference text, HUBERT.bin (int32 T_hub, f32 [T_hub][768]) its audio
 // features; t2s_session_compute_ref_emb extracts the prompt codes, prompt 1's text is embedded
 // after the reference, slot 0 is prefilled and decoded; prints the codes and the tokens.
@@ -16,6 +16,7 @@
 #include <algorithm>
 #include <cstdio>
 #include <cstring>
+#include <string>
 #include <vector>
 
 using namespace gpt_sovits;
@@ -119,6 +120,19 @@ int main(int argc, char** argv) {
         if (!t2s_flex_graph_compute(session, g)) return 5;
         const int tok = g.sampled[0];
         t2s_flex_graph_free(g);
+        if (t2s_session_get_n_kv(session) != (int)(session.n_batch * session.slot_size)) return 10;
+        if (argc > 6) {   // the cached reference embeddings, raw f32
+            const std::vector<float> te = t2s_session_get_ref_text_emb(session, model);
+            const std::vector<float> ae = t2s_session_get_ref_audio_emb(session, model);
+            const std::string base = argv[6];
+            FILE* ft = std::fopen((base + ".text").c_str(), "wb");
+            FILE* fa = std::fopen((base + ".audio").c_str(), "wb");
+            if (!ft || !fa) return 11;
+            std::fwrite(te.data(), 4, te.size(), ft);
+            std::fwrite(ae.data(), 4, ae.size(), fa);
+            std::fclose(ft);
+            std::fclose(fa);
+        }
         std::printf("{\"codes\": [");
         for (size_t i = 0; i < session.ref_codes.size(); ++i) std::printf("%s%d", i ? ", " : "", session.ref_codes[i]);
         std::printf("], \"T_prompt\": %lld, \"tokens\": [", (long long)t2s_session_get_ref_T_prompt(session));

@@ -124,7 +124,8 @@ def test_cpp_compute_ref_emb_matches_oracle(t2sx_mod, orc, tmp_path):
     with open(hub_path, "wb") as f:
         np.array([T_hub], np.int32).tofile(f)
         hub.tofile(f)
-    r = subprocess.run([exe, path, inp, "2", "ref", hub_path], capture_output=True, text=True, timeout=600)
+    emb = str(tmp_path / "refemb")
+    r = subprocess.run([exe, path, inp, "2", "ref", hub_path, emb], capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, (r.returncode, r.stderr)
     got = json.loads(r.stdout)
 
@@ -141,3 +142,12 @@ def test_cpp_compute_ref_emb_matches_oracle(t2sx_mod, orc, tmp_path):
     assert got["codes"] == [int(c) for c in codes]
     assert got["T_prompt"] == codes.size
     assert got["tokens"] == [int(tok)]
+    # t2s_session_get_ref_text_emb / get_ref_audio_emb: the reference rows of the prefill input
+    m = orc.Model(path)
+    x_ref = m.embed_prefill(ref_ph, ref_bert, codes)
+    m.close()
+    text = np.fromfile(emb + ".text", dtype=np.float32).reshape(-1, 512)
+    audio = np.fromfile(emb + ".audio", dtype=np.float32).reshape(-1, 512)
+    assert text.shape == (ref_ph.size, 512) and audio.shape == (codes.size, 512)
+    assert np.array_equal(text.view(np.uint32), x_ref[:ref_ph.size].view(np.uint32))
+    assert np.array_equal(audio.view(np.uint32), x_ref[ref_ph.size:].view(np.uint32))
