@@ -91,6 +91,7 @@ static int64_t row_bytes(int type, int64_t n) {
         case W_F16: return n * 2;
         case W_Q8_0: return n % 32 ? -1 : n / 32 * 34;
         case W_Q4_0: return n % 32 ? -1 : n / 32 * 18;
+        case W_Q5_0: return n % 32 ? -1 : n / 32 * 22;
         case W_Q4_K: return n % 256 ? -1 : n / 256 * 144;
     }
     return -1;
@@ -141,6 +142,26 @@ static bool repack_weight(int type, const uint8_t* src, int64_t N, int64_t K, Ar
                 d[n * (K / 32) + b] = host_h2f(hd);
                 memcpy(&q[n * K + b * 32], blk + 2, 32);
             }
+        w.q8 = ar.add(as_bytes(q)); w.d = ar.add(as_bytes(d));
+    } else if (type == W_Q5_0) {
+        // ggml block_q5_0 (f16 d, uint32 qh of fifth bits, 16 bytes of low nibbles; elements j and
+        // j + 16 share byte j) -> the Q8_0 layout: int8 value in [-16, 15] and f32 d per block.  The
+        // ggml dot with Q8_0 activations (integer block sum, then the scale fold) is the Q8_0 one.
+        std::vector<int8_t> q((size_t)N * K);
+        std::vector<float> d((size_t)N * (K / 32));
+        for (int64_t n = 0; n < N; ++n)
+            for (int64_t b = 0; b < K / 32; ++b) {
+                const uint8_t* blk = src + (n * (K / 32) + b) * 22;
+                uint16_t hd; memcpy(&hd, blk, 2);
+                uint32_t qh; memcpy(&qh, blk + 2, 4);
+                d[n * (K / 32) + b] = host_h2f(hd);
+                for (int i = 0; i < 32; ++i) {
+                    const int j = i & 15;
+                    const int lo = (i < 16) ? (blk[6 + j] & 0xF) : (blk[6 + j] >> 4);
+                    q[n * K + b * 32 + i] = (int8_t)((lo | (int)(((qh >> i) & 1u) << 4)) - 16);
+                }
+            }
+        w.type = W_Q8_0;
         w.q8 = ar.add(as_bytes(q)); w.d = ar.add(as_bytes(d));
     } else if (type == W_Q4_0) {
         std::vector<uint8_t> q((size_t)N * (K / 2));

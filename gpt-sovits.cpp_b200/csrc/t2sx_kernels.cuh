@@ -27,7 +27,9 @@ inline void launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t sme
     cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
-enum WType : int { W_F32 = 0, W_F16 = 1, W_Q4_0 = 2, W_Q8_0 = 8, W_Q4_K = 12 };
+// GGUF tensor types.  Q5_0 only occurs in files: the loader expands it to the Q8_0 layout (int8
+// values and a per-block scale), whose kernels compute its dot exactly as ggml does.
+enum WType : int { W_F32 = 0, W_F16 = 1, W_Q4_0 = 2, W_Q5_0 = 6, W_Q8_0 = 8, W_Q4_K = 12 };
 
 // A linear weight [N rows][K] repacked for the device.
 //   Q8_0: q8 [N][K] int8, d [N][K/32] f32 (the f16 block scales widened)

@@ -7,7 +7,7 @@ quantised, embeddings and other 2-D tensors are f16, 1-D tensors f32, codebook f
 Weights are N(0, 0.02) from numpy.random.default_rng(seed) in tensor order, LayerNorm
 gamma = 1 and beta = 0, positional alphas = 1.0.  There is no real checkpoint here.
 
-Q8_0 and Q4_0 use gguf-py's own quantizers (the converter's).  Q4_K has no quantizer in
+Q8_0, Q5_0 and Q4_0 use gguf-py's own quantizers (the converter's).  Q4_K has no quantizer in
 gguf-py, so `quantize_q4_k` below encodes it (any valid Q4_K encoding serves: the oracle and
 the GPU consume the same bytes).
 """
@@ -16,9 +16,9 @@ from __future__ import annotations
 import os
 import numpy as np
 
-GGML_F32, GGML_F16, GGML_Q4_0, GGML_Q8_0, GGML_Q4_K = 0, 1, 2, 8, 12
-TYPE_NAMES = {"f32": GGML_F32, "f16": GGML_F16, "q4_0": GGML_Q4_0, "q8_0": GGML_Q8_0, "q4_k": GGML_Q4_K}
-BLOCK = {GGML_Q8_0: 32, GGML_Q4_0: 32, GGML_Q4_K: 256}
+GGML_F32, GGML_F16, GGML_Q4_0, GGML_Q5_0, GGML_Q8_0, GGML_Q4_K = 0, 1, 2, 6, 8, 12
+TYPE_NAMES = {"f32": GGML_F32, "f16": GGML_F16, "q4_0": GGML_Q4_0, "q5_0": GGML_Q5_0, "q8_0": GGML_Q8_0, "q4_k": GGML_Q4_K}
+BLOCK = {GGML_Q8_0: 32, GGML_Q5_0: 32, GGML_Q4_0: 32, GGML_Q4_K: 256}
 
 ATTN_NAMES = ["qkv_w", "qkv_b", "out_proj_w", "out_proj_b", "ln1_w", "ln1_b",
               "ffn_up_w", "ffn_up_b", "ffn_down_w", "ffn_down_b", "ln2_w", "ln2_b"]

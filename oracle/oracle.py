@@ -15,7 +15,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "liborc.so")
 _lib = None
 
-F32, F16, Q4_0, Q8_0, Q4_K = 0, 1, 2, 8, 12
+F32, F16, Q4_0, Q5_0, Q8_0, Q4_K = 0, 1, 2, 6, 8, 12
 
 
 def build(force: bool = False) -> str:

@@ -17,7 +17,7 @@
 //
 // ggml semantics restated (ggml itself is absent from the reference snapshot):
 //   mul_mat     the f32 activation row is converted to the weight type's dot type first:
-//               Q8_0 and Q4_0 weights -> Q8_0 activations (x86 AVX2 rule: id = 127/amax,
+//               Q8_0, Q5_0 and Q4_0 weights -> Q8_0 activations (x86 AVX2 rule: id = 127/amax,
 //               round-half-even, scale stored f16); Q4_K -> Q8_K (ggml reference rule: scale
 //               -127/max, f32); F16 -> f16 (round-half-even); F32 stays f32.  Per block the
 //               integer dot is exact.  Float order (fixed here): blocks in increasing order,
@@ -135,12 +135,23 @@ static void q4k_scale_min(const uint8_t* sc, int j, int& s, int& m) {
     }
 }
 
+// Element i (0..31) of a Q5_0 block as a signed integer in [-16, 15] (ggml dequantize_row_q5_0:
+// elements j and j + 16 share byte j of qs, low and high nibble; bit j / j + 16 of qh is the fifth bit).
+static int q5_0_value(const uint8_t* blk, int i) {
+    uint32_t qh;
+    memcpy(&qh, blk + 2, 4);
+    const int j = i & 15;
+    const int lo = (i < 16) ? (blk[6 + j] & 0xF) : (blk[6 + j] >> 4);
+    return (lo | (int)(((qh >> i) & 1u) << 4)) - 16;
+}
+
 int64_t orc_row_bytes(int type, int64_t n) {
     switch (type) {
         case ORC_F32: return n * 4;
         case ORC_F16: return n * 2;
         case ORC_Q8_0: return n / 32 * 34;
         case ORC_Q4_0: return n / 32 * 18;
+        case ORC_Q5_0: return n / 32 * 22;
         case ORC_Q4_K: return n / 256 * 144;
     }
     return -1;
@@ -166,6 +177,13 @@ void orc_dequantize(int type, const void* data, int64_t n, float* out) {
                     out[b * 32 + i] = (float)((blk[2 + i] & 0xF) - 8) * d;
                     out[b * 32 + 16 + i] = (float)((blk[2 + i] >> 4) - 8) * d;
                 }
+            }
+            break;
+        case ORC_Q5_0:   // ggml block_q5_0: f16 d, uint32 qh (fifth bits), 16 bytes of low nibbles
+            for (int64_t b = 0; b < n / 32; ++b) {
+                const uint8_t* blk = p + b * 22;
+                float d = h2f(rd16(blk));
+                for (int i = 0; i < 32; ++i) out[b * 32 + i] = (float)q5_0_value(blk, i) * d;
             }
             break;
         case ORC_Q4_K:
@@ -254,7 +272,7 @@ struct ActRow {
 
 static void prep_act(int wtype, const float* x, int64_t K, ActRow& a) {
     a.type = wtype;
-    if (wtype == ORC_Q8_0 || wtype == ORC_Q4_0) { a.q8.resize(K / 32); quant_q8_0(x, K, a.q8.data(), nullptr); }
+    if (wtype == ORC_Q8_0 || wtype == ORC_Q4_0 || wtype == ORC_Q5_0) { a.q8.resize(K / 32); quant_q8_0(x, K, a.q8.data(), nullptr); }
     else if (wtype == ORC_Q4_K) { a.q8k.resize(K / 256); quant_q8_K(x, K, a.q8k.data()); }
     else if (wtype == ORC_F16) { a.f.resize(K); for (int64_t i = 0; i < K; ++i) a.f[i] = h2f(f2h(x[i])); }
     else { a.f.assign(x, x + K); }
@@ -283,6 +301,17 @@ static float qdot(int wtype, const uint8_t* w, int64_t K, const ActRow& a) {
                 isum += ((int)(wb[2 + i] & 0xF) - 8) * (int)a.q8[b].qs[i];
                 isum += ((int)(wb[2 + i] >> 4) - 8) * (int)a.q8[b].qs[16 + i];
             }
+            const float dd = h2f(rd16(wb)) * a.q8[b].d;
+            acc = fmaf(dd, (float)isum, acc);
+        }
+        return acc;
+    }
+    if (wtype == ORC_Q5_0) {   // ggml_vec_dot_q5_0_q8_0: integer block dot, then the Q8_0 fold
+        float acc = 0.0f;
+        for (int64_t b = 0; b < K / 32; ++b) {
+            const uint8_t* wb = w + b * 22;
+            int isum = 0;
+            for (int i = 0; i < 32; ++i) isum += q5_0_value(wb, i) * (int)a.q8[b].qs[i];
             const float dd = h2f(rd16(wb)) * a.q8[b].d;
             acc = fmaf(dd, (float)isum, acc);
         }

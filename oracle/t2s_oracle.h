@@ -20,7 +20,7 @@ extern "C" {
 #endif
 
 // ggml type ids used by the GGUF files (ggml.h enum ggml_type).
-enum { ORC_F32 = 0, ORC_F16 = 1, ORC_Q4_0 = 2, ORC_Q8_0 = 8, ORC_Q4_K = 12 };
+enum { ORC_F32 = 0, ORC_F16 = 1, ORC_Q4_0 = 2, ORC_Q5_0 = 6, ORC_Q8_0 = 8, ORC_Q4_K = 12 };
 
 // ---- primitives -------------------------------------------------------------------------
 float    orc_expf(float x);

@@ -26,6 +26,8 @@ def _weights(fmt, N, K, seed):
         return 8, gguf.quantize(w, gguf.GGMLQuantizationType.Q8_0)
     if fmt == "q4_0":
         return 2, gguf.quantize(w, gguf.GGMLQuantizationType.Q4_0)
+    if fmt == "q5_0":
+        return 6, gguf.quantize(w, gguf.GGMLQuantizationType.Q5_0)
     if fmt == "q4_k":
         return 12, synth.quantize_q4_k(w)
     if fmt == "f16":
@@ -39,7 +41,7 @@ def same_bits(a, b):
     return a.shape == b.shape and np.array_equal(a.view(np.uint32), b.view(np.uint32))
 
 
-@pytest.mark.parametrize("fmt", ["q8_0", "q4_0", "q4_k", "f16", "f32"])
+@pytest.mark.parametrize("fmt", ["q8_0", "q5_0", "q4_0", "q4_k", "f16", "f32"])
 @pytest.mark.parametrize("NK", [(1536, 512), (512, 2048), (1025, 512)])
 @pytest.mark.parametrize("M", [1, 7, 8, 16, 17, 32, 33, 64, 65, 130, 255, 2048])
 def test_matmul_bit_exact(t2sx_mod, orc, fmt, NK, M):
@@ -116,7 +118,7 @@ def _run_pair(t2sx_mod, orc, path, lengths, steps, rep_penalty=1.0, eos_mask=Tru
     return gpu_tokens
 
 
-@pytest.mark.parametrize("fmt", ["q8_0", "q4_0", "q4_k", "f16"])
+@pytest.mark.parametrize("fmt", ["q8_0", "q5_0", "q4_0", "q4_k", "f16"])
 def test_decode_small_model_bit_exact(t2sx_mod, orc, fmt):
     _need_gpu()
     import synth

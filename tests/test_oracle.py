@@ -35,7 +35,7 @@ def test_expf_accuracy(orc):
     assert L.orc_expf(float("-inf")) == 0.0 and L.orc_expf(-200.0) == 0.0
 
 
-@pytest.mark.parametrize("fmt", ["q8_0", "q4_0", "q4_k", "f16"])
+@pytest.mark.parametrize("fmt", ["q8_0", "q5_0", "q4_0", "q4_k", "f16"])
 def test_dequant_bit_exact_vs_gguf_py(orc, fmt):
     import gguf
     import synth
@@ -108,7 +108,7 @@ def q8_k_act(x):
 
 def f64_matmul(wtype, wbytes, N, K, x, orc):
     wd = orc.dequantize(wtype, wbytes.reshape(-1), N * K).astype(np.float64).reshape(N, K)
-    if wtype in (8, 2):
+    if wtype in (8, 6, 2):   # Q8_0, Q5_0, Q4_0 weights: Q8_0 activations
         q, d = q8_0_act(x)
         xa = (q * d[:, None]).reshape(x.shape).astype(np.float64)
     elif wtype == 12:
@@ -121,7 +121,7 @@ def f64_matmul(wtype, wbytes, N, K, x, orc):
     return xa @ wd.T
 
 
-@pytest.mark.parametrize("fmt,wtype", [("q8_0", 8), ("q4_0", 2), ("q4_k", 12), ("f16", 1)])
+@pytest.mark.parametrize("fmt,wtype", [("q8_0", 8), ("q5_0", 6), ("q4_0", 2), ("q4_k", 12), ("f16", 1)])
 def test_matmul_matches_float64(orc, fmt, wtype):
     import gguf
     import synth
@@ -130,6 +130,7 @@ def test_matmul_matches_float64(orc, fmt, wtype):
     w = rng.standard_normal((N, K)).astype(np.float32) * 0.02
     wb = {"q8_0": lambda: gguf.quantize(w, gguf.GGMLQuantizationType.Q8_0),
           "q4_0": lambda: gguf.quantize(w, gguf.GGMLQuantizationType.Q4_0),
+          "q5_0": lambda: gguf.quantize(w, gguf.GGMLQuantizationType.Q5_0),
           "q4_k": lambda: synth.quantize_q4_k(w), "f16": lambda: w.astype(np.float16).view(np.uint8)}[fmt]()
     x = rng.standard_normal((M, K)).astype(np.float32)
     got = orc.matmul(wtype, wb, N, K, x)
