@@ -399,6 +399,114 @@ int tc_min_rows() {
     return v;
 }
 
+// F16 / F32 weights for many rows (CUDA cores): a CTA computes a 64 x 64 block of outputs (64
+// weight rows x 64 activation rows), each of its 256 threads a 4 x 4 sub-block.  The arithmetic
+// per output is the small kernel's: per 32-element block a chain of fmas from 0 over the
+// elements in order, and the blocks added in order from 0.  Each block's weight and activation
+// slices are staged in shared memory as f32, K-major, double-buffered.
+template <int WT>
+__global__ void __launch_bounds__(256) k_mm_fp_tile(DevW W, ActQ A, int M, const float* __restrict__ bias, int relu,
+                                                     float* __restrict__ y, QKVStore qkv, int use_qkv) {
+    pdl_trigger();
+    pdl_wait();
+    constexpr int TN = 64, TM = 64, KB = 32;
+    __shared__ __align__(16) float ws[2][KB][TN];
+    __shared__ __align__(16) float xs[2][KB][TM];
+    const int N = W.N, K = W.K, nb = K / KB;
+    const int n0 = blockIdx.x * TN, m0 = blockIdx.y * TM;
+    const int tid = threadIdx.x, tn = tid & 15, tm = tid >> 4;
+    // staging: thread t copies 8 consecutive elements of one row (of W and of A) per block; the
+    // next block's global loads are issued before this block's fmas and stored to shared memory
+    // after them
+    const int lr = tid >> 2, lk = (tid & 3) * 8;
+    uint4 wraw, xraw;        // F16: 8 halves each
+    float4 wf0, wf1, xf0, xf1;   // F32
+    auto load = [&](int b) {
+        const int n = n0 + lr, m = m0 + lr, k = b * KB + lk;
+        if (WT == W_F16) {
+            wraw = n < N ? *reinterpret_cast<const uint4*>(W.h + (size_t)n * K + k) : make_uint4(0, 0, 0, 0);
+            xraw = m < M ? *reinterpret_cast<const uint4*>(A.h + (size_t)m * K + k) : make_uint4(0, 0, 0, 0);
+        } else {
+            const float4 z = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            wf0 = n < N ? *reinterpret_cast<const float4*>(W.f + (size_t)n * K + k) : z;
+            wf1 = n < N ? *reinterpret_cast<const float4*>(W.f + (size_t)n * K + k + 4) : z;
+            xf0 = m < M ? *reinterpret_cast<const float4*>(A.f + (size_t)m * K + k) : z;
+            xf1 = m < M ? *reinterpret_cast<const float4*>(A.f + (size_t)m * K + k + 4) : z;
+        }
+    };
+    auto store = [&](int buf) {
+        float wv[8], xv[8];
+        if (WT == W_F16) {
+            const uint32_t w4[4] = {wraw.x, wraw.y, wraw.z, wraw.w}, x4[4] = {xraw.x, xraw.y, xraw.z, xraw.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                wv[2 * i] = h2f((uint16_t)(w4[i] & 0xffffu)); wv[2 * i + 1] = h2f((uint16_t)(w4[i] >> 16));
+                xv[2 * i] = h2f((uint16_t)(x4[i] & 0xffffu)); xv[2 * i + 1] = h2f((uint16_t)(x4[i] >> 16));
+            }
+        } else {
+            wv[0] = wf0.x; wv[1] = wf0.y; wv[2] = wf0.z; wv[3] = wf0.w; wv[4] = wf1.x; wv[5] = wf1.y; wv[6] = wf1.z; wv[7] = wf1.w;
+            xv[0] = xf0.x; xv[1] = xf0.y; xv[2] = xf0.z; xv[3] = xf0.w; xv[4] = xf1.x; xv[5] = xf1.y; xv[6] = xf1.z; xv[7] = xf1.w;
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) { ws[buf][lk + i][lr] = wv[i]; xs[buf][lk + i][lr] = xv[i]; }
+    };
+    float acc[4][4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[j][i] = 0.0f;
+    load(0);
+    store(0);
+    __syncthreads();
+    for (int b = 0; b < nb; ++b) {
+        const int buf = b & 1;
+        if (b + 1 < nb) load(b + 1);
+        float sblk[4][4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) sblk[j][i] = 0.0f;
+#pragma unroll
+        for (int k = 0; k < KB; ++k) {
+            const float4 w4 = *reinterpret_cast<const float4*>(&ws[buf][k][4 * tn]);
+            const float4 x4 = *reinterpret_cast<const float4*>(&xs[buf][k][4 * tm]);
+            const float wr[4] = {w4.x, w4.y, w4.z, w4.w}, xr[4] = {x4.x, x4.y, x4.z, x4.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) sblk[j][i] = __fmaf_rn(wr[j], xr[i], sblk[j][i]);
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) acc[j][i] = __fadd_rn(acc[j][i], sblk[j][i]);
+        if (b + 1 < nb) store(buf ^ 1);   // buf ^ 1 was last read before the previous barrier
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int m = m0 + 4 * tm + i;
+        if (m >= M) continue;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int n = n0 + 4 * tn + j;
+            if (n >= N) continue;
+            const float v = epi(acc[j][i], bias, n, relu);
+            if (use_qkv) qkv_store(qkv, m, n, v);
+            else y[(size_t)m * N + n] = v;
+        }
+    }
+}
+
+// Rows from which F16 / F32 weights use the tiled kernel (T2SX_FP_TILE_MIN_ROWS; 0 = never).
+static int fp_tile_min_rows() {
+    static const int v = [] {
+        const char* e = getenv("T2SX_FP_TILE_MIN_ROWS");
+        return e ? atoi(e) : kSmallM + 1;
+    }();
+    return v;
+}
+
 void matmul(const DevW& W, const ActQ& a, int M, const float* bias, int relu, float* y, cudaStream_t st, const Epi& e) {
     const bool quant = W.type == W_Q8_0 || W.type == W_Q4_0 || W.type == W_Q4_K;
     if (quant && M >= tc_min_rows() && matmul_tc(W, a, M, bias, relu, y, e.qkv, st)) return;
@@ -407,6 +515,16 @@ void matmul(const DevW& W, const ActQ& a, int M, const float* bias, int relu, fl
         return;
     QKVStore qkv{};
     if (e.qkv) qkv = *e.qkv;
+    // (16-byte loads: the f32 activations may be a caller's pointer)
+    const bool fp_aligned = W.type == W_F16 ? (((uintptr_t)a.h | (uintptr_t)W.h) & 15) == 0
+                                            : (((uintptr_t)a.f | (uintptr_t)W.f) & 15) == 0;
+    if ((W.type == W_F16 || W.type == W_F32) && fp_tile_min_rows() > 0 && M >= fp_tile_min_rows() && W.K % 32 == 0 &&
+        fp_aligned && !(e.tail && M <= kSmallM)) {
+        const dim3 grid((W.N + 63) / 64, (M + 63) / 64);
+        if (W.type == W_F16) launch_k(k_mm_fp_tile<W_F16>, grid, dim3(256), 0, st, W, a, M, bias, relu, y, qkv, e.qkv ? 1 : 0);
+        else launch_k(k_mm_fp_tile<W_F32>, grid, dim3(256), 0, st, W, a, M, bias, relu, y, qkv, e.qkv ? 1 : 0);
+        return;
+    }
     Tail tail{};
     const bool use_tail = e.tail && M <= kSmallM;
     if (use_tail) tail = *e.tail;
