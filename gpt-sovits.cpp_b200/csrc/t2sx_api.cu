@@ -644,6 +644,7 @@ static Rows rows_of(t2sx_session* s, Work& w) {
 static KVView kv_of(t2sx_session* s) {
     KVView v;
     v.pool = s->pool; v.ptab = s->ptab; v.max_pages = s->pages_per_slot; v.n_layer = s->n_layer;
+    v.n_pages = s->n_slots * s->pages_per_slot;
     return v;
 }
 
@@ -1315,7 +1316,8 @@ extern "C" int t2sx_read_kv(t2sx_session* s, int32_t slot, int32_t layer, int32_
     std::vector<uint16_t> page((size_t)kHeads * kPage * kHeadDim);
     for (int p0 = 0; p0 < n; p0 += kPage) {
         const int pg = s->ptab_h[(size_t)slot * s->pages_per_slot + p0 / kPage];
-        const size_t off = ((((size_t)pg * s->n_layer + layer) * 2 + which) * kHeads) * kPage * kHeadDim;
+        const size_t n_pages = (size_t)s->n_slots * s->pages_per_slot;
+        const size_t off = ((((size_t)layer * n_pages + pg) * 2 + which) * kHeads) * kPage * kHeadDim;
         CK(cudaMemcpy(page.data(), s->pool + off, page.size() * 2, cudaMemcpyDeviceToHost));
         for (int i = p0; i < n && i < p0 + kPage; ++i)
             for (int h = 0; h < kHeads; ++h)

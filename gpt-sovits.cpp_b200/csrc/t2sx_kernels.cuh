@@ -62,14 +62,17 @@ struct ActQ {
     const float* f = nullptr;
 };
 
-// Paged f16 KV cache: page p holds kPage positions of every layer,
-// element (p, layer, kv, head, pos, dim) at
-//   pool[((((p * n_layer + layer) * 2 + kv) * kHeads + head) * kPage + pos) * kHeadDim + dim]
+// Paged f16 KV cache, layer-major: page p holds kPage positions, and each layer's slices of all
+// n_pages pages are one contiguous region (an attention launch reads one layer, so its pages lie
+// in n_pages * 128 KB of address space instead of spread over the whole pool);
+// element (layer, p, kv, head, pos, dim) at
+//   pool[(((((size_t)layer * n_pages + p) * 2 + kv) * kHeads + head) * kPage + pos) * kHeadDim + dim]
 struct KVView {
     uint16_t* pool = nullptr;
     const int32_t* ptab = nullptr;  // [n_slots][max_pages]
     int max_pages = 0;
     int n_layer = 0;
+    int n_pages = 0;                // pages in the pool
 };
 
 // Per-row routing of one forward pass (rows = tokens of this pass).

@@ -5,9 +5,9 @@
 
 namespace t2sx {
 
-// Element offset of (page, layer, K|V, head, position in page, dim 0) in the page pool.
+// Element offset of (layer, page, K|V, head, position in page, dim 0) in the page pool (layer-major).
 __device__ __forceinline__ size_t kv_off(const KVView& kv, int page, int layer, int which, int head, int pos_in_page) {
-    return (((((size_t)page * kv.n_layer + layer) * 2 + which) * kHeads + head) * kPage + pos_in_page) * kHeadDim;
+    return (((((size_t)layer * kv.n_pages + page) * 2 + which) * kHeads + head) * kPage + pos_in_page) * kHeadDim;
 }
 
 // cp.async copies global -> shared (16 or 4 bytes; a false `valid` copies nothing and zero-fills),

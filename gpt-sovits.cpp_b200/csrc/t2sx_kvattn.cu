@@ -122,6 +122,7 @@ extern "C" int t2sx_kvcache_write(t2sx_kvcache* c, int32_t seq, int32_t pos0, in
     KCK(cudaMemcpyAsync(c->stage + (size_t)len * row, v, (size_t)len * row * 2, cudaMemcpyHostToDevice, c->st));
     KVView kv;
     kv.pool = c->pool; kv.ptab = c->ptab; kv.max_pages = c->pages_per_seq; kv.n_layer = 1;
+    kv.n_pages = c->n_seqs * c->pages_per_seq;
     const int threads = len * kHeads * 4;
     k_kv_scatter<<<(threads + 255) / 256, 256, 0, c->st>>>(len, pos0, seq, c->stage, c->stage + (size_t)len * row, kv);
     KCK(cudaGetLastError());
@@ -165,6 +166,7 @@ static int kv_attn(t2sx_kvcache* c, int32_t n, const int32_t* seqs, const int32_
     if (rc) return rc;
     KVView kv;
     kv.pool = c->pool; kv.ptab = c->ptab; kv.max_pages = c->pages_per_seq; kv.n_layer = 1;
+    kv.n_pages = c->n_seqs * c->pages_per_seq;
     const float scale = 1.0f / sqrtf((float)kHeadDim);
     attention_decode(n, q, rows, kv, 0, scale, out, -1, ActQ(), st);
     KCK(cudaGetLastError());
