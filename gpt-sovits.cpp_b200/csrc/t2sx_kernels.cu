@@ -688,9 +688,11 @@ __global__ void __launch_bounds__(32 * HPC) k_attn_decode(const uint16_t* __rest
     pdl_wait();
     __shared__ AbsMax s_am[8];
     __shared__ float s_is;
-    const int r = blockIdx.x;
+    // CTAs in (row, head group) order, head group fastest: the CTAs of one row run together and
+    // share the address translations of its pages
+    const int r = blockIdx.x / (kHeads / HPC), hg = blockIdx.x % (kHeads / HPC);
     const int warp = threadIdx.x >> 5;
-    const int h = blockIdx.y * HPC + warp;
+    const int h = hg * HPC + warp;
     const int lane = threadIdx.x & 31;
     const int s = rows.slot[r];
     const int L = rows.L[r];
@@ -757,7 +759,7 @@ __global__ void __launch_bounds__(32 * HPC) k_attn_decode(const uint16_t* __rest
         }
         cp_wait<0>();
     }
-    attn_finish<HPC>(st, r, blockIdx.y, warp, lane, out, qtype, qo, s_am, &s_is);
+    attn_finish<HPC>(st, r, hg, warp, lane, out, qtype, qo, s_am, &s_is);
 }
 
 // Dynamic shared memory of the small-batch (PIPE) attention variant: the cp.async ring plus the
@@ -778,17 +780,17 @@ void attention_decode(int T, const uint16_t* q16, Rows rows, KVView kv, int laye
     // a Q8_K output block spans eight heads, so that format needs eight heads per CTA; otherwise
     // small batches spread the heads over more CTAs
     if (qtype == W_Q4_K && T < 64) {
-        launch_k((k_attn_decode<8, true>), dim3(dim3(T, kHeads / 8)), dim3(256), attn_pipe_smem<8>(kv), st, q16, rows, kv, layer, scale, out, qtype, qo);
+        launch_k((k_attn_decode<8, true>), dim3(T * (kHeads / 8)), dim3(256), attn_pipe_smem<8>(kv), st, q16, rows, kv, layer, scale, out, qtype, qo);
     } else if (qtype == W_Q4_K) {
         // many rows: four heads per CTA with an f32 row, then the Q8_K conversion as its own pass
         // (eight-head CTAs that convert in place wait on two CTA barriers per row: 8.65 -> 8.39 ms
         // for the 2048-row decode step)
-        launch_k((k_attn_decode<4, false>), dim3(dim3(T, kHeads / 4)), dim3(128), 0, st, q16, rows, kv, layer, scale, out, -1, qo);
+        launch_k((k_attn_decode<4, false>), dim3(T * (kHeads / 4)), dim3(128), 0, st, q16, rows, kv, layer, scale, out, -1, qo);
         quantize_act(W_Q4_K, out, T, kD, qo, st);
     } else if (T < 64) {
-        launch_k((k_attn_decode<2, true>), dim3(dim3(T, kHeads / 2)), dim3(64), attn_pipe_smem<2>(kv), st, q16, rows, kv, layer, scale, out, qtype, qo);
+        launch_k((k_attn_decode<2, true>), dim3(T * (kHeads / 2)), dim3(64), attn_pipe_smem<2>(kv), st, q16, rows, kv, layer, scale, out, qtype, qo);
     } else {
-        launch_k((k_attn_decode<4, false>), dim3(dim3(T, kHeads / 4)), dim3(128), 0, st, q16, rows, kv, layer, scale, out, qtype, qo);
+        launch_k((k_attn_decode<4, false>), dim3(T * (kHeads / 4)), dim3(128), 0, st, q16, rows, kv, layer, scale, out, qtype, qo);
     }
 }
 
