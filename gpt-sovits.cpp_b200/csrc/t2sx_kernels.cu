@@ -79,26 +79,66 @@ __global__ void k_quant_q8_K(const float* __restrict__ x, int64_t nblk, int8_t* 
 // dot type of a weight format with the same rules as the k_quant_* kernels.  wtype < 0 or F32:
 // nothing to write (an F32 matmul reads the f32 row itself).
 __device__ void quant_row512_strided(const float (&y)[kD / 32], int lane, int wtype, const ActQ& o, size_t row) {
+    // The blocks' warp reductions run side by side (a max, a first-index |x| max and integer sums
+    // do not depend on the merge order), so their shuffles overlap instead of running block by block.
     if (wtype == W_Q8_0 || wtype == W_Q4_0) {
+        float a[kD / 32];
 #pragma unroll
-        for (int t = 0; t < kD / 32; ++t)
-            o.q[row * kD + 32 * t + lane] = (int8_t)q8_0_lane(y[t], o.d + row * (kD / 32) + t, lane);
+        for (int t = 0; t < kD / 32; ++t) a[t] = fabsf(y[t]);
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1)
+#pragma unroll
+            for (int t = 0; t < kD / 32; ++t) a[t] = fmaxf(a[t], __shfl_xor_sync(0xffffffffu, a[t], off));
+#pragma unroll
+        for (int t = 0; t < kD / 32; ++t) {
+            // the rule of q8_0_lane (x86 AVX2 quantize_row_q8_0): d = amax/127 as f16, q = rint(v * 127/amax)
+            const float dd = __fdiv_rn(a[t], 127.0f);
+            const float id = (a[t] != 0.0f) ? __fdiv_rn(127.0f, a[t]) : 0.0f;
+            float r = rintf(__fmul_rn(y[t], id));
+            r = fminf(fmaxf(r, -128.0f), 127.0f);
+            o.q[row * kD + 32 * t + lane] = (int8_t)(int)r;
+            if (lane == 0) o.d[row * (kD / 32) + t] = __half2float(__float2half_rn(dd));
+        }
     } else if (wtype == W_Q4_K) {
+        constexpr int NB = kD / 256;
+        AbsMax am[NB];
 #pragma unroll
-        for (int B = 0; B < kD / 256; ++B) {
-            AbsMax am{0.0f, 0.0f, 0x7fffffff};
+        for (int B = 0; B < NB; ++B) {
+            am[B] = AbsMax{0.0f, 0.0f, 0x7fffffff};
 #pragma unroll
-            for (int k = 0; k < 8; ++k) absmax_take(am, y[8 * B + k], lane + 32 * k);
-            am = absmax_warp(am);
-            const float iscale = q8k_iscale(am);
-            if (lane == 0) o.d[row * (kD / 256) + B] = q8k_d(iscale);
+            for (int k = 0; k < 8; ++k) absmax_take(am[B], y[8 * B + k], lane + 32 * k);
+        }
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1)
+#pragma unroll
+            for (int B = 0; B < NB; ++B) {
+                AbsMax w;
+                w.a = __shfl_xor_sync(0xffffffffu, am[B].a, off);
+                w.m = __shfl_xor_sync(0xffffffffu, am[B].m, off);
+                w.i = __shfl_xor_sync(0xffffffffu, am[B].i, off);
+                absmax_merge(am[B], w);
+            }
+        int qv[kD / 32];
+#pragma unroll
+        for (int B = 0; B < NB; ++B) {
+            const float iscale = q8k_iscale(am[B]);
+            if (lane == 0) o.d[row * NB + B] = q8k_d(iscale);
 #pragma unroll
             for (int k = 0; k < 8; ++k) {
-                const int qv = q8k_q(iscale, y[8 * B + k]);
-                o.q[row * kD + 256 * B + 32 * k + lane] = (int8_t)qv;
-                const int sum = warp_sum_i(qv);
-                if (lane == 0) o.bs[row * (kD / 32) + 8 * B + k] = sum;
+                qv[8 * B + k] = q8k_q(iscale, y[8 * B + k]);
+                o.q[row * kD + 256 * B + 32 * k + lane] = (int8_t)qv[8 * B + k];
             }
+        }
+        int sum[kD / 32];
+#pragma unroll
+        for (int t = 0; t < kD / 32; ++t) sum[t] = qv[t];
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1)
+#pragma unroll
+            for (int t = 0; t < kD / 32; ++t) sum[t] += __shfl_xor_sync(0xffffffffu, sum[t], off);
+        if (lane == 0) {
+#pragma unroll
+            for (int t = 0; t < kD / 32; ++t) o.bs[row * (kD / 32) + t] = sum[t];
         }
     } else if (wtype == W_F16) {
 #pragma unroll
