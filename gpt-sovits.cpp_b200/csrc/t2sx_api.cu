@@ -560,6 +560,9 @@ struct Work {
     int8_t* aq;
     float* ad;
     int32_t *abs, *row_slot, *row_pos, *row_L, *tok, *lastrow, *greedy;
+    int2* grp;          // prefill row groups of the pass (first row, rows): consecutive rows of one slot
+    int n_grp = 0;      // groups of the current pass (0: the per-row attention kernels only)
+    int grp_row0 = 0;   // first row covered by the groups
 };
 
 static size_t work_bytes(int R, int V, int ff) {
@@ -570,6 +573,7 @@ static size_t work_bytes(int R, int V, int ff) {
     add((size_t)R * kD * 2); add((size_t)R * ff * 2); add((size_t)R * ff); add((size_t)R * (ff / 32) * 4);
     add((size_t)R * (ff / 32) * 4);
     for (int i = 0; i < 6; ++i) add((size_t)R * 4);
+    add((size_t)R * 8);
     return b;
 }
 
@@ -591,6 +595,7 @@ static int work_alloc(Work& w, int R, int V, int ff) {
     w.row_slot = (int32_t*)take((size_t)R * 4); w.row_pos = (int32_t*)take((size_t)R * 4);
     w.row_L = (int32_t*)take((size_t)R * 4); w.tok = (int32_t*)take((size_t)R * 4); w.lastrow = (int32_t*)take((size_t)R * 4);
     w.greedy = (int32_t*)take((size_t)R * 4);
+    w.grp = (int2*)take((size_t)R * 8);
     w.cap = R;
     return T2SX_OK;
 }
@@ -677,6 +682,24 @@ static int tail_rows() {
     return v;
 }
 
+// Prefill row groups of rows [row0, T) (rs = slot of each row): up to 16 consecutive rows of one
+// slot each, uploaded to w.grp.  Fewer than 64 such rows: no groups (the per-row kernels serve).
+static int set_row_groups(t2sx_session* s, Work& w, int T, int row0, const std::vector<int32_t>& rs) {
+    w.n_grp = 0;
+    w.grp_row0 = row0;
+    if (T - row0 < 64) return T2SX_OK;
+    std::vector<int2> g;
+    for (int r = row0; r < T;) {
+        int n = 1;
+        while (r + n < T && n < 16 && rs[r + n] == rs[r]) ++n;
+        g.push_back(make_int2(r, n));
+        r += n;
+    }
+    CK(cudaMemcpyAsync(w.grp, g.data(), g.size() * sizeof(int2), cudaMemcpyHostToDevice, s->st));
+    w.n_grp = (int)g.size();
+    return T2SX_OK;
+}
+
 static void run_layers(t2sx_session* s, Work& w, int T, bool decode, int final_qtype) {
     const t2sx_model* m = s->m;
     Rows rows = rows_of(s, w);
@@ -696,7 +719,7 @@ static void run_layers(t2sx_session* s, Work& w, int T, bool decode, int final_q
         e_qkv.qkv = &qs;
         matmul(L.qkv, act_for(w, w.x), T, L.qkv_b, 0, nullptr, s->st, e_qkv);
         // decode and prefill rows alike: the row attends to positions [0, L) of its slot
-        attention_decode(T, w.q16, rows, kv, l, kAttnScale, w.attn, L.out.type, act_of(w), s->st);
+        attention_rows(T, w.grp_row0, w.grp, w.n_grp, w.q16, rows, kv, l, kAttnScale, w.attn, L.out.type, act_of(w), s->st);
         if (small) {
             Tail t1;
             t1.kind = 1; t1.resid = w.x; t1.g = L.ln1_w; t1.beta = L.ln1_b; t1.eps = 1e-5f; t1.y_out = w.ln1;
@@ -1000,7 +1023,9 @@ extern "C" int t2sx_prefill(t2sx_session* s, int32_t n, const int32_t* slots, co
             ActQ a0 = act_of(w);
             quantize_act(m->layers[0].qkv.type, w.x, T, kD, a0, s->st);
         }
+        if ((rc = set_row_groups(s, w, T, 0, rs))) return rc;
         run_layers(s, w, T, false, -1);
+        w.n_grp = 0;
         // sampler on each slot's last row
         gather_rows(ns, w.x, w.lastrow, kD, w.xl, s->st);
         ActQ a = act_for(w, w.xl);
@@ -1261,7 +1286,9 @@ extern "C" int t2sx_flex_step(t2sx_session* s, int32_t n_dec, const int32_t* dec
         ActQ a0 = act_of(w);
         quantize_act(m->layers[0].qkv.type, w.x, T, kD, a0, s->st);
     }
+    if ((rc = set_row_groups(s, w, T, n_dec, rs))) return rc;
     run_layers(s, w, T, false, -1);
+    w.n_grp = 0;
     gather_rows(ns, w.x, w.lastrow, kD, w.xl, s->st);
     ActQ a = act_for(w, w.xl);
     quantize_act(m->lm_head.type, w.xl, ns, kD, a, s->st);

@@ -802,6 +802,89 @@ __global__ void __launch_bounds__(32 * HPC) k_attn_decode(const uint16_t* __rest
     attn_finish<HPC>(st, r, hg, warp, lane, out, qtype, qo, s_am, &s_is);
 }
 
+// Prefill attention: a CTA takes a group of up to 16 consecutive rows of one slot (the rows of a
+// prompt) and one head, one warp per row.  The group's K/V are staged in shared memory a page (64
+// positions) at a time, double-buffered with cp.async, and every warp folds them with the decode
+// kernel's lane order (lane l: positions l, l + 32, ...; page p gives its steps 2p and 2p + 1), so
+// the K/V of a prompt are read once per 16 rows instead of once per row.  Staged 16-byte chunks
+// are swizzled by position so that the lanes' reads of one chunk hit distinct banks.  f32 rows out.
+// (Staging f32 instead, converted once for all rows, was slower: twice the shared-memory reads.)
+__global__ void __launch_bounds__(512, 1) k_attn_group(const int2* __restrict__ groups, const uint16_t* __restrict__ q16,
+                                                       Rows rows, KVView kv, int layer, float scale, float* __restrict__ out) {
+    pdl_trigger();
+    pdl_wait();
+    __shared__ __align__(16) uint8_t sm[2][2][kPage * kHeadDim * 2];   // [buffer][K|V][64 positions x 64 B]
+    __shared__ int s_lmax;
+    const int2 gr = groups[blockIdx.x >> 4];   // (first row, rows)
+    const int h = blockIdx.x & 15;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const bool active = warp < gr.y;
+    const int r = gr.x + warp;
+    const int L = active ? rows.L[r] : 0;
+    if (threadIdx.x == 0) s_lmax = 0;
+    __syncthreads();
+    if (lane == 0 && active) atomicMax(&s_lmax, L);
+    __syncthreads();
+    const int Lmax = s_lmax;
+    const int32_t* pt = kv.ptab + (size_t)rows.slot[gr.x] * kv.max_pages;
+    float q[kHeadDim];
+    if (active) load_row32(q16 + (size_t)r * kD + h * kHeadDim, q);
+    AttnState st;
+    st_empty(st);
+    const int npg = (Lmax + kPage - 1) / kPage;
+    // thread t copies 16 bytes: K or V (t / 256), position (t / 4) % 64, chunk t % 4
+    const int cw = threadIdx.x >> 8, cp = (threadIdx.x >> 2) & 63, cc = threadIdx.x & 3;
+    const int coff = cp * 64 + ((cc ^ ((cp >> 1) & 3)) << 4);
+    auto stage = [&](int pg, int buf) {
+        const uint16_t* src = kv.pool + kv_off(kv, pt[pg], layer, cw, h, cp) + cc * 8;
+        cp_async16(&sm[buf][cw][coff], src, pg * kPage + cp < Lmax);
+        cp_commit();
+    };
+    if (npg > 0) stage(0, 0);
+    const int sw = (lane >> 1) & 3;   // the swizzle of positions lane and lane + 32
+    for (int pg = 0; pg < npg; ++pg) {
+        if (pg + 1 < npg) stage(pg + 1, (pg + 1) & 1);
+        else cp_commit();
+        cp_wait<1>();
+        __syncthreads();
+        const int buf = pg & 1;
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+            const int p = half * 32 + lane;
+            if (pg * kPage + p < L) {
+                uint4 kr[4], vr[4];
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    kr[c] = *reinterpret_cast<const uint4*>(&sm[buf][0][p * 64 + ((c ^ sw) << 4)]);
+                    vr[c] = *reinterpret_cast<const uint4*>(&sm[buf][1][p * 64 + ((c ^ sw) << 4)]);
+                }
+                float k32[kHeadDim], v32[kHeadDim];
+                unpack_row32(kr, k32);
+                unpack_row32(vr, v32);
+                st_update(st, __fmul_rn(dot32(q, k32), scale), v32);
+            }
+        }
+        __syncthreads();   // this buffer is refilled in the next step
+    }
+    cp_wait<0>();
+    if (active) attn_finish<1>(st, r, h, 0, lane, out, -1, ActQ(), nullptr, nullptr);
+}
+
+// Attention of a pass whose rows [row0, T) are prefill rows grouped by `groups` (device, n_groups
+// entries of (first row, rows), consecutive rows of one slot): rows [0, row0) by the per-row
+// kernels, the groups by k_attn_group; the rows are then converted to the out-projection's dot
+// type.  n_groups == 0: attention_decode.
+void attention_rows(int T, int row0, const int2* groups, int n_groups, const uint16_t* q16, Rows rows, KVView kv, int layer,
+                    float scale, float* out, int qtype, ActQ qo, cudaStream_t st) {
+    if (n_groups <= 0 || !groups) {
+        attention_decode(T, q16, rows, kv, layer, scale, out, qtype, qo, st);
+        return;
+    }
+    if (row0 > 0) attention_decode(row0, q16, rows, kv, layer, scale, out, -1, qo, st);
+    launch_k(k_attn_group, dim3(n_groups * kHeads), dim3(512), 0, st, groups, q16, rows, kv, layer, scale, out);
+    if (qtype >= 0 && qtype != W_F32) quantize_act(qtype, out, T, kD, qo, st);
+}
+
 // Dynamic shared memory of the small-batch (PIPE) attention variant: the cp.async ring plus the
 // row's page numbers; the kernel's limit is raised once.
 template <int HPC>

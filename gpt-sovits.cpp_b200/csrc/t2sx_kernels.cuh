@@ -134,6 +134,8 @@ void embed_decode(int T, const int32_t* row_slot, const int32_t* token_in, const
                   const float* pe, int pe_rows, float alpha, Rows rows, float* x, int qtype, ActQ qo, cudaStream_t st);
 void attention_decode(int T, const uint16_t* q16, Rows rows, KVView kv, int layer, float scale, float* out, int qtype,
                       ActQ qo, cudaStream_t st);
+void attention_rows(int T, int row0, const int2* groups, int n_groups, const uint16_t* q16, Rows rows, KVView kv, int layer,
+                    float scale, float* out, int qtype, ActQ qo, cudaStream_t st);
 void residual_layernorm(int T, const float* a, const float* b, const float* g, const float* beta, float eps,
                         float* y, int qtype, ActQ qo, cudaStream_t st);
 // Logit given to EOS when EOS is masked (finite, so the masked-lerp filters stay finite).

@@ -50,7 +50,7 @@ struct t2sx_kvcache {
     int32_t* err = nullptr;
     uint16_t* stage = nullptr;   // K then V rows of one write
     size_t stage_rows = 0;
-    int32_t* rows_mem = nullptr;  // slot [cap_rows] then L [cap_rows]
+    int32_t* rows_mem = nullptr;  // slot [cap_rows], L [cap_rows], groups [cap_rows] of int2
     size_t cap_rows = 0;
     cudaStream_t st = nullptr;
 };
@@ -141,7 +141,7 @@ static int kv_rows(t2sx_kvcache* c, int32_t n, const int32_t* seqs, const int32_
         cudaFree(c->rows_mem);
         c->rows_mem = nullptr;
         c->cap_rows = 0;
-        KCK(cudaMalloc(&c->rows_mem, (size_t)n * 2 * 4));
+        KCK(cudaMalloc(&c->rows_mem, (size_t)n * 4 * 4));   // slot, L, then up to n groups of (first row, rows)
         c->cap_rows = (size_t)n;
     }
     KCK(cudaMemcpyAsync(c->rows_mem, seqs, (size_t)n * 4, cudaMemcpyHostToDevice, st));
@@ -157,7 +157,7 @@ static int kv_rows(t2sx_kvcache* c, int32_t n, const int32_t* seqs, const int32_
 }
 
 static int kv_attn(t2sx_kvcache* c, int32_t n, const int32_t* seqs, const int32_t* lens, const uint16_t* q, float* out,
-                   void* stream) {
+                   void* stream, bool grouped) {
     if (!c || n <= 0 || !seqs || !lens || !q || !out) return t2sx_set_error(T2SX_ERR_INVALID, "attention: bad arguments");
     KCK(cudaSetDevice(c->device));
     cudaStream_t st = (cudaStream_t)stream;
@@ -168,18 +168,32 @@ static int kv_attn(t2sx_kvcache* c, int32_t n, const int32_t* seqs, const int32_
     kv.pool = c->pool; kv.ptab = c->ptab; kv.max_pages = c->pages_per_seq; kv.n_layer = 1;
     kv.n_pages = c->n_seqs * c->pages_per_seq;
     const float scale = 1.0f / sqrtf((float)kHeadDim);
-    attention_decode(n, q, rows, kv, 0, scale, out, -1, ActQ(), st);
+    int n_groups = 0;
+    if (grouped && n >= 64) {
+        // runs of up to 16 consecutive rows of one sequence (the rows of a prompt)
+        std::vector<int2> g;
+        for (int r = 0; r < n;) {
+            int k = 1;
+            while (r + k < n && k < 16 && seqs[r + k] == seqs[r]) ++k;
+            g.push_back(make_int2(r, k));
+            r += k;
+        }
+        KCK(cudaMemcpyAsync(c->rows_mem + 2 * c->cap_rows, g.data(), g.size() * sizeof(int2), cudaMemcpyHostToDevice, st));
+        n_groups = (int)g.size();
+    }
+    attention_rows(n, 0, reinterpret_cast<const int2*>(c->rows_mem + 2 * c->cap_rows), n_groups, q, rows, kv, 0, scale, out, -1,
+                   ActQ(), st);
     KCK(cudaGetLastError());
     return T2SX_OK;
 }
 
 extern "C" int t2sx_kvcache_attn_decode(t2sx_kvcache* c, int32_t n, const int32_t* seqs, const int32_t* lens,
                                         const uint16_t* q, float* out, void* stream) {
-    return kv_attn(c, n, seqs, lens, q, out, stream);
+    return kv_attn(c, n, seqs, lens, q, out, stream, false);
 }
 
 extern "C" int t2sx_kvcache_attn_prefill(t2sx_kvcache* c, int32_t n, const int32_t* seqs, const int32_t* lens,
                                          const uint16_t* q, float* out, void* stream) {
-    // the same computation: causal prefill rows differ only in their prefix lengths
-    return kv_attn(c, n, seqs, lens, q, out, stream);
+    // the same result as t2sx_kvcache_attn_decode; consecutive rows of one sequence share the staged K/V
+    return kv_attn(c, n, seqs, lens, q, out, stream, true);
 }

@@ -205,9 +205,10 @@ T2SX_API void t2sx_kvcache_free(t2sx_kvcache* c);
 T2SX_API int t2sx_kvcache_write(t2sx_kvcache* c, int32_t seq, int32_t pos0, int32_t len, const uint16_t* k,
                                 const uint16_t* v);
 /* Row r (q_dev f16 [n][512]) attends to positions [0, lens[r]) of sequence seqs[r] (host arrays);
- * out_dev f32 [n][512], with the kernel of the decode step and the prefill (32 position lanes per
- * head, butterfly merge).  The two entry points run the same computation; causal prefill rows
- * give each query its own prefix length. */
+ * out_dev f32 [n][512] (32 position lanes per head, butterfly merge).  The two entry points give
+ * the same result; the prefill one runs consecutive rows of one sequence (a prompt's rows, each
+ * with its own causal prefix length) together, reading their K/V once per 16 rows, as the
+ * session prefill does. */
 T2SX_API int t2sx_kvcache_attn_decode(t2sx_kvcache* c, int32_t n, const int32_t* seqs, const int32_t* lens,
                                       const uint16_t* q_dev, float* out_dev, void* stream);
 T2SX_API int t2sx_kvcache_attn_prefill(t2sx_kvcache* c, int32_t n, const int32_t* seqs, const int32_t* lens,

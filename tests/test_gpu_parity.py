@@ -318,6 +318,29 @@ def test_kvcache_prefill_causal(t2sx_mod, orc):
     c.close()
 
 
+def test_kvcache_prefill_grouped_rows(t2sx_mod, orc):
+    """Prompt rows in order (the grouped prefill kernel: up to 16 consecutive rows of a sequence
+    share the staged K/V), text rows with one common prefix followed by causal rows, prompts of
+    1, 15, 16, 17 and 300 rows, prefixes crossing pages: bit-exact to the oracle and to the
+    per-row entry point."""
+    _need_gpu()
+    n_seqs, max_len = 6, 400
+    rng, k, v = _kv_case(n_seqs, max_len, seed=34)
+    c = _kv_fill(t2sx_mod, k, v, np.full(n_seqs, max_len), chunks=2)
+    spec = [(0, 1, 0), (1, 15, 3), (2, 16, 0), (3, 17, 40), (4, 300, 120), (5, 70, 64)]   # (seq, rows, text rows)
+    seqs, lens = [], []
+    for s, nq, tt in spec:
+        for j in range(nq):
+            seqs.append(s); lens.append(tt if j < tt else j + 1 + 10)
+    seqs = np.array(seqs, dtype=np.int32); lens = np.minimum(np.array(lens, dtype=np.int32), max_len)
+    q16 = rng.standard_normal((len(seqs), 512), dtype=np.float32).astype(np.float16).view(np.uint16)
+    got = _kv_run(c, 1, seqs, lens, q16)
+    ref = orc.attn_rows(seqs, lens, q16, k, v)
+    assert same_bits(got, ref), f"{int((got != ref).sum())} mismatches"
+    assert same_bits(_kv_run(c, 0, seqs, lens, q16), got)
+    c.close()
+
+
 def test_kvcache_edge_lengths_and_errors(t2sx_mod, orc):
     """Length 1, exact page multiples, a single sequence repeated across rows, small batches
     (the pipelined decode variant), and host-side rejection of bad rows and writes."""
