@@ -178,21 +178,8 @@ __device__ __forceinline__ void tmem_ld3x8(uint32_t taddr, int (&v)[24]) {
           "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23])
         : "r"(taddr), "r"(taddr + (uint32_t)BN), "r"(taddr + (uint32_t)(2 * BN)));
 }
-// 8 consecutive 32-bit TMEM columns of this thread's lane (no wait)
-__device__ __forceinline__ void tmem_ld8(uint32_t taddr, int (&v)[8]) {
-    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];\n"
-                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
-                 : "r"(taddr));
-}
-__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory"); }
 // wait for this thread's TMEM loads, then pin the loaded registers after the wait (the compiler
 // must not read them earlier)
-template <int NR>
-__device__ __forceinline__ void tmem_wait_ld_regs(int (&v)[NR]) {
-    asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
-#pragma unroll
-    for (int i = 0; i < NR; ++i) asm volatile("" : "+r"(v[i]));
-}
 template <int NR>
 __device__ __forceinline__ void tmem_wait_ld_regs2(int (&v)[NR], int (&w)[NR]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
@@ -235,8 +222,6 @@ __device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
     return u2f(r);
 }
 
-// exact int -> float for |i| < 2^22 (block dots of Q8_0 / Q4_0 are below 2^19)
-__device__ __forceinline__ float i2f_small(int i) { return __fsub_rn(__int_as_float(0x4B400000 + i), 12582912.0f); }
 
 __global__ void __launch_bounds__(THREADS, 1)
 k_mm_tc_q4k(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
