@@ -414,18 +414,19 @@ def test_extract_latent_bit_exact(t2sx_mod, orc, fmt):
     s.close(); m_gpu.close(); m_orc.close()
 
 
-@pytest.mark.parametrize("rp", [1.0, 1.35])
-def test_flex_step_mixed_plan_bit_exact(t2sx_mod, orc, rp):
+@pytest.mark.parametrize("rp,refill", [(1.0, (25, 25, 44)), (1.35, (25, 25, 44)), (1.0, (60, 70, 45))],
+                         ids=["greedy-50rows", "penalty-50rows", "greedy-130rows"])
+def test_flex_step_mixed_plan_bit_exact(t2sx_mod, orc, rp, refill):
     """t2sx_flex_step (session.cpp:461-859 with decode and prefill slots in one plan): a decode of a
     subset of the active slots, then a released slot prefilled in the same pass as the others'
     decode step, then ordinary decode steps.  Tokens, logits and the refilled slot's KV equal the
-    oracle's separate decode and prefill; the repetition penalty applies to the decode rows only."""
+    oracle's separate decode and prefill; the repetition penalty applies to the decode rows only.
+    A 130-row refill runs its rows on the grouped prefill attention, the decode rows per row."""
     _need_gpu()
     import synth
     path = synth.ensure_gguf("q4_k", 7, n_layer=2)
     m_gpu, m_orc = t2sx_mod.Model(path), orc.Model(path)
     lengths = [(30, 20, 41), (12, 40, 42), (50, 5, 43)]
-    refill = (25, 25, 44)
     n, cap, V = len(lengths), 160, m_orc.vocab
     s_gpu = t2sx_mod.Session(m_gpu, n, cap, eos_mask=True, repetition_penalty=rp)
     s_orc = orc.Session(m_orc, n, cap)
