@@ -897,6 +897,16 @@ static size_t attn_pipe_smem(const KVView& kv) {
     return (size_t)(16 / HPC) * 8 * (32 * HPC) * 16 + (size_t)kv.max_pages * 4;
 }
 
+// Rows below which the decode attention runs one head per CTA with 16 positions per lane in flight
+// (T2SX_ATTN_PIPE1_ROWS; bs=1 step 0.940 -> 0.918 ms).
+static int pipe1_rows() {
+    static const int v = [] {
+        const char* e = getenv("T2SX_ATTN_PIPE1_ROWS");
+        return e ? atoi(e) : 4;
+    }();
+    return v;
+}
+
 void attention_decode(int T, const uint16_t* q16, Rows rows, KVView kv, int layer, float scale, float* out, int qtype,
                       ActQ qo, cudaStream_t st) {
     if (T <= 0) return;
@@ -910,6 +920,9 @@ void attention_decode(int T, const uint16_t* q16, Rows rows, KVView kv, int laye
         // for the 2048-row decode step)
         launch_k((k_attn_decode<4, false>), dim3(T * (kHeads / 4)), dim3(128), 0, st, q16, rows, kv, layer, scale, out, -1, qo);
         quantize_act(W_Q4_K, out, T, kD, qo, st);
+    } else if (T < pipe1_rows()) {
+        // very few rows: one head per CTA, 16 positions per lane in flight
+        launch_k((k_attn_decode<1, true>), dim3(T * kHeads), dim3(32), attn_pipe_smem<1>(kv), st, q16, rows, kv, layer, scale, out, qtype, qo);
     } else if (T < 64) {
         launch_k((k_attn_decode<2, true>), dim3(T * (kHeads / 2)), dim3(64), attn_pipe_smem<2>(kv), st, q16, rows, kv, layer, scale, out, qtype, qo);
     } else {
