@@ -327,18 +327,19 @@ bool matmul_mma(const DevW& W, const ActQ& a, int M, const float* bias, int relu
     return false;
 }
 
-// Narrow tiles (32 weight rows x 16 or 32 activation rows, 2 warps per CTA) for few activation
-// rows: the whole matmul then spreads over N/32 CTAs, and the activation tile is staged once per
-// CTA in shared memory instead of being re-read per weight row.  With few CTAs per SM the K loop
-// is latency-bound, so the ring keeps 5 stages (640 elements of K) in flight.
+// Narrow tiles (32 weight rows x 16 activation rows, 2 warps per CTA) for few activation rows:
+// the matmul spreads over N/32 CTAs along the weight rows and ceil(M/16) along the activation
+// rows, and the activation tile is staged once per CTA in shared memory instead of being re-read
+// per weight row.  16-row tiles also for 17-32 rows: the 512-wide projections then run on 32
+// CTAs instead of 16 (32 sessions: 1.66 -> 1.44 ms per decode step).  With few CTAs per SM the
+// K loop is latency-bound, so the ring keeps 5 stages (640 elements of K) in flight.
 bool matmul_mma_narrow(const DevW& W, const ActQ& a, int M, const float* bias, int relu, float* y, const QKVStore* qkv,
                        cudaStream_t st) {
     if (W.K % (32 * KB) || M > 32) return false;
-    const bool m16 = M <= 16;
     switch (W.type) {
-        case W_Q8_0: m16 ? launch_mma<W_Q8_0, 1, 1, 6>(W, a, M, bias, relu, y, qkv, st) : launch_mma<W_Q8_0, 2, 1, 6>(W, a, M, bias, relu, y, qkv, st); return true;
-        case W_Q4_0: m16 ? launch_mma<W_Q4_0, 1, 1, 6>(W, a, M, bias, relu, y, qkv, st) : launch_mma<W_Q4_0, 2, 1, 6>(W, a, M, bias, relu, y, qkv, st); return true;
-        case W_Q4_K: m16 ? launch_mma<W_Q4_K, 1, 1, 6>(W, a, M, bias, relu, y, qkv, st) : launch_mma<W_Q4_K, 2, 1, 6>(W, a, M, bias, relu, y, qkv, st); return true;
+        case W_Q8_0: launch_mma<W_Q8_0, 1, 1, 6>(W, a, M, bias, relu, y, qkv, st); return true;
+        case W_Q4_0: launch_mma<W_Q4_0, 1, 1, 6>(W, a, M, bias, relu, y, qkv, st); return true;
+        case W_Q4_K: launch_mma<W_Q4_K, 1, 1, 6>(W, a, M, bias, relu, y, qkv, st); return true;
     }
     return false;
 }
