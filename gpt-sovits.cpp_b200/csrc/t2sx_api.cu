@@ -728,13 +728,12 @@ static void run_layers(t2sx_session* s, Work& w, int T, bool decode, int final_q
             e1.tail = &t1;
             matmul(L.out, act_for(w, w.attn), T, L.out_b, 0, w.o, s->st, e1);
             matmul(L.up, act_for(w, w.ln1), T, L.up_b, 1, w.h, s->st);
-            ActQ ah = act_of(w);
-            quantize_act(L.down.type, w.h, T, s->ff, ah, s->st);
             Tail t3;
             t3.kind = 1; t3.resid = w.ln1; t3.g = L.ln2_w; t3.beta = L.ln2_b; t3.eps = 1e-5f; t3.y_out = w.x;
             t3.qtype = next_q; t3.qo = act_of(w); t3.counter = s->tail_ctr;
             Epi e3;
             e3.tail = &t3;
+            e3.quant_in = true;   // the FFN rows' conversion (Q8_0: inside the down projection)
             matmul(L.down, act_for(w, w.h), T, L.down_b, 0, w.f, s->st, e3);
         } else {
             matmul(L.out, act_for(w, w.attn), T, L.out_b, 0, w.o, s->st);
@@ -1453,6 +1452,8 @@ struct t2sx_weight {
 extern "C" int t2sx_weight_create(int32_t device, int32_t type, const void* host_bytes, int64_t N, int64_t K, t2sx_weight** out) {
     if (!host_bytes || !out || N <= 0 || K <= 0 || row_bytes(type, K) < 0) return fail(T2SX_ERR_INVALID, "t2sx_weight_create: bad arguments");
     if (type == W_Q4_K ? K % 256 : K % 32) return fail(T2SX_ERR_INVALID, "K not a multiple of the block size");
+    // the few-row kernel keeps one row's 32-element block sums in shared memory (64 of them)
+    if (K > 2048) return fail(T2SX_ERR_INVALID, "t2sx_weight_create: K above 2048 is not supported");
     CK(cudaSetDevice(device));
     Arena ar;
     WOff wo;

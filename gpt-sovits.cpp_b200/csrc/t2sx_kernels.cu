@@ -212,13 +212,37 @@ __device__ __forceinline__ void qkv_store(const QKVStore& e, int m, int n, float
     e.kv.pool[kv_off(e.kv, page, e.layer, which, j / kHeadDim, pos % kPage) + (j % kHeadDim)] = h;
 }
 
+// qkv_store in two steps, for kernels that look the destination up ahead of the dot products:
+// qkv_dest gives row m's cache page and position ((-1, 0): no K/V store, as qkv_store skips a
+// position outside the slot's capacity).  Its capacity and page-table loads are independent
+// (the page-table index is clamped), so they cost one round trip after the position and slot.
+__device__ __forceinline__ int2 qkv_dest(const QKVStore& e, int pos, int s) {
+    const int pg = min(max(pos, 0) / kPage, e.kv.max_pages - 1);
+    const int cap = e.rows.cap[s];
+    const int page = e.kv.ptab[(size_t)s * e.kv.max_pages + pg];
+    return (pos < 0 || pos >= cap) ? make_int2(-1, 0) : make_int2(page, pos);
+}
+
+__device__ __forceinline__ void qkv_store_at(const QKVStore& e, int m, int n, float v, int2 dst) {
+    const uint16_t h = f2h(v);
+    if (n < kD) { e.q16[(size_t)m * kD + n] = h; return; }
+    if (dst.x < 0) return;
+    const int which = (n - kD) / kD, j = (n - kD) % kD;
+    e.kv.pool[kv_off(e.kv, dst.x, e.layer, which, j / kHeadDim, dst.y % kPage) + (j % kHeadDim)] = h;
+}
+
 // y = LN(a + b) * g + beta for one row held by one warp (ggml_norm + mul + add,
 // block.cpp:615-619 / :630-634): lane l sums elements l, l+32, ... in double, the lanes combine
 // by an xor butterfly.  `b_l2` reads b through L2 (written by other CTAs of the same kernel).
 __device__ void ln_row_warp(const float* __restrict__ a, const float* __restrict__ b, bool b_l2,
                             const float* __restrict__ g, const float* __restrict__ beta, float eps, int lane,
                             float (&out)[kD / 32]) {
-    float v[kD / 32];
+    float v[kD / 32], gv[kD / 32], bv[kD / 32];
+#pragma unroll
+    for (int t = 0; t < kD / 32; ++t) {   // loaded with the row: one round trip, not one after the sums
+        gv[t] = g[lane + 32 * t];
+        bv[t] = beta[lane + 32 * t];
+    }
     double s = 0.0;
 #pragma unroll
     for (int t = 0; t < kD / 32; ++t) {
@@ -240,10 +264,7 @@ __device__ void ln_row_warp(const float* __restrict__ a, const float* __restrict
     const float var = __double2float_rn(__ddiv_rn(s2, (double)kD));
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
 #pragma unroll
-    for (int t = 0; t < kD / 32; ++t) {
-        const int i = lane + 32 * t;
-        out[t] = __fadd_rn(__fmul_rn(__fmul_rn(v[t], scale), g[i]), beta[i]);
-    }
+    for (int t = 0; t < kD / 32; ++t) out[t] = __fadd_rn(__fmul_rn(__fmul_rn(v[t], scale), gv[t]), bv[t]);
 }
 
 // Work of the last CTA of a small-M matmul, once every CTA's output is written: residual +
@@ -292,11 +313,35 @@ __device__ __forceinline__ void tail_if_last(const Tail& tl, const float* y, int
 // Small-M kernel: one warp per weight row; lanes compute block partials (phase A) into shared
 // memory, then lane m runs the ordered chain of row m (phase B).  Optional epilogues: QKV store
 // (Q and the K/V cache append) and a last-CTA tail.
+// Latency: the launch is a chain of memory round trips, so every load that does not depend on a
+// dot product is issued with the weights: the bias, the K/V destination's position and slot,
+// and (up to kDDM rows) the block scales, whose products phase A stages in shared memory so
+// that phase B's chain reads no global memory.  The arithmetic and its order are unchanged.
+constexpr int kDDM = 8;
+
+__device__ __forceinline__ float epi_v(float acc, bool has_bias, float bv, int relu) {
+    float v = has_bias ? __fadd_rn(acc, bv) : acc;
+    if (relu) v = (v > 0.0f) ? v : 0.0f;
+    return v;
+}
+
 template <int WT>
 __device__ __forceinline__ void mm_small_row(const DevW& W, const ActQ& A, int M, const float* __restrict__ bias, int relu,
                                              float* __restrict__ y, const QKVStore* qkv, int (&s_a)[kSmallM][64],
-                                             int (&s_m)[kSmallM][8], int n, int lane) {
+                                             int (&s_m)[kSmallM][8], float (&s_dd)[kDDM][64], int n, int lane,
+                                             bool fq = false) {
     const int K = W.K;
+    const bool own = lane < M;
+    const float bv = (bias && own) ? bias[n] : 0.0f;
+    const bool kvcol = qkv && own && n >= kD;
+    int kpos = 0, kslot = 0;
+    if (kvcol) { kpos = qkv->rows.pos[lane]; kslot = qkv->rows.slot[lane]; }
+    const bool stage_dd = M <= kDDM;
+    auto finish = [&](float acc) {
+        const float v_ = epi_v(acc, bias != nullptr, bv, relu);
+        if (qkv) qkv_store_at(*qkv, lane, n, v_, kvcol ? qkv_dest(*qkv, kpos, kslot) : make_int2(-1, 0));
+        else y[(size_t)lane * W.N + n] = v_;
+    };
     if (WT == W_Q8_0 || WT == W_Q4_0) {
         const int nb = K / 32;
         for (int b = lane; b < nb; b += 32) {
@@ -309,20 +354,34 @@ __device__ __forceinline__ void mm_small_row(const DevW& W, const ActQ& A, int M
                 w0 = make_int4(q4lo(raw.x), q4lo(raw.y), q4lo(raw.z), q4lo(raw.w));
                 w1 = make_int4(q4hi(raw.x), q4hi(raw.y), q4hi(raw.z), q4hi(raw.w));
             }
+            const float wd = W.d[(size_t)n * nb + b];
             for (int m = 0; m < M; ++m) {
-                const int4* xp = reinterpret_cast<const int4*>(A.q + (size_t)m * K + b * 32);
-                s_a[m][b] = dp8(w0, w1, xp[0], xp[1]);
+                int4 x0, x1;
+                float ad;
+                if (fq) {   // the f32 rows quantised to Q8_0 here (then stage_dd holds)
+                    q8_0_block_thread(A.f + (size_t)m * K + b * 32, x0, x1, ad);
+                } else {
+                    const int4* xp = reinterpret_cast<const int4*>(A.q + (size_t)m * K + b * 32);
+                    x0 = xp[0]; x1 = xp[1];
+                    ad = stage_dd ? A.d[(size_t)m * nb + b] : 0.0f;
+                }
+                s_a[m][b] = dp8(w0, w1, x0, x1);
+                if (stage_dd) s_dd[m][b] = __fmul_rn(wd, ad);
             }
         }
         __syncwarp();
-        if (lane < M) {
+        if (own) {
             const int m = lane;
             float acc = 0.0f;
-            for (int b = 0; b < nb; ++b) {
-                const float dd = __fmul_rn(W.d[(size_t)n * nb + b], A.d[(size_t)m * nb + b]);
-                acc = __fmaf_rn(dd, (float)s_a[m][b], acc);
+            if (stage_dd) {
+                for (int b = 0; b < nb; ++b) acc = __fmaf_rn(s_dd[m][b], (float)s_a[m][b], acc);
+            } else {
+                for (int b = 0; b < nb; ++b) {
+                    const float dd = __fmul_rn(W.d[(size_t)n * nb + b], A.d[(size_t)m * nb + b]);
+                    acc = __fmaf_rn(dd, (float)s_a[m][b], acc);
+                }
             }
-            { const float v_ = epi(acc, bias, n, relu); if (qkv) qkv_store(*qkv, m, n, v_); else y[(size_t)m * W.N + n] = v_; }
+            finish(acc);
         }
     } else if (WT == W_Q4_K) {
         const int nsub = K / 32, nsb = K / 256;
@@ -332,6 +391,7 @@ __device__ __forceinline__ void mm_small_row(const DevW& W, const ActQ& A, int M
             const int sb = j >> 3, js = j & 7, c = js >> 1, hi = js & 1;
             int4 w0 = make_int4(0, 0, 0, 0), w1 = w0;
             int sc = 0, mn = 0;
+            float wd = 0.0f, wdm = 0.0f;
             if (act) {
                 const int4* wp = reinterpret_cast<const int4*>(W.q4 + ((size_t)n * nsb + sb) * 128 + 32 * c);
                 const int4 r0 = wp[0], r1 = wp[1];
@@ -345,9 +405,14 @@ __device__ __forceinline__ void mm_small_row(const DevW& W, const ActQ& A, int M
                 const uint8_t* scm = W.scm + ((size_t)n * nsb + sb) * 16;
                 sc = scm[js];
                 mn = scm[8 + js];
+                if (js == 0 && stage_dd) {
+                    wd = W.d[(size_t)n * nsb + sb];
+                    wdm = W.dmin[(size_t)n * nsb + sb];
+                }
             }
             for (int m = 0; m < M; ++m) {
                 int sa = 0, sm = 0;
+                const float dx = (act && js == 0 && stage_dd) ? A.d[(size_t)m * nsb + sb] : 0.0f;
                 if (act) {
                     const int4* xp = reinterpret_cast<const int4*>(A.q + (size_t)m * K + j * 32);
                     sa = sc * dp8(w0, w1, xp[0], xp[1]);
@@ -359,21 +424,34 @@ __device__ __forceinline__ void mm_small_row(const DevW& W, const ActQ& A, int M
                 sm += __shfl_xor_sync(0xffffffffu, sm, 1);
                 sm += __shfl_xor_sync(0xffffffffu, sm, 2);
                 sm += __shfl_xor_sync(0xffffffffu, sm, 4);
-                if (act && js == 0) { s_a[m][sb] = sa; s_m[m][sb] = sm; }
+                if (act && js == 0) {
+                    s_a[m][sb] = sa;
+                    s_m[m][sb] = sm;
+                    if (stage_dd) {
+                        s_dd[m][sb] = __fmul_rn(dx, wd);
+                        s_dd[m][8 + sb] = __fmul_rn(-dx, wdm);
+                    }
+                }
             }
         }
         __syncwarp();
-        if (lane < M) {
+        if (own) {
             const int m = lane;
             float acc_a = 0.0f, acc_m = 0.0f;
             for (int sb = 0; sb < nsb; ++sb) {
-                const float dx = A.d[(size_t)m * nsb + sb];
-                const float dd = __fmul_rn(dx, W.d[(size_t)n * nsb + sb]);
-                const float dm = __fmul_rn(-dx, W.dmin[(size_t)n * nsb + sb]);
+                float dd, dm;
+                if (stage_dd) {
+                    dd = s_dd[m][sb];
+                    dm = s_dd[m][8 + sb];
+                } else {
+                    const float dx = A.d[(size_t)m * nsb + sb];
+                    dd = __fmul_rn(dx, W.d[(size_t)n * nsb + sb]);
+                    dm = __fmul_rn(-dx, W.dmin[(size_t)n * nsb + sb]);
+                }
                 acc_a = __fmaf_rn(dd, (float)s_a[m][sb], acc_a);
                 acc_m = __fmaf_rn(dm, (float)s_m[m][sb], acc_m);
             }
-            { const float v_ = epi(__fadd_rn(acc_a, acc_m), bias, n, relu); if (qkv) qkv_store(*qkv, m, n, v_); else y[(size_t)m * W.N + n] = v_; }
+            finish(__fadd_rn(acc_a, acc_m));
         }
     } else {  // F16 / F32
         const int nb = K / 32;
@@ -397,11 +475,11 @@ __device__ __forceinline__ void mm_small_row(const DevW& W, const ActQ& A, int M
             }
         }
         __syncwarp();
-        if (lane < M) {
+        if (own) {
             const int m = lane;
             float acc = 0.0f;
             for (int b = 0; b < nb; ++b) acc = __fadd_rn(acc, __int_as_float(s_a[m][b]));
-            { const float v_ = epi(acc, bias, n, relu); if (qkv) qkv_store(*qkv, m, n, v_); else y[(size_t)m * W.N + n] = v_; }
+            finish(acc);
         }
     }
 }
@@ -410,14 +488,20 @@ __device__ __forceinline__ void mm_small_row(const DevW& W, const ActQ& A, int M
 template <int WT>
 __global__ void __launch_bounds__(128) k_mm_small(DevW W, ActQ A, int M, const float* __restrict__ bias, int relu,
                                                   float* __restrict__ y, QKVStore qkv, int use_qkv, Tail tail,
-                                                  int use_tail) {
+                                                  int use_tail, int fq) {
     pdl_trigger();
     pdl_wait();
     __shared__ int s_a[4][kSmallM][64];
     __shared__ int s_m[4][kSmallM][8];
+    __shared__ float s_dd[4][kDDM][64];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n = blockIdx.x * 4 + warp;
-    if (n < W.N) mm_small_row<WT>(W, A, M, bias, relu, y, use_qkv ? &qkv : nullptr, s_a[warp], s_m[warp], n, lane);
+    if (n < W.N) {
+        if ((WT == W_Q8_0 || WT == W_Q4_0) && fq)
+            mm_small_row<WT>(W, A, M, bias, relu, y, use_qkv ? &qkv : nullptr, s_a[warp], s_m[warp], s_dd[warp], n, lane, true);
+        else
+            mm_small_row<WT>(W, A, M, bias, relu, y, use_qkv ? &qkv : nullptr, s_a[warp], s_m[warp], s_dd[warp], n, lane);
+    }
     if (use_tail) tail_if_last(tail, y, M, W.N);
 }
 
@@ -547,8 +631,14 @@ static int fp_tile_min_rows() {
     return v;
 }
 
-void matmul(const DevW& W, const ActQ& a, int M, const float* bias, int relu, float* y, cudaStream_t st, const Epi& e) {
+void matmul(const DevW& W, const ActQ& a_in, int M, const float* bias, int relu, float* y, cudaStream_t st, const Epi& e) {
     const bool quant = W.type == W_Q8_0 || W.type == W_Q4_0 || W.type == W_Q4_K;
+    ActQ a = a_in;
+    // fused input quantisation: the few-row kernel is the one that runs (no narrow or tensor
+    // tiles: M below their thresholds, or a tail), at most kDDM rows, 16-byte aligned rows
+    const bool fq = e.quant_in && (W.type == W_Q8_0 || W.type == W_Q4_0) && M <= kDDM &&
+                    (M < narrow_min_rows() || e.tail) && M < tc_min_rows() && (((uintptr_t)a.f) & 15) == 0;
+    if (e.quant_in && !fq) quantize_act(W.type, a.f, M, W.K, a, st);
     if (quant && M >= tc_min_rows() && matmul_tc(W, a, M, bias, relu, y, e.qkv, st)) return;
     if (quant && M > kSmallM && matmul_mma(W, a, M, bias, relu, y, e.qkv, st)) return;
     if (quant && M >= narrow_min_rows() && !(e.tail && M <= kSmallM) && matmul_mma_narrow(W, a, M, bias, relu, y, e.qkv, st))
@@ -586,13 +676,13 @@ void matmul(const DevW& W, const ActQ& a, int M, const float* bias, int relu, fl
             qq.q16 += (size_t)m0 * kD;
         }
         const int grid = (W.N + 3) / 4;
-        const int uq = e.qkv ? 1 : 0, ut = use_tail ? 1 : 0;
+        const int uq = e.qkv ? 1 : 0, ut = use_tail ? 1 : 0, ufq = fq ? 1 : 0;
         switch (W.type) {
-            case W_Q8_0: launch_k(k_mm_small<W_Q8_0>, dim3(grid), dim3(128), 0, st, W, as, mm, bias, relu, yy, qq, uq, tail, ut); break;
-            case W_Q4_0: launch_k(k_mm_small<W_Q4_0>, dim3(grid), dim3(128), 0, st, W, as, mm, bias, relu, yy, qq, uq, tail, ut); break;
-            case W_Q4_K: launch_k(k_mm_small<W_Q4_K>, dim3(grid), dim3(128), 0, st, W, as, mm, bias, relu, yy, qq, uq, tail, ut); break;
-            case W_F16: launch_k(k_mm_small<W_F16>, dim3(grid), dim3(128), 0, st, W, as, mm, bias, relu, yy, qq, uq, tail, ut); break;
-            default: launch_k(k_mm_small<W_F32>, dim3(grid), dim3(128), 0, st, W, as, mm, bias, relu, yy, qq, uq, tail, ut); break;
+            case W_Q8_0: launch_k(k_mm_small<W_Q8_0>, dim3(grid), dim3(128), 0, st, W, as, mm, bias, relu, yy, qq, uq, tail, ut, ufq); break;
+            case W_Q4_0: launch_k(k_mm_small<W_Q4_0>, dim3(grid), dim3(128), 0, st, W, as, mm, bias, relu, yy, qq, uq, tail, ut, ufq); break;
+            case W_Q4_K: launch_k(k_mm_small<W_Q4_K>, dim3(grid), dim3(128), 0, st, W, as, mm, bias, relu, yy, qq, uq, tail, ut, 0); break;
+            case W_F16: launch_k(k_mm_small<W_F16>, dim3(grid), dim3(128), 0, st, W, as, mm, bias, relu, yy, qq, uq, tail, ut, 0); break;
+            default: launch_k(k_mm_small<W_F32>, dim3(grid), dim3(128), 0, st, W, as, mm, bias, relu, yy, qq, uq, tail, ut, 0); break;
         }
     }
 }

@@ -110,6 +110,9 @@ struct Tail {
 struct Epi {
     const QKVStore* qkv = nullptr;
     const Tail* tail = nullptr;
+    // The activations are only in a.f (f32): Q8_0/Q4_0 weights for at most 8 rows quantise them
+    // inside the few-row kernel; otherwise matmul converts them (quantize_act) first.
+    bool quant_in = false;
 };
 
 void quantize_act(int wtype, const float* x, int M, int K, ActQ& a, cudaStream_t st);

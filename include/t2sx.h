@@ -169,7 +169,8 @@ T2SX_API int t2sx_profile_step(t2sx_session* s, int32_t iters, float* ms);
 /* ---- kernels on caller-provided device buffers (isolated measurements) ------------------- */
 
 /* A linear weight [N][K] given as ggml block bytes on the host (Q8_0, Q4_0, Q4_K, F16 or F32),
- * repacked to the device layout. */
+ * repacked to the device layout.  K <= 2048 (the largest T2S contraction, the FFN down
+ * projection); larger K returns T2SX_ERR_INVALID. */
 typedef struct t2sx_weight t2sx_weight;
 T2SX_API int t2sx_weight_create(int32_t device, int32_t ggml_type, const void* host_bytes, int64_t N,
                        int64_t K, t2sx_weight** out);

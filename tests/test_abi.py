@@ -33,3 +33,15 @@ def test_errors_without_device(t2sx_mod):
     assert L.t2sx_session_find_free_slot(None) == -1
     assert L.t2sx_session_slot_n_pos(None, 0) == -1
     assert L.t2sx_version() == 1
+
+
+def test_weight_create_rejects_large_k(t2sx_mod):
+    """K above 2048 (the few-row kernel's shared-memory bound) is rejected before any device work."""
+    import ctypes
+    L = t2sx_mod.lib()
+    K = 2048 + 32
+    buf = (ctypes.c_uint8 * (K // 32 * 34))()
+    h = ctypes.c_void_p()
+    assert L.t2sx_weight_create(0, 8, buf, 1, K, ctypes.byref(h)) == t2sx_mod.ERR_INVALID
+    assert b"K above 2048" in L.t2sx_last_error()
+    assert not h.value
