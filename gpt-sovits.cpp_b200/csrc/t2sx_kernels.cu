@@ -892,6 +892,144 @@ __global__ void __launch_bounds__(32 * HPC) k_attn_decode(const uint16_t* __rest
     attn_finish<HPC>(st, r, hg, warp, lane, out, qtype, qo, s_am, &s_is);
 }
 
+// Decode attention for very few rows: one CTA per (row, head), 4 threads per position lane.  With
+// one warp per head the fold was a single instruction stream per SM (about 200 dependent
+// instructions per position); here thread (lane group a, quarter j) of warp w folds position lane
+// vl = 8w + a over dims 8j..8j+7.  The score's 32-term dot is four sequential 8-term fma chains
+// summed as (c0 + c1) + (c2 + c3): thread j runs chain j and the two xor shuffles sum them in that
+// order, so all four threads hold the same score and run the same online update (m, l) on their
+// own 8 dims of o.  The merge keeps the butterfly partners 16, 8, 4, 2, 1 (the first two between
+// warps, through shared memory) and the merge formula, so the row equals the one-warp kernel's.
+constexpr int kQD = 16;   // positions per lane in flight
+
+__device__ __forceinline__ void st_update8(float& m, float& l, float (&o)[8], float s, const float (&v)[8]) {
+    if (s > m) {
+        const float t = t2s_expf(__fsub_rn(m, s));
+        m = s;
+        l = __fmaf_rn(l, t, 1.0f);
+#pragma unroll
+        for (int d = 0; d < 8; ++d) o[d] = __fmaf_rn(o[d], t, v[d]);
+    } else {
+        const float t = t2s_expf(__fsub_rn(s, m));
+        l = __fadd_rn(l, t);
+#pragma unroll
+        for (int d = 0; d < 8; ++d) o[d] = __fmaf_rn(t, v[d], o[d]);
+    }
+}
+
+__device__ __forceinline__ void st_merge8(float& m, float& l, float (&o)[8], float mB, float lB, const float (&oB)[8]) {
+    float M, a, b, ln;
+    bool empty;
+    st_merge_scalars(m, l, mB, lB, M, a, b, ln, empty);
+#pragma unroll
+    for (int d = 0; d < 8; ++d) o[d] = empty ? 0.0f : __fadd_rn(__fmul_rn(o[d], a), __fmul_rn(oB[d], b));
+    m = empty ? __int_as_float(0xff800000) : M;
+    l = ln;
+}
+
+__device__ __forceinline__ void unpack8(const uint4& u, float (&out)[8]) {
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        out[2 * e] = h2f((uint16_t)(w[e] & 0xffffu));
+        out[2 * e + 1] = h2f((uint16_t)(w[e] >> 16));
+    }
+}
+
+__global__ void __launch_bounds__(128) k_attn_decode_split(const uint16_t* __restrict__ q16, Rows rows, KVView kv, int layer,
+                                                          float scale, float* __restrict__ out, int qtype, ActQ qo) {
+    pdl_trigger();
+    pdl_wait();
+    extern __shared__ __align__(16) uint8_t dsm[];
+    // [slot][K | V][thread] 16-byte chunks, then the merge exchange (10 floats per thread), the
+    // output head, and the row's page numbers
+    float* s_x = reinterpret_cast<float*>(dsm + kQD * 2 * 128 * 16);
+    float* s_val = s_x + 10 * 128;
+    int32_t* s_pt = reinterpret_cast<int32_t*>(s_val + 32);
+    const int r = blockIdx.x / kHeads, h = blockIdx.x % kHeads;
+    const int tid = threadIdx.x, w = tid >> 5, t = tid & 31, a = t >> 2, j = t & 3;
+    const int vl = 8 * w + a;
+    const int s = rows.slot[r];
+    const int L = rows.L[r];
+    float q[8];
+    unpack8(*reinterpret_cast<const uint4*>(q16 + (size_t)r * kD + h * kHeadDim + 8 * j), q);
+    const int32_t* pt = kv.ptab + (size_t)s * kv.max_pages;
+    const int np = (L + kPage - 1) / kPage;
+    for (int i = tid; i < np; i += 128) s_pt[i] = pt[i];
+    __syncthreads();
+    float m = __int_as_float(0xff800000), l = 0.0f, o[8];
+#pragma unroll
+    for (int d = 0; d < 8; ++d) o[d] = 0.0f;
+    const int nk = (L - vl + kAttnLanes - 1) / kAttnLanes;   // this position lane's positions
+    const unsigned gmask = 0xFu << (4 * a);                  // the four threads of the lane
+    auto issue = [&](int k) {
+        if (k < nk) {
+            const int i = vl + kAttnLanes * k;
+            const int page = s_pt[k >> 1];
+            uint8_t* dst = dsm + (size_t)(k % kQD) * 2 * 128 * 16 + tid * 16;
+            cp_async16(dst, kv.pool + kv_off(kv, page, layer, 0, h, i % kPage) + 8 * j, true);
+            cp_async16(dst + 128 * 16, kv.pool + kv_off(kv, page, layer, 1, h, i % kPage) + 8 * j, true);
+        }
+        cp_commit();
+    };
+#pragma unroll
+    for (int k = 0; k < kQD - 1; ++k) issue(k);
+    for (int k = 0; k < nk; ++k) {
+        asm volatile("" ::: "memory");   // the previous step's reads of that slot stay before the refill
+        issue(k + kQD - 1);
+        cp_wait<kQD - 1>();
+        const uint8_t* src = dsm + (size_t)(k % kQD) * 2 * 128 * 16 + tid * 16;
+        float kf[8], vf[8];
+        unpack8(*reinterpret_cast<const uint4*>(src), kf);
+        unpack8(*reinterpret_cast<const uint4*>(src + 128 * 16), vf);
+        float c = 0.0f;
+#pragma unroll
+        for (int d = 0; d < 8; ++d) c = __fmaf_rn(q[d], kf[d], c);
+        const float c2 = __fadd_rn(c, __shfl_xor_sync(gmask, c, 1));
+        const float dot = __fadd_rn(c2, __shfl_xor_sync(gmask, c2, 2));
+        st_update8(m, l, o, __fmul_rn(dot, scale), vf);
+    }
+    cp_wait<0>();
+    // butterfly rounds 16 and 8: partner thread tid ^ 64, then tid ^ 32
+#pragma unroll
+    for (int rnd = 0; rnd < 2; ++rnd) {
+        const int pt_ = tid ^ (rnd == 0 ? 64 : 32);
+        __syncthreads();
+        s_x[tid * 10] = m;
+        s_x[tid * 10 + 1] = l;
+#pragma unroll
+        for (int d = 0; d < 8; ++d) s_x[tid * 10 + 2 + d] = o[d];
+        __syncthreads();
+        float oB[8];
+#pragma unroll
+        for (int d = 0; d < 8; ++d) oB[d] = s_x[pt_ * 10 + 2 + d];
+        st_merge8(m, l, o, s_x[pt_ * 10], s_x[pt_ * 10 + 1], oB);
+    }
+    // rounds 4, 2, 1: partner lane group a ^ off, the same quarter (lane t ^ 4 * off)
+#pragma unroll
+    for (int off = 4; off >= 1; off >>= 1) {
+        const float mB = __shfl_xor_sync(0xffffffffu, m, 4 * off);
+        const float lB = __shfl_xor_sync(0xffffffffu, l, 4 * off);
+        float oB[8];
+#pragma unroll
+        for (int d = 0; d < 8; ++d) oB[d] = __shfl_xor_sync(0xffffffffu, o[d], 4 * off);
+        st_merge8(m, l, o, mB, lB, oB);
+    }
+    // every thread now holds the merged state of its quarter; lane d of warp 0 takes dim d
+    if (w == 0 && a == 0) {
+        const float inv = __fdiv_rn(1.0f, l);
+#pragma unroll
+        for (int d = 0; d < 8; ++d) s_val[8 * j + d] = __fmul_rn(o[d], inv);
+    }
+    __syncthreads();
+    if (w != 0) return;
+    const float val = s_val[t];
+    const size_t e = (size_t)r * kD + h * kHeadDim + t;
+    if (qtype == W_Q8_0 || qtype == W_Q4_0) qo.q[e] = (int8_t)q8_0_lane(val, qo.d + (size_t)r * (kD / 32) + h, t);
+    else if (qtype == W_F16) qo.h[e] = f2h(val);
+    else out[e] = val;
+}
+
 // Prefill attention: a CTA takes a group of up to 16 consecutive rows of one slot (the rows of a
 // prompt) and one head, one warp per row.  The group's K/V are staged in shared memory a page (64
 // positions) at a time, double-buffered with cp.async, and every warp folds them with the decode
@@ -997,6 +1135,15 @@ static int pipe1_rows() {
     return v;
 }
 
+// Below pipe1_rows() rows: the four-threads-per-lane kernel (T2SX_ATTN_SPLIT=0: one warp per head).
+static bool attn_split() {
+    static const bool v = [] {
+        const char* e = getenv("T2SX_ATTN_SPLIT");
+        return !(e && e[0] == '0');
+    }();
+    return v;
+}
+
 void attention_decode(int T, const uint16_t* q16, Rows rows, KVView kv, int layer, float scale, float* out, int qtype,
                       ActQ qo, cudaStream_t st) {
     if (T <= 0) return;
@@ -1010,6 +1157,15 @@ void attention_decode(int T, const uint16_t* q16, Rows rows, KVView kv, int laye
         // for the 2048-row decode step)
         launch_k((k_attn_decode<4, false>), dim3(T * (kHeads / 4)), dim3(128), 0, st, q16, rows, kv, layer, scale, out, -1, qo);
         quantize_act(W_Q4_K, out, T, kD, qo, st);
+    } else if (T < pipe1_rows() && attn_split()) {
+        // very few rows: one head per CTA, four threads per position lane
+        static bool configured = false;
+        if (!configured) {
+            cudaFuncSetAttribute(k_attn_decode_split, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+            configured = true;
+        }
+        const size_t smem = (size_t)kQD * 2 * 128 * 16 + (10 * 128 + 32) * 4 + (size_t)kv.max_pages * 4;
+        launch_k(k_attn_decode_split, dim3(T * kHeads), dim3(128), smem, st, q16, rows, kv, layer, scale, out, qtype, qo);
     } else if (T < pipe1_rows()) {
         // very few rows: one head per CTA, 16 positions per lane in flight
         launch_k((k_attn_decode<1, true>), dim3(T * kHeads), dim3(32), attn_pipe_smem<1>(kv), st, q16, rows, kv, layer, scale, out, qtype, qo);
