@@ -252,7 +252,9 @@ __device__ void ln_row_warp(const float* __restrict__ a, const float* __restrict
     }
 #pragma unroll
     for (int off = 16; off >= 1; off >>= 1) s = __dadd_rn(s, __shfl_xor_sync(0xffffffffu, s, off));
-    const float mean = __double2float_rn(__ddiv_rn(s, (double)kD));
+    // kD is a power of two: s * (1/kD) is the same correctly rounded value as s / kD
+    static_assert((kD & (kD - 1)) == 0, "kD must be a power of two");
+    const float mean = __double2float_rn(__dmul_rn(s, 1.0 / kD));
     double s2 = 0.0;
 #pragma unroll
     for (int t = 0; t < kD / 32; ++t) {
@@ -261,7 +263,7 @@ __device__ void ln_row_warp(const float* __restrict__ a, const float* __restrict
     }
 #pragma unroll
     for (int off = 16; off >= 1; off >>= 1) s2 = __dadd_rn(s2, __shfl_xor_sync(0xffffffffu, s2, off));
-    const float var = __double2float_rn(__ddiv_rn(s2, (double)kD));
+    const float var = __double2float_rn(__dmul_rn(s2, 1.0 / kD));
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
 #pragma unroll
     for (int t = 0; t < kD / 32; ++t) out[t] = __fadd_rn(__fmul_rn(__fmul_rn(v[t], scale), gv[t]), bv[t]);
@@ -503,6 +505,89 @@ __global__ void __launch_bounds__(128) k_mm_small(DevW W, ActQ A, int M, const f
             mm_small_row<WT>(W, A, M, bias, relu, y, use_qkv ? &qkv : nullptr, s_a[warp], s_m[warp], s_dd[warp], n, lane);
     }
     if (use_tail) tail_if_last(tail, y, M, W.N);
+}
+
+// Few-row matmul whose input is a residual + LayerNorm (ggml_norm + mul + add, block.cpp:615-619 /
+// :630-634) of the preceding matmul's output: the norm runs at the start of every CTA instead of
+// in the last CTA of the preceding matmul.  One warp per row normalises (ln_row_warp) and converts
+// it to Q8_0 in shared memory (quant_row512_strided) while the CTA's weight loads are in flight;
+// CTA 0 also stores the normalised rows (the next residual).  No ticket, no fence, and one round
+// trip less than the tail.  Q8_0/Q4_0 weights, K = 512, at most 2 rows; the block sums and their
+// ordered fold are those of mm_small_row.
+template <int WT>
+__global__ void __launch_bounds__(128) k_mm_ln(DevW W, LnIn ln, int M, const float* __restrict__ bias, int relu,
+                                               float* __restrict__ y, QKVStore qkv, int use_qkv) {
+    pdl_trigger();
+    pdl_wait();
+    constexpr int nb = kD / 32;
+    __shared__ __align__(16) int8_t s_xq[kLnRows * kD];
+    __shared__ float s_xd[kLnRows * nb];
+    __shared__ int s_a[4][kLnRows][nb];
+    __shared__ float s_dd[4][kLnRows][nb];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n = blockIdx.x * 4 + warp;
+    const bool row = n < W.N;
+    // this warp's weight row (block `lane`) and the epilogue's loads, issued before the norm
+    int4 w0 = make_int4(0, 0, 0, 0), w1 = w0;
+    float wd = 0.0f;
+    if (row && lane < nb) {
+        if (WT == W_Q8_0) {
+            const int4* wp = reinterpret_cast<const int4*>(W.q8 + (size_t)n * kD + lane * 32);
+            w0 = wp[0]; w1 = wp[1];
+        } else {
+            const int4 raw = *reinterpret_cast<const int4*>(W.q4 + ((size_t)n * nb + lane) * 16);
+            w0 = make_int4(q4lo(raw.x), q4lo(raw.y), q4lo(raw.z), q4lo(raw.w));
+            w1 = make_int4(q4hi(raw.x), q4hi(raw.y), q4hi(raw.z), q4hi(raw.w));
+        }
+        wd = W.d[(size_t)n * nb + lane];
+    }
+    const bool own = row && lane < M;
+    const float bv = (bias && own) ? bias[n] : 0.0f;
+    const bool kvcol = use_qkv && own && n >= kD;
+    int kpos = 0, kslot = 0;
+    if (kvcol) { kpos = qkv.rows.pos[lane]; kslot = qkv.rows.slot[lane]; }
+    if (warp < M) {
+        float o[kD / 32];
+        ln_row_warp(ln.a + (size_t)warp * kD, ln.b + (size_t)warp * kD, true, ln.g, ln.beta, ln.eps, lane, o);
+        if (blockIdx.x == 0) {
+#pragma unroll
+            for (int t = 0; t < kD / 32; ++t) ln.y_out[(size_t)warp * kD + lane + 32 * t] = o[t];
+        }
+        ActQ sq;
+        sq.q = s_xq;
+        sq.d = s_xd;
+        quant_row512_strided(o, lane, W_Q8_0, sq, (size_t)warp);
+    }
+    __syncthreads();
+    if (!row) return;
+    if (lane < nb) {
+        for (int m = 0; m < M; ++m) {
+            const int4* xp = reinterpret_cast<const int4*>(s_xq + m * kD + lane * 32);
+            s_a[warp][m][lane] = dp8(w0, w1, xp[0], xp[1]);
+            s_dd[warp][m][lane] = __fmul_rn(wd, s_xd[m * nb + lane]);
+        }
+    }
+    __syncwarp();
+    if (own) {
+        const int m = lane;
+        float acc = 0.0f;
+#pragma unroll
+        for (int b = 0; b < nb; ++b) acc = __fmaf_rn(s_dd[warp][m][b], (float)s_a[warp][m][b], acc);
+        const float v_ = epi_v(acc, bias != nullptr, bv, relu);
+        if (use_qkv) qkv_store_at(qkv, m, n, v_, kvcol ? qkv_dest(qkv, kpos, kslot) : make_int2(-1, 0));
+        else y[(size_t)m * W.N + n] = v_;
+    }
+}
+
+bool matmul_ln(const DevW& W, const LnIn& ln, int M, const float* bias, int relu, float* y, const QKVStore* qkv,
+               cudaStream_t st) {
+    if (M < 1 || M > kLnRows || W.K != kD || (W.type != W_Q8_0 && W.type != W_Q4_0)) return false;
+    QKVStore q{};
+    if (qkv) q = *qkv;
+    const int grid = (W.N + 3) / 4;
+    if (W.type == W_Q8_0) launch_k(k_mm_ln<W_Q8_0>, dim3(grid), dim3(128), 0, st, W, ln, M, bias, relu, y, q, qkv ? 1 : 0);
+    else launch_k(k_mm_ln<W_Q4_0>, dim3(grid), dim3(128), 0, st, W, ln, M, bias, relu, y, q, qkv ? 1 : 0);
+    return true;
 }
 
 int narrow_min_rows() {
@@ -854,12 +939,12 @@ __global__ void __launch_bounds__(32 * HPC) k_attn_decode(const uint16_t* __rest
         for (int j = threadIdx.x; j < np; j += NT) s_pt[j] = pt[j];
         __syncthreads();
         const int nk = (L - lane + kAttnLanes - 1) / kAttnLanes;   // this lane's positions
+        // position lane + 32k lies in page k / 2 at lane + 32 (k & 1)
+        const uint16_t* kvb = kv_head_base(kv, layer, h) + lane * kHeadDim;
         auto issue = [&](int k) {
             if (k < nk) {
-                const int i = lane + kAttnLanes * k;
-                const int page = s_pt[k >> 1];
-                const uint16_t* kp = kv.pool + kv_off(kv, page, layer, 0, h, i % kPage);
-                const uint16_t* vp = kv.pool + kv_off(kv, page, layer, 1, h, i % kPage);
+                const uint16_t* kp = kvb + (size_t)s_pt[k >> 1] * kPageElems + (k & 1) * (kAttnLanes * kHeadDim);
+                const uint16_t* vp = kp + kHalfPageElems;
                 uint8_t* dst = dsm + (size_t)(k % D) * 8 * NT * 16 + threadIdx.x * 16;
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
@@ -962,13 +1047,14 @@ __global__ void __launch_bounds__(128) k_attn_decode_split(const uint16_t* __res
     for (int d = 0; d < 8; ++d) o[d] = 0.0f;
     const int nk = (L - vl + kAttnLanes - 1) / kAttnLanes;   // this position lane's positions
     const unsigned gmask = 0xFu << (4 * a);                  // the four threads of the lane
+    // position vl + 32k lies in page k / 2 at vl + 32 (k & 1)
+    const uint16_t* kvb = kv_head_base(kv, layer, h) + vl * kHeadDim + 8 * j;
     auto issue = [&](int k) {
         if (k < nk) {
-            const int i = vl + kAttnLanes * k;
-            const int page = s_pt[k >> 1];
+            const uint16_t* kp = kvb + (size_t)s_pt[k >> 1] * kPageElems + (k & 1) * (kAttnLanes * kHeadDim);
             uint8_t* dst = dsm + (size_t)(k % kQD) * 2 * 128 * 16 + tid * 16;
-            cp_async16(dst, kv.pool + kv_off(kv, page, layer, 0, h, i % kPage) + 8 * j, true);
-            cp_async16(dst + 128 * 16, kv.pool + kv_off(kv, page, layer, 1, h, i % kPage) + 8 * j, true);
+            cp_async16(dst, kp, true);
+            cp_async16(dst + 128 * 16, kp + kHalfPageElems, true);
         }
         cp_commit();
     };

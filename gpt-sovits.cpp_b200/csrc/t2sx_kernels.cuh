@@ -116,6 +116,20 @@ struct Epi {
 };
 
 void quantize_act(int wtype, const float* x, int M, int K, ActQ& a, cudaStream_t st);
+// Input of a few-row matmul that starts with y_out = LN(a + b) * g + beta (rows of kD; CTA 0
+// stores y_out).
+constexpr int kLnRows = 2;
+struct LnIn {
+    const float* a = nullptr;
+    const float* b = nullptr;
+    const float* g = nullptr;
+    const float* beta = nullptr;
+    float eps = 1e-5f;
+    float* y_out = nullptr;
+};
+// false (nothing launched) unless Q8_0/Q4_0 weights with K == kD and 1..kLnRows rows
+bool matmul_ln(const DevW& W, const LnIn& ln, int M, const float* bias, int relu, float* y, const QKVStore* qkv,
+               cudaStream_t st);
 void matmul(const DevW& W, const ActQ& a, int M, const float* bias, int relu, float* y, cudaStream_t st,
             const Epi& epi = Epi());
 // tcgen05 path (TMA-fed, TMEM accumulators; Q4_K weights) for large M; false if not supported.

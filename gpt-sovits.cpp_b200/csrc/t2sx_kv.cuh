@@ -10,6 +10,14 @@ __device__ __forceinline__ size_t kv_off(const KVView& kv, int page, int layer, 
     return (((((size_t)layer * kv.n_pages + page) * 2 + which) * kHeads + head) * kPage + pos_in_page) * kHeadDim;
 }
 
+// Elements of one page (K and V of every head) and of its K (or V) half: kv_off is linear in the
+// page, so a kernel can hold (layer, head) fixed in a base pointer and add page and position.
+constexpr size_t kPageElems = (size_t)2 * kHeads * kPage * kHeadDim;
+constexpr int kHalfPageElems = kHeads * kPage * kHeadDim;
+__device__ __forceinline__ const uint16_t* kv_head_base(const KVView& kv, int layer, int head) {
+    return kv.pool + kv_off(kv, 0, layer, 0, head, 0);
+}
+
 // cp.async copies global -> shared (16 or 4 bytes; a false `valid` copies nothing and zero-fills),
 // grouped per thread by commit; wait until at most N of this thread's groups are pending.
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool valid) {

@@ -127,6 +127,18 @@ def test_decode_small_model_bit_exact(t2sx_mod, orc, fmt):
     _run_pair(t2sx_mod, orc, path, lengths, steps=70)
 
 
+@pytest.mark.parametrize("n", [1, 2])
+@pytest.mark.parametrize("fmt", ["q8_0", "q5_0", "q4_0", "q4_k", "f16"])
+def test_decode_one_or_two_sessions_bit_exact(t2sx_mod, orc, fmt, n):
+    """One or two rows per step: Q8_0/Q4_0 (and Q5_0, held as Q8_0) weights run each LayerNorm at
+    the start of the matmul that consumes it, Q4_K/F16 in the last CTA of the preceding matmul."""
+    _need_gpu()
+    import synth
+    path = synth.ensure_gguf(fmt, 7, n_layer=2)
+    lengths = [(40, 30, 31), (17, 50, 32)][:n]
+    _run_pair(t2sx_mod, orc, path, lengths, steps=40)
+
+
 def test_decode_repetition_penalty_bit_exact(t2sx_mod, orc):
     _need_gpu()
     import synth
