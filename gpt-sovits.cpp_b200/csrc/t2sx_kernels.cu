@@ -344,7 +344,53 @@ __device__ __forceinline__ void mm_small_row(const DevW& W, const ActQ& A, int M
         if (qkv) qkv_store_at(*qkv, lane, n, v_, kvcol ? qkv_dest(*qkv, kpos, kslot) : make_int2(-1, 0));
         else y[(size_t)lane * W.N + n] = v_;
     };
-    if (WT == W_Q8_0 || WT == W_Q4_0) {
+    if ((WT == W_Q8_0 || WT == W_Q4_0) && fq && M == 1) {
+        // one row quantised here (K <= 2048: at most two blocks per lane), both blocks' weights
+        // and activations fetched before any arithmetic
+        const int nb = K / 32;
+        int4 wq[2][2];
+        float wd[2];
+        float4 xv[2][8];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            const int b = lane + 32 * u;
+            if (b < nb) {
+                if (WT == W_Q8_0) {
+                    const int4* wp = reinterpret_cast<const int4*>(W.q8 + (size_t)n * K + b * 32);
+                    wq[u][0] = wp[0]; wq[u][1] = wp[1];
+                } else {
+                    wq[u][0] = *reinterpret_cast<const int4*>(W.q4 + ((size_t)n * nb + b) * 16);
+                }
+                wd[u] = W.d[(size_t)n * nb + b];
+                const float4* xp = reinterpret_cast<const float4*>(A.f + b * 32);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) xv[u][i] = xp[i];
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            const int b = lane + 32 * u;
+            if (b < nb) {
+                int4 w0 = wq[u][0], w1 = wq[u][1];
+                if (WT == W_Q4_0) {
+                    const int4 raw = wq[u][0];
+                    w0 = make_int4(q4lo(raw.x), q4lo(raw.y), q4lo(raw.z), q4lo(raw.w));
+                    w1 = make_int4(q4hi(raw.x), q4hi(raw.y), q4hi(raw.z), q4hi(raw.w));
+                }
+                int4 x0, x1;
+                float ad;
+                q8_0_block_regs(xv[u], x0, x1, ad);
+                s_a[0][b] = dp8(w0, w1, x0, x1);
+                s_dd[0][b] = __fmul_rn(wd[u], ad);
+            }
+        }
+        __syncwarp();
+        if (own) {
+            float acc = 0.0f;
+            for (int b = 0; b < nb; ++b) acc = __fmaf_rn(s_dd[0][b], (float)s_a[0][b], acc);
+            finish(acc);
+        }
+    } else if (WT == W_Q8_0 || WT == W_Q4_0) {
         const int nb = K / 32;
         for (int b = lane; b < nb; b += 32) {
             int4 w0, w1;
@@ -1058,22 +1104,37 @@ __global__ void __launch_bounds__(128) k_attn_decode_split(const uint16_t* __res
         }
         cp_commit();
     };
+    // positions in pairs: the two scores are independent chains (computed side by side), the two
+    // updates run in position order; each pair refills the two slots the previous pair read
 #pragma unroll
-    for (int k = 0; k < kQD - 1; ++k) issue(k);
-    for (int k = 0; k < nk; ++k) {
-        asm volatile("" ::: "memory");   // the previous step's reads of that slot stay before the refill
+    for (int k = 0; k < kQD - 2; ++k) issue(k);
+    for (int k = 0; k < nk; k += 2) {
+        asm volatile("" ::: "memory");   // the previous pair's reads of those slots stay before the refill
+        issue(k + kQD - 2);
         issue(k + kQD - 1);
-        cp_wait<kQD - 1>();
-        const uint8_t* src = dsm + (size_t)(k % kQD) * 2 * 128 * 16 + tid * 16;
-        float kf[8], vf[8];
-        unpack8(*reinterpret_cast<const uint4*>(src), kf);
-        unpack8(*reinterpret_cast<const uint4*>(src + 128 * 16), vf);
-        float c = 0.0f;
+        cp_wait<kQD - 2>();
+        const uint8_t* src0 = dsm + (size_t)(k % kQD) * 2 * 128 * 16 + tid * 16;
+        const uint8_t* src1 = dsm + (size_t)((k + 1) % kQD) * 2 * 128 * 16 + tid * 16;
+        float k0[8], k1[8];
+        unpack8(*reinterpret_cast<const uint4*>(src0), k0);
+        unpack8(*reinterpret_cast<const uint4*>(src1), k1);
+        float c0 = 0.0f, c1 = 0.0f;
 #pragma unroll
-        for (int d = 0; d < 8; ++d) c = __fmaf_rn(q[d], kf[d], c);
-        const float c2 = __fadd_rn(c, __shfl_xor_sync(gmask, c, 1));
-        const float dot = __fadd_rn(c2, __shfl_xor_sync(gmask, c2, 2));
-        st_update8(m, l, o, __fmul_rn(dot, scale), vf);
+        for (int d = 0; d < 8; ++d) {
+            c0 = __fmaf_rn(q[d], k0[d], c0);
+            c1 = __fmaf_rn(q[d], k1[d], c1);
+        }
+        const float a0 = __fadd_rn(c0, __shfl_xor_sync(gmask, c0, 1));
+        const float a1 = __fadd_rn(c1, __shfl_xor_sync(gmask, c1, 1));
+        const float dot0 = __fadd_rn(a0, __shfl_xor_sync(gmask, a0, 2));
+        const float dot1 = __fadd_rn(a1, __shfl_xor_sync(gmask, a1, 2));
+        float vf[8];
+        unpack8(*reinterpret_cast<const uint4*>(src0 + 128 * 16), vf);
+        st_update8(m, l, o, __fmul_rn(dot0, scale), vf);
+        if (k + 1 < nk) {   // (the same for the lane's four threads)
+            unpack8(*reinterpret_cast<const uint4*>(src1 + 128 * 16), vf);
+            st_update8(m, l, o, __fmul_rn(dot1, scale), vf);
+        }
     }
     cp_wait<0>();
     // butterfly rounds 16 and 8: partner thread tid ^ 64, then tid ^ 32

@@ -124,19 +124,22 @@ __device__ __forceinline__ int q8_0_lane(float v, float* d_slot, int lane) {
 }
 
 // q8_0_lane's rule for a whole 32-element block in one thread (the |x| maximum is the same in
-// any order): the block's bytes as the activation buffer holds them (little-endian, elements
-// 0-15 in lo, 16-31 in hi) and its f16-rounded scale.  x is 16-byte aligned.
-__device__ __forceinline__ void q8_0_block_thread(const float* __restrict__ x, int4& lo, int4& hi, float& d) {
+// any order, so it is taken as a tree): the block's bytes as the activation buffer holds them
+// (little-endian, elements 0-15 in lo, 16-31 in hi) and its f16-rounded scale.
+__device__ __forceinline__ void q8_0_block_regs(const float4 (&x4)[8], int4& lo, int4& hi, float& d) {
     float v[32];
-    const float4* xp = reinterpret_cast<const float4*>(x);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-        const float4 t = xp[i];
-        v[4 * i] = t.x; v[4 * i + 1] = t.y; v[4 * i + 2] = t.z; v[4 * i + 3] = t.w;
+        v[4 * i] = x4[i].x; v[4 * i + 1] = x4[i].y; v[4 * i + 2] = x4[i].z; v[4 * i + 3] = x4[i].w;
     }
-    float a = fabsf(v[0]);
+    float t[16];
 #pragma unroll
-    for (int i = 1; i < 32; ++i) a = fmaxf(a, fabsf(v[i]));
+    for (int i = 0; i < 16; ++i) t[i] = fmaxf(fabsf(v[i]), fabsf(v[i + 16]));
+#pragma unroll
+    for (int w = 8; w >= 1; w >>= 1)
+#pragma unroll
+        for (int i = 0; i < w; ++i) t[i] = fmaxf(t[i], t[i + w]);
+    const float a = t[0];
     const float dd = __fdiv_rn(a, 127.0f);
     const float id = (a != 0.0f) ? __fdiv_rn(127.0f, a) : 0.0f;
     int w[8];
@@ -154,6 +157,15 @@ __device__ __forceinline__ void q8_0_block_thread(const float* __restrict__ x, i
     lo = make_int4(w[0], w[1], w[2], w[3]);
     hi = make_int4(w[4], w[5], w[6], w[7]);
     d = __half2float(__float2half_rn(dd));
+}
+
+// the same from 32 floats at x (16-byte aligned)
+__device__ __forceinline__ void q8_0_block_thread(const float* __restrict__ x, int4& lo, int4& hi, float& d) {
+    float4 x4[8];
+    const float4* xp = reinterpret_cast<const float4*>(x);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) x4[i] = xp[i];
+    q8_0_block_regs(x4, lo, hi, d);
 }
 
 // Running (|x| max, signed value, first index) of a Q8_K block (ggml quantize_row_q8_K_ref).
