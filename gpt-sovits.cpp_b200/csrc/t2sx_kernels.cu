@@ -82,23 +82,47 @@ __device__ void quant_row512_strided(const float (&y)[kD / 32], int lane, int wt
     // The blocks' warp reductions run side by side (a max, a first-index |x| max and integer sums
     // do not depend on the merge order), so their shuffles overlap instead of running block by block.
     if (wtype == W_Q8_0 || wtype == W_Q4_0) {
-        float a[kD / 32];
+        // The 16 block maxima as a reduce-scatter (fmaxf is exact, so any order gives the same
+        // maximum): at the rounds with partners 16, 8, 4, 2 a lane keeps the half of its blocks
+        // selected by that lane bit, so lane l ends with block l >> 1, completed by partner 1.
+        // Lane l then forms that block's scale and inverse (the rule of q8_0_lane, x86 AVX2
+        // quantize_row_q8_0: d = amax/127 as f16, q = rint(v * 127/amax)); block t's inverse
+        // comes from lane 2t.
+        float a16[16], a8[8], a4[4], a2[2];
 #pragma unroll
-        for (int t = 0; t < kD / 32; ++t) a[t] = fabsf(y[t]);
+        for (int t = 0; t < 16; ++t) a16[t] = fabsf(y[t]);
+        auto half_round = [&](auto& in, auto& out, int off, int n) {
+            const bool hi = (lane & off) != 0;
 #pragma unroll
-        for (int off = 16; off >= 1; off >>= 1)
-#pragma unroll
-            for (int t = 0; t < kD / 32; ++t) a[t] = fmaxf(a[t], __shfl_xor_sync(0xffffffffu, a[t], off));
+            for (int u = 0; u < 8; ++u) {
+                if (u < n) {
+                    const float keep = hi ? in[n + u] : in[u];
+                    const float send = hi ? in[u] : in[n + u];
+                    out[u] = fmaxf(keep, __shfl_xor_sync(0xffffffffu, send, off));
+                }
+            }
+        };
+        half_round(a16, a8, 16, 8);
+        half_round(a8, a4, 8, 4);
+        half_round(a4, a2, 4, 2);
+        float a1;
+        {
+            const bool hi = (lane & 2) != 0;
+            const float keep = hi ? a2[1] : a2[0];
+            const float send = hi ? a2[0] : a2[1];
+            a1 = fmaxf(keep, __shfl_xor_sync(0xffffffffu, send, 2));
+        }
+        a1 = fmaxf(a1, __shfl_xor_sync(0xffffffffu, a1, 1));
+        const float dd = __fdiv_rn(a1, 127.0f);
+        const float id = (a1 != 0.0f) ? __fdiv_rn(127.0f, a1) : 0.0f;
 #pragma unroll
         for (int t = 0; t < kD / 32; ++t) {
-            // the rule of q8_0_lane (x86 AVX2 quantize_row_q8_0): d = amax/127 as f16, q = rint(v * 127/amax)
-            const float dd = __fdiv_rn(a[t], 127.0f);
-            const float id = (a[t] != 0.0f) ? __fdiv_rn(127.0f, a[t]) : 0.0f;
-            float r = rintf(__fmul_rn(y[t], id));
+            const float idt = __shfl_sync(0xffffffffu, id, 2 * t);
+            float r = rintf(__fmul_rn(y[t], idt));
             r = fminf(fmaxf(r, -128.0f), 127.0f);
             o.q[row * kD + 32 * t + lane] = (int8_t)(int)r;
-            if (lane == 0) o.d[row * (kD / 32) + t] = __half2float(__float2half_rn(dd));
         }
+        if ((lane & 1) == 0) o.d[row * (kD / 32) + (lane >> 1)] = __half2float(__float2half_rn(dd));
     } else if (wtype == W_Q4_K) {
         constexpr int NB = kD / 256;
         AbsMax am[NB];
