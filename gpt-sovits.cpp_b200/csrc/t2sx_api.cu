@@ -700,6 +700,15 @@ static int set_row_groups(t2sx_session* s, Work& w, int T, int row0, const std::
     return T2SX_OK;
 }
 
+// Programmatic launches for the one- and two-row layer chain (T2SX_PDL_SMALL=0: off).
+static bool pdl_small() {
+    static const bool v = [] {
+        const char* e = getenv("T2SX_PDL_SMALL");
+        return !(e && e[0] == '0');
+    }();
+    return v;
+}
+
 // The LayerNorm-prologue matmuls take Q8_0/Q4_0 QKV and FFN-up weights (Q5_0 is held as Q8_0).
 static bool ln_prologue_ok(const t2sx_model* m) {
     for (const LayerD& L : m->layers)
@@ -717,33 +726,39 @@ static void run_layers(t2sx_session* s, Work& w, int T, bool decode, int final_q
     if (small && T <= kLnRows && ln_prologue_ok(m)) {
         // each norm runs at the start of the matmul that consumes it (matmul_ln): the QKV
         // projection of layer l > 0 normalises the previous layer's FFN output, the FFN up
-        // projection the attention output; the last layer's second norm is its own kernel
-        for (int l = 0; l < nl; ++l) {
-            const LayerD& L = m->layers[l];
-            QKVStore qs;
-            qs.rows = rows;
-            qs.kv = kv;
-            qs.layer = l;
-            qs.q16 = w.q16;
-            if (l == 0) {
-                Epi e_qkv;
-                e_qkv.qkv = &qs;
-                matmul(L.qkv, act_for(w, w.x), T, L.qkv_b, 0, nullptr, s->st, e_qkv);
-            } else {
-                const LayerD& P = m->layers[l - 1];
-                LnIn n2;
-                n2.a = w.ln1; n2.b = w.f; n2.g = P.ln2_w; n2.beta = P.ln2_b; n2.y_out = w.x;
-                matmul_ln(L.qkv, n2, T, L.qkv_b, 0, nullptr, &qs, s->st);
+        // projection the attention output; the last layer's second norm is its own kernel.
+        // The chain's kernels are launched programmatically (T2SX_PDL_SMALL=0 turns that off):
+        // each fetches its weights (the attention its page numbers and earlier positions' K/V)
+        // while its predecessor finishes.
+        {
+            PdlScope pdl(pdl_small());
+            for (int l = 0; l < nl; ++l) {
+                const LayerD& L = m->layers[l];
+                QKVStore qs;
+                qs.rows = rows;
+                qs.kv = kv;
+                qs.layer = l;
+                qs.q16 = w.q16;
+                if (l == 0) {
+                    Epi e_qkv;
+                    e_qkv.qkv = &qs;
+                    matmul(L.qkv, act_for(w, w.x), T, L.qkv_b, 0, nullptr, s->st, e_qkv);
+                } else {
+                    const LayerD& P = m->layers[l - 1];
+                    LnIn n2;
+                    n2.a = w.ln1; n2.b = w.f; n2.g = P.ln2_w; n2.beta = P.ln2_b; n2.y_out = w.x;
+                    matmul_ln(L.qkv, n2, T, L.qkv_b, 0, nullptr, &qs, s->st);
+                }
+                attention_rows(T, w.grp_row0, w.grp, w.n_grp, w.q16, rows, kv, l, kAttnScale, w.attn, L.out.type, act_of(w), s->st);
+                matmul(L.out, act_for(w, w.attn), T, L.out_b, 0, w.o, s->st);
+                LnIn n1;
+                n1.a = w.x; n1.b = w.o; n1.g = L.ln1_w; n1.beta = L.ln1_b; n1.y_out = w.ln1;
+                matmul_ln(L.up, n1, T, L.up_b, 1, w.h, nullptr, s->st);
+                Epi e3;
+                e3.quant_in = true;
+                matmul(L.down, act_for(w, w.h), T, L.down_b, 0, w.f, s->st, e3);
             }
-            attention_rows(T, w.grp_row0, w.grp, w.n_grp, w.q16, rows, kv, l, kAttnScale, w.attn, L.out.type, act_of(w), s->st);
-            matmul(L.out, act_for(w, w.attn), T, L.out_b, 0, w.o, s->st);
-            LnIn n1;
-            n1.a = w.x; n1.b = w.o; n1.g = L.ln1_w; n1.beta = L.ln1_b; n1.y_out = w.ln1;
-            matmul_ln(L.up, n1, T, L.up_b, 1, w.h, nullptr, s->st);
-            Epi e3;
-            e3.quant_in = true;
-            matmul(L.down, act_for(w, w.h), T, L.down_b, 0, w.f, s->st, e3);
-        }
+        }   // (the final norm is launched without the attribute)
         const LayerD& Z = m->layers[nl - 1];
         residual_layernorm(T, w.ln1, w.f, Z.ln2_w, Z.ln2_b, 1e-5f, w.x, final_qtype, act_of(w), s->st);
         return;

@@ -11,15 +11,20 @@
 
 namespace t2sx {
 
-// Off unless T2SX_PDL=1: measured on B200 inside the step graph it did not shorten the bs=1 step
-// and slowed the 32-row step (early-resident dependents hold SM slots).
+// Off unless T2SX_PDL=1 or inside a PdlScope: measured on B200 inside the step graph it slowed
+// the 32-row step (early-resident dependents hold SM slots).
+static thread_local bool t_pdl_scope = false;
+
 bool pdl_enabled() {
     static const bool on = [] {
         const char* e = getenv("T2SX_PDL");
         return e && e[0] == '1';
     }();
-    return on;
+    return on || t_pdl_scope;
 }
+
+PdlScope::PdlScope(bool on) : prev(t_pdl_scope) { t_pdl_scope = prev || on; }
+PdlScope::~PdlScope() { t_pdl_scope = prev; }
 
 // ============================================================================================
 // activation quantisation
@@ -28,8 +33,8 @@ bool pdl_enabled() {
 // Q8_0 (x86 AVX2 rule of ggml quantize_row_q8_0): one warp per 32-element block.
 __global__ void k_quant_q8_0(const float* __restrict__ x, int64_t nblk, int8_t* __restrict__ q,
                              float* __restrict__ d) {
-    pdl_trigger();
     pdl_wait();
+    pdl_trigger();
     const int lane = threadIdx.x & 31;
     const int64_t wstride = ((int64_t)gridDim.x * blockDim.x) >> 5;
     for (int64_t b = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; b < nblk; b += wstride)
@@ -67,8 +72,8 @@ __device__ __forceinline__ void quant_block_q8_K(const float* __restrict__ xb, i
 // Q8_K (ggml quantize_row_q8_K_ref rule): one warp per 256-element block.
 __global__ void k_quant_q8_K(const float* __restrict__ x, int64_t nblk, int8_t* __restrict__ q,
                              float* __restrict__ d, int32_t* __restrict__ bs) {
-    pdl_trigger();
     pdl_wait();
+    pdl_trigger();
     const int lane = threadIdx.x & 31;
     const int64_t wstride = ((int64_t)gridDim.x * blockDim.x) >> 5;
     for (int64_t b = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; b < nblk; b += wstride)
@@ -171,8 +176,8 @@ __device__ void quant_row512_strided(const float (&y)[kD / 32], int lane, int wt
 }
 
 __global__ void k_quant_f16(const float* __restrict__ x, int64_t n, uint16_t* __restrict__ h) {
-    pdl_trigger();
     pdl_wait();
+    pdl_trigger();
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
         h[i] = f2h(x[i]);
 }
@@ -361,7 +366,13 @@ __device__ __forceinline__ void mm_small_row(const DevW& W, const ActQ& A, int M
     const float bv = (bias && own) ? bias[n] : 0.0f;
     const bool kvcol = qkv && own && n >= kD;
     int kpos = 0, kslot = 0;
-    if (kvcol) { kpos = qkv->rows.pos[lane]; kslot = qkv->rows.slot[lane]; }
+    // Loads before this point read constants (weights, bias); with a programmatic launch they
+    // overlap the preceding kernel.  Every branch calls it once, before reading activations.
+    auto after_wait = [&]() {
+        pdl_wait();
+        pdl_trigger();
+        if (kvcol) { kpos = qkv->rows.pos[lane]; kslot = qkv->rows.slot[lane]; }
+    };
     const bool stage_dd = M <= kDDM;
     auto finish = [&](float acc) {
         const float v_ = epi_v(acc, bias != nullptr, bv, relu);
@@ -386,6 +397,13 @@ __device__ __forceinline__ void mm_small_row(const DevW& W, const ActQ& A, int M
                     wq[u][0] = *reinterpret_cast<const int4*>(W.q4 + ((size_t)n * nb + b) * 16);
                 }
                 wd[u] = W.d[(size_t)n * nb + b];
+            }
+        }
+        after_wait();
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            const int b = lane + 32 * u;
+            if (b < nb) {
                 const float4* xp = reinterpret_cast<const float4*>(A.f + b * 32);
 #pragma unroll
                 for (int i = 0; i < 8; ++i) xv[u][i] = xp[i];
@@ -416,17 +434,33 @@ __device__ __forceinline__ void mm_small_row(const DevW& W, const ActQ& A, int M
         }
     } else if (WT == W_Q8_0 || WT == W_Q4_0) {
         const int nb = K / 32;
+        // the lane's first block of weights ahead of the wait
+        int4 p0 = make_int4(0, 0, 0, 0), p1 = p0;
+        float pd = 0.0f;
+        if (lane < nb) {
+            if (WT == W_Q8_0) {
+                const int4* wp = reinterpret_cast<const int4*>(W.q8 + (size_t)n * K + lane * 32);
+                p0 = wp[0]; p1 = wp[1];
+            } else {
+                p0 = *reinterpret_cast<const int4*>(W.q4 + ((size_t)n * nb + lane) * 16);
+            }
+            pd = W.d[(size_t)n * nb + lane];
+        }
+        after_wait();
         for (int b = lane; b < nb; b += 32) {
             int4 w0, w1;
             if (WT == W_Q8_0) {
-                const int4* wp = reinterpret_cast<const int4*>(W.q8 + (size_t)n * K + b * 32);
-                w0 = wp[0]; w1 = wp[1];
+                if (b == lane) { w0 = p0; w1 = p1; }
+                else {
+                    const int4* wp = reinterpret_cast<const int4*>(W.q8 + (size_t)n * K + b * 32);
+                    w0 = wp[0]; w1 = wp[1];
+                }
             } else {
-                const int4 raw = *reinterpret_cast<const int4*>(W.q4 + ((size_t)n * nb + b) * 16);
+                const int4 raw = b == lane ? p0 : *reinterpret_cast<const int4*>(W.q4 + ((size_t)n * nb + b) * 16);
                 w0 = make_int4(q4lo(raw.x), q4lo(raw.y), q4lo(raw.z), q4lo(raw.w));
                 w1 = make_int4(q4hi(raw.x), q4hi(raw.y), q4hi(raw.z), q4hi(raw.w));
             }
-            const float wd = W.d[(size_t)n * nb + b];
+            const float wd = b == lane ? pd : W.d[(size_t)n * nb + b];
             for (int m = 0; m < M; ++m) {
                 int4 x0, x1;
                 float ad;
@@ -456,6 +490,7 @@ __device__ __forceinline__ void mm_small_row(const DevW& W, const ActQ& A, int M
             finish(acc);
         }
     } else if (WT == W_Q4_K) {
+        after_wait();
         const int nsub = K / 32, nsb = K / 256;
         for (int t = 0; t < (nsub + 31) / 32; ++t) {
             const int j = lane + 32 * t;
@@ -526,6 +561,7 @@ __device__ __forceinline__ void mm_small_row(const DevW& W, const ActQ& A, int M
             finish(__fadd_rn(acc_a, acc_m));
         }
     } else {  // F16 / F32
+        after_wait();
         const int nb = K / 32;
         for (int b = lane; b < nb; b += 32) {
             float w[32];
@@ -561,8 +597,6 @@ template <int WT>
 __global__ void __launch_bounds__(128) k_mm_small(DevW W, ActQ A, int M, const float* __restrict__ bias, int relu,
                                                   float* __restrict__ y, QKVStore qkv, int use_qkv, Tail tail,
                                                   int use_tail, int fq) {
-    pdl_trigger();
-    pdl_wait();
     __shared__ int s_a[4][kSmallM][64];
     __shared__ int s_m[4][kSmallM][8];
     __shared__ float s_dd[4][kDDM][64];
@@ -573,6 +607,9 @@ __global__ void __launch_bounds__(128) k_mm_small(DevW W, ActQ A, int M, const f
             mm_small_row<WT>(W, A, M, bias, relu, y, use_qkv ? &qkv : nullptr, s_a[warp], s_m[warp], s_dd[warp], n, lane, true);
         else
             mm_small_row<WT>(W, A, M, bias, relu, y, use_qkv ? &qkv : nullptr, s_a[warp], s_m[warp], s_dd[warp], n, lane);
+    } else {   // (a row's warp waits inside mm_small_row)
+        pdl_wait();
+        pdl_trigger();
     }
     if (use_tail) tail_if_last(tail, y, M, W.N);
 }
@@ -587,8 +624,6 @@ __global__ void __launch_bounds__(128) k_mm_small(DevW W, ActQ A, int M, const f
 template <int WT>
 __global__ void __launch_bounds__(128) k_mm_ln(DevW W, LnIn ln, int M, const float* __restrict__ bias, int relu,
                                                float* __restrict__ y, QKVStore qkv, int use_qkv) {
-    pdl_trigger();
-    pdl_wait();
     constexpr int nb = kD / 32;
     __shared__ __align__(16) int8_t s_xq[kLnRows * kD];
     __shared__ float s_xd[kLnRows * nb];
@@ -613,6 +648,10 @@ __global__ void __launch_bounds__(128) k_mm_ln(DevW W, LnIn ln, int M, const flo
     }
     const bool own = row && lane < M;
     const float bv = (bias && own) ? bias[n] : 0.0f;
+    // weights and bias are constants: with a programmatic launch they are in flight while the
+    // preceding matmul finishes; everything below reads data of earlier kernels
+    pdl_wait();
+    pdl_trigger();
     const bool kvcol = use_qkv && own && n >= kD;
     int kpos = 0, kslot = 0;
     if (kvcol) { kpos = qkv.rows.pos[lane]; kslot = qkv.rows.slot[lane]; }
@@ -686,8 +725,8 @@ int tc_min_rows() {
 template <int WT>
 __global__ void __launch_bounds__(256) k_mm_fp_tile(DevW W, ActQ A, int M, const float* __restrict__ bias, int relu,
                                                      float* __restrict__ y, QKVStore qkv, int use_qkv) {
-    pdl_trigger();
     pdl_wait();
+    pdl_trigger();
     constexpr int TN = 64, TM = 64, KB = 32;
     __shared__ __align__(16) float ws[2][KB][TN];
     __shared__ __align__(16) float xs[2][KB][TM];
@@ -854,8 +893,8 @@ __global__ void k_embed_decode(int T, const int32_t* __restrict__ row_slot, cons
                                const uint16_t* __restrict__ emb16, const float* __restrict__ emb32, int emb_rows,
                                const float* __restrict__ pe, int pe_rows, float alpha, Rows rows, float* __restrict__ x,
                                int qtype, ActQ qo) {
-    pdl_trigger();
     pdl_wait();
+    pdl_trigger();
     const int lane = threadIdx.x & 31;
     const int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     if (r >= T) return;
@@ -969,8 +1008,8 @@ __device__ __forceinline__ void attn_finish(AttnState& st, int r, int hg, int wa
 template <int HPC, bool PIPE>
 __global__ void __launch_bounds__(32 * HPC) k_attn_decode(const uint16_t* __restrict__ q16, Rows rows, KVView kv, int layer,
                                                           float scale, float* __restrict__ out, int qtype, ActQ qo) {
-    pdl_trigger();
     pdl_wait();
+    pdl_trigger();
     __shared__ AbsMax s_am[8];
     __shared__ float s_is;
     // CTAs in (row, head group) order, head group fastest: the CTAs of one row run together and
@@ -1093,8 +1132,6 @@ __device__ __forceinline__ void unpack8(const uint4& u, float (&out)[8]) {
 
 __global__ void __launch_bounds__(128) k_attn_decode_split(const uint16_t* __restrict__ q16, Rows rows, KVView kv, int layer,
                                                           float scale, float* __restrict__ out, int qtype, ActQ qo) {
-    pdl_trigger();
-    pdl_wait();
     extern __shared__ __align__(16) uint8_t dsm[];
     // [slot][K | V][thread] 16-byte chunks, then the merge exchange (10 floats per thread), the
     // output head, and the row's page numbers
@@ -1104,10 +1141,12 @@ __global__ void __launch_bounds__(128) k_attn_decode_split(const uint16_t* __res
     const int r = blockIdx.x / kHeads, h = blockIdx.x % kHeads;
     const int tid = threadIdx.x, w = tid >> 5, t = tid & 31, a = t >> 2, j = t & 3;
     const int vl = 8 * w + a;
+    // Before pdl_wait (a programmatic launch overlaps the preceding QKV projection): the row's slot
+    // and length (written two or more launches back), its page numbers, and the K/V of every
+    // position but the last T (the rows of this pass): those the QKV projection is appending.
     const int s = rows.slot[r];
     const int L = rows.L[r];
-    float q[8];
-    unpack8(*reinterpret_cast<const uint4*>(q16 + (size_t)r * kD + h * kHeadDim + 8 * j), q);
+    const int T = gridDim.x / kHeads;
     const int32_t* pt = kv.ptab + (size_t)s * kv.max_pages;
     const int np = (L + kPage - 1) / kPage;
     for (int i = tid; i < np; i += 128) s_pt[i] = pt[i];
@@ -1119,8 +1158,11 @@ __global__ void __launch_bounds__(128) k_attn_decode_split(const uint16_t* __res
     const unsigned gmask = 0xFu << (4 * a);                  // the four threads of the lane
     // position vl + 32k lies in page k / 2 at vl + 32 (k & 1)
     const uint16_t* kvb = kv_head_base(kv, layer, h) + vl * kHeadDim + 8 * j;
+    // this lane's last position is among the ones being appended (at most one per lane: T < 32)
+    const bool new_last = nk > 0 && vl + kAttnLanes * (nk - 1) >= L - T;
+    bool early = true;   // issuing before pdl_wait
     auto issue = [&](int k) {
-        if (k < nk) {
+        if (k < nk && !(early && new_last && k == nk - 1)) {
             const uint16_t* kp = kvb + (size_t)s_pt[k >> 1] * kPageElems + (k & 1) * (kAttnLanes * kHeadDim);
             uint8_t* dst = dsm + (size_t)(k % kQD) * 2 * 128 * 16 + tid * 16;
             cp_async16(dst, kp, true);
@@ -1132,6 +1174,18 @@ __global__ void __launch_bounds__(128) k_attn_decode_split(const uint16_t* __res
     // updates run in position order; each pair refills the two slots the previous pair read
 #pragma unroll
     for (int k = 0; k < kQD - 2; ++k) issue(k);
+    early = false;
+    pdl_wait();
+    pdl_trigger();
+    float q[8];
+    unpack8(*reinterpret_cast<const uint4*>(q16 + (size_t)r * kD + h * kHeadDim + 8 * j), q);
+    if (new_last && nk - 1 < kQD - 2) {   // its slot was committed empty above: read it now
+        const int k = nk - 1;
+        const uint16_t* kp = kvb + (size_t)s_pt[k >> 1] * kPageElems + (k & 1) * (kAttnLanes * kHeadDim);
+        uint8_t* dst = dsm + (size_t)(k % kQD) * 2 * 128 * 16 + tid * 16;
+        *reinterpret_cast<uint4*>(dst) = __ldcg(reinterpret_cast<const uint4*>(kp));
+        *reinterpret_cast<uint4*>(dst + 128 * 16) = __ldcg(reinterpret_cast<const uint4*>(kp + kHalfPageElems));
+    }
     for (int k = 0; k < nk; k += 2) {
         asm volatile("" ::: "memory");   // the previous pair's reads of those slots stay before the refill
         issue(k + kQD - 2);
@@ -1210,8 +1264,8 @@ __global__ void __launch_bounds__(128) k_attn_decode_split(const uint16_t* __res
 // (Staging f32 instead, converted once for all rows, was slower: twice the shared-memory reads.)
 __global__ void __launch_bounds__(512, 1) k_attn_group(const int2* __restrict__ groups, const uint16_t* __restrict__ q16,
                                                        Rows rows, KVView kv, int layer, float scale, float* __restrict__ out) {
-    pdl_trigger();
     pdl_wait();
+    pdl_trigger();
     __shared__ __align__(16) uint8_t sm[2][2][kPage * kHeadDim * 2];   // [buffer][K|V][64 positions x 64 B]
     __shared__ int s_lmax;
     const int2 gr = groups[blockIdx.x >> 4];   // (first row, rows)
@@ -1352,8 +1406,8 @@ void attention_decode(int T, const uint16_t* q16, Rows rows, KVView kv, int laye
 __global__ void k_residual_ln(int T, const float* __restrict__ a, const float* __restrict__ b,
                               const float* __restrict__ g, const float* __restrict__ beta, float eps,
                               float* __restrict__ y, int qtype, ActQ qo) {
-    pdl_trigger();
     pdl_wait();
+    pdl_trigger();
     const int lane = threadIdx.x & 31;
     const int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     if (r >= T) return;
@@ -1374,8 +1428,8 @@ void residual_layernorm(int T, const float* a, const float* b, const float* g, c
 __global__ void k_sample_greedy(const float* __restrict__ logits, int V, const int32_t* __restrict__ row_slot,
                                 const uint8_t* __restrict__ seen, float rp, float inv_rp, int eos_mask, int eos,
                                 int32_t* __restrict__ tok_out, int32_t* __restrict__ greedy_out) {
-    pdl_trigger();
     pdl_wait();
+    pdl_trigger();
     __shared__ float s_v[8];
     __shared__ int s_i[8];
     const int r = blockIdx.x;
@@ -1441,8 +1495,8 @@ __global__ void __launch_bounds__(1024) k_sample_full(const float* __restrict__ 
                                                       const int32_t* __restrict__ row_slot,
                                                       const uint8_t* __restrict__ seen, SamplerArgs a,
                                                       int32_t* __restrict__ tok_out, int32_t* __restrict__ greedy_out) {
-    pdl_trigger();
     pdl_wait();
+    pdl_trigger();
     __shared__ float key[kSortN];
     __shared__ int idx[kSortN];
     __shared__ float prob[kSortN];
@@ -1560,8 +1614,8 @@ void sample_full(int T, const float* logits, int V, const int32_t* row_slot, con
 __global__ void k_advance(int T, const int32_t* __restrict__ row_slot, const int32_t* __restrict__ tok,
                           int32_t* __restrict__ token_in, int32_t* __restrict__ n_pos, uint8_t* __restrict__ seen, int V,
                           int32_t* __restrict__ ring, int ring_len, int32_t* __restrict__ ring_step) {
-    pdl_trigger();
     pdl_wait();
+    pdl_trigger();
     const int step = *ring_step;
     for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < T; r += gridDim.x * blockDim.x) {
         const int s = row_slot[r];
@@ -1574,8 +1628,8 @@ __global__ void k_advance(int T, const int32_t* __restrict__ row_slot, const int
 }
 
 __global__ void k_step_inc(int32_t* ring_step) {
-    pdl_trigger();
-    pdl_wait(); *ring_step += 1; }
+    pdl_wait();
+    pdl_trigger(); *ring_step += 1; }
 
 void advance(int T, const int32_t* row_slot, const int32_t* tok, int32_t* token_in, int32_t* n_pos, uint8_t* seen,
              int V, int32_t* ring, int ring_len, int32_t* ring_step, cudaStream_t st) {
@@ -1585,8 +1639,8 @@ void advance(int T, const int32_t* row_slot, const int32_t* tok, int32_t* token_
 
 __global__ void k_gather_rows(int n, const float* __restrict__ src, const int32_t* __restrict__ idx, int ld,
                               float* __restrict__ dst) {
-    pdl_trigger();
     pdl_wait();
+    pdl_trigger();
     const int r = blockIdx.x;
     if (r >= n) return;
     for (int c = threadIdx.x; c < ld; c += blockDim.x) dst[(size_t)r * ld + c] = src[(size_t)idx[r] * ld + c];
@@ -1603,8 +1657,8 @@ __global__ void k_embed_prefill(int T_text, int T_prompt, const int32_t* __restr
                                 const uint16_t* __restrict__ text16, const float* __restrict__ text32,
                                 const uint16_t* __restrict__ audio16, const float* __restrict__ audio32,
                                 const float* __restrict__ pe, float alpha_t, float alpha_a, float* __restrict__ x) {
-    pdl_trigger();
     pdl_wait();
+    pdl_trigger();
     const int r = blockIdx.x;
     for (int d = threadIdx.x; d < kD; d += blockDim.x) {
         float v;

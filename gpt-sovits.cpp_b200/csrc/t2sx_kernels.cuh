@@ -11,6 +11,14 @@ namespace t2sx {
 // serialization (PDL): each kernel lets its successor launch early and waits for its predecessor
 // before touching data that predecessor produced (see pdl_wait in t2sx_math.cuh).
 bool pdl_enabled();
+// Launches made on this host thread while a PdlScope(true) lives carry the attribute as well.
+struct PdlScope {
+    explicit PdlScope(bool on);
+    ~PdlScope();
+    PdlScope(const PdlScope&) = delete;
+    PdlScope& operator=(const PdlScope&) = delete;
+    bool prev;
+};
 
 template <typename... KArgs, typename... Args>
 inline void launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args&&... args) {

@@ -205,9 +205,10 @@ __device__ __forceinline__ int q8k_q(float iscale, float v) {
 namespace t2sx {
 // Programmatic dependent launch (sm_90+): `pdl_trigger` lets the next kernel in the stream begin
 // launching; `pdl_wait` blocks until the preceding kernel has completed and its writes are
-// visible.  A kernel may only read data produced by earlier kernels after pdl_wait; before it,
-// only data constant across the decode step (weights, page tables).  Both are no-ops when the
-// kernel was launched without the programmatic-serialization attribute.
+// visible.  Every kernel triggers only after its own wait, so a kernel that starts early overlaps
+// its predecessor alone: before pdl_wait it may read constants (weights, page tables, K/V of
+// earlier steps) and data of kernels two or more launches back, never its predecessor's output.
+// Both are no-ops when the kernel was launched without the programmatic-serialization attribute.
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
 }  // namespace t2sx

@@ -76,8 +76,8 @@ __global__ void __launch_bounds__(64 * WN_) k_mm_mma(DevW W, ActQ A, int M, cons
     const int N = W.N, K = W.K;
     const int nb32 = K / 32, nsb = K / 256;
     const int nstage = K / (32 * KB);
-    pdl_trigger();
     pdl_wait();
+    pdl_trigger();
 
     auto sW = [&](int buf) { return smem + buf * C::STAGE; };
     auto sX = [&](int buf) { return smem + buf * C::STAGE + C::W_BYTES; };

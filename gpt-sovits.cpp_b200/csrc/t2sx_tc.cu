@@ -238,7 +238,6 @@ k_mm_tc_q4k(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUt
     const uint32_t full0 = smem_u32(bars), empty0 = full0 + 8 * NS, tfull0 = empty0 + 8 * NS,
                    tempty0 = tfull0 + 8 * NBUF, done_bar = tempty0 + 8 * NBUF;
 
-    pdl_trigger();
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (tid == 0) {   // the producer's first copies need both descriptors
         asm volatile("prefetch.tensormap [%0];\n" ::"l"((uint64_t)&tmW) : "memory");
@@ -280,6 +279,7 @@ k_mm_tc_q4k(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUt
 
     // the set-up above touches no data of earlier kernels; everything below may
     pdl_wait();
+    pdl_trigger();
     bool aborted = false;
     if (warp < EPI_WARP0) {   // control warpgroup: warp 0 TMA, warps 1-3 MMA (one plane each)
         asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;\n" ::"n"(kCtrlRegs));
