@@ -638,6 +638,13 @@ struct t2sx_session {
     bool graph_noise = false;      // sampler kind captured in the step graph
     float last_ms = 0.0f;
     std::vector<int32_t> active;   // slots in row order
+    int graph_gen = 0;             // bumped whenever the step graph is instantiated
+    // t2sx_decode_step_host with tokens in and out: one graph (pinned token copies, scatter,
+    // ring reset, timing events, the step, the token copy back) built for graph_gen
+    cudaGraphExec_t host_graph = nullptr;
+    int host_gen = -1;
+    int32_t* pin_in = nullptr;     // [n_slots] pinned
+    int32_t* pin_out = nullptr;    // [n_slots] pinned
 };
 
 static Rows rows_of(t2sx_session* s, Work& w) {
@@ -808,6 +815,9 @@ static void free_session(t2sx_session* s) {
     cudaSetDevice(s->device);
     if (s->st) cudaStreamSynchronize(s->st);
     if (s->graph) cudaGraphExecDestroy(s->graph);
+    if (s->host_graph) cudaGraphExecDestroy(s->host_graph);
+    if (s->pin_in) cudaFreeHost(s->pin_in);
+    if (s->pin_out) cudaFreeHost(s->pin_out);
     for (void* p : {(void*)s->pool, (void*)s->ptab, (void*)s->n_pos, (void*)s->audio_off, (void*)s->token_in, (void*)s->cap,
                     (void*)s->err, (void*)s->seen, (void*)s->pe, (void*)s->dec.mem, (void*)s->pre.mem, (void*)s->ring,
                     (void*)s->ring_step, (void*)s->scratch_i, (void*)s->noise, (void*)s->tail_ctr})
@@ -1180,6 +1190,7 @@ static int prepare_decode(t2sx_session* s, int n_steps) {
             if (e != cudaSuccess) { s->graph = nullptr; return fail(T2SX_ERR_CUDA, "decode graph instantiate: %s", cudaGetErrorString(e)); }
             s->dec_rows = T;
             s->graph_noise = s->noise_on;
+            ++s->graph_gen;
         }
         s->dec_dirty = false;
     }
@@ -1252,6 +1263,43 @@ __global__ void k_scatter_tokens(int T, const int32_t* row_slot, const int32_t* 
     if (r < T) token_in[row_slot[r]] = tok[r];
 }
 
+// The host-step graph (T2SX_HOST_GRAPH=0: separate copies and launches, as before).
+static bool host_graph_on() {
+    static const bool v = [] {
+        const char* e = getenv("T2SX_HOST_GRAPH");
+        return !(e && e[0] == '0');
+    }();
+    return v;
+}
+
+// Captures, for the current step graph, the whole host step: pinned tokens -> device, scatter to
+// the slots, ring reset, timing event, the step, timing event, next tokens -> pinned.
+static int build_host_graph(t2sx_session* s) {
+    if (s->host_graph && s->host_gen == s->graph_gen) return T2SX_OK;
+    if (s->host_graph) { cudaGraphExecDestroy(s->host_graph); s->host_graph = nullptr; }
+    if (!s->pin_in) CK(cudaHostAlloc((void**)&s->pin_in, (size_t)s->n_slots * 4, cudaHostAllocDefault));
+    if (!s->pin_out) CK(cudaHostAlloc((void**)&s->pin_out, (size_t)s->n_slots * 4, cudaHostAllocDefault));
+    const int T = (int)s->active.size();
+    cudaGraph_t g;
+    CK(cudaStreamBeginCapture(s->st, cudaStreamCaptureModeThreadLocal));
+    cudaMemcpyAsync(s->scratch_i, s->pin_in, (size_t)T * 4, cudaMemcpyHostToDevice, s->st);
+    k_scatter_tokens<<<(T + 255) / 256, 256, 0, s->st>>>(T, s->dec.row_slot, s->scratch_i, s->token_in);
+    cudaMemsetAsync(s->ring_step, 0, 4, s->st);
+    cudaEventRecordWithFlags(s->ev0, s->st, cudaEventRecordExternal);   // (event-record nodes, not capture markers)
+    enqueue_step(s);
+    cudaEventRecordWithFlags(s->ev1, s->st, cudaEventRecordExternal);
+    cudaMemcpyAsync(s->pin_out, s->dec.tok, (size_t)T * 4, cudaMemcpyDeviceToHost, s->st);
+    cudaError_t e = cudaStreamEndCapture(s->st, &g);
+    if (e != cudaSuccess) return fail(T2SX_ERR_CUDA, "host step graph capture: %s", cudaGetErrorString(e));
+    e = cudaGetLastError();
+    if (e != cudaSuccess) { cudaGraphDestroy(g); return fail(T2SX_ERR_CUDA, "host step graph: %s", cudaGetErrorString(e)); }
+    e = cudaGraphInstantiate(&s->host_graph, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) { s->host_graph = nullptr; return fail(T2SX_ERR_CUDA, "host step graph instantiate: %s", cudaGetErrorString(e)); }
+    s->host_gen = s->graph_gen;
+    return T2SX_OK;
+}
+
 extern "C" int t2sx_decode_step_host(t2sx_session* s, const int32_t* tokens_in, int32_t* tokens_out) {
     if (!s) return fail(T2SX_ERR_INVALID, "null session");
     CK(cudaSetDevice(s->m->device));
@@ -1262,9 +1310,24 @@ extern "C" int t2sx_decode_step_host(t2sx_session* s, const int32_t* tokens_in, 
     int rc;
     if ((rc = prepare_decode(s, 1))) return rc;
     const int T = (int)s->active.size();
-    if (tokens_in) {
+    if (tokens_in)
         for (int i = 0; i < T; ++i)
             if (tokens_in[i] < 0 || tokens_in[i] >= s->m->audio_rows) return fail(T2SX_ERR_INVALID, "token id %d out of range", tokens_in[i]);
+    if (tokens_in && tokens_out && host_graph_on()) {
+        // one launch per step: the tokens pass through session-owned pinned buffers
+        if ((rc = build_host_graph(s))) return rc;
+        memcpy(s->pin_in, tokens_in, (size_t)T * 4);
+        CK(cudaGraphLaunch(s->host_graph, s->st));
+        for (int sl : s->active) s->n_pos_h[sl] += 1;
+        s->last_rows = T;
+        s->last_logits = s->dec.logits;
+        s->last_greedy = s->dec.greedy;
+        CK(cudaStreamSynchronize(s->st));
+        memcpy(tokens_out, s->pin_out, (size_t)T * 4);
+        CK(cudaEventElapsedTime(&s->last_ms, s->ev0, s->ev1));
+        return T2SX_OK;
+    }
+    if (tokens_in) {
         CK(cudaMemcpyAsync(s->scratch_i, tokens_in, T * 4, cudaMemcpyHostToDevice, s->st));
         k_scatter_tokens<<<(T + 255) / 256, 256, 0, s->st>>>(T, s->dec.row_slot, s->scratch_i, s->token_in);
         CK(cudaGetLastError());
