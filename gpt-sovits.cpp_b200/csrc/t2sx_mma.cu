@@ -12,6 +12,8 @@
 // the A fragment's byte order; a Q4_0 block's 16 bytes hold elements j (low nibble) and j+16
 // (high nibble), i.e. exactly the a0/a2 (and a1/a3) register pairs of one 32-bit load.
 #include "t2sx_kernels.cuh"
+
+#include <cstdlib>
 #include "t2sx_math.cuh"
 #include "t2sx_kv.cuh"
 
@@ -32,13 +34,14 @@ __device__ __forceinline__ float i2f_small(int i) { return __fsub_rn(__int_as_fl
 constexpr int KB = 4;            // 32-element blocks per stage
 constexpr int XROW = KB * 32 + 16;   // smem bytes per activation row (int8, padded)
 
-template <int WT, int MT_, int WN_, int NSTG_ = 2>
+template <int WT, int MT_, int WN_, int NSTG_ = 2, int IT_ = 2>
 struct Cfg {
     static constexpr int NSTG = NSTG_;                            // cp.async ring depth (stages)
     static constexpr int MT = MT_;                                // m8 tiles per warp
     static constexpr int WN = WN_;                                // warps along the weight rows
+    static constexpr int IT = IT_;                                // m16 weight-row tiles per warp
     static constexpr int NT = 64 * WN;                            // threads (WN x 2 warps)
-    static constexpr int BN = 32 * WN;                            // weight rows per CTA
+    static constexpr int BN = 16 * IT * WN;                       // weight rows per CTA
     static constexpr int BM = 2 * 8 * MT;                         // activation rows per CTA
     static constexpr int WROW = (WT == W_Q8_0) ? KB * 32 + 16 : KB * 16 + 16;  // weight bytes per row
     static constexpr int W_BYTES = BN * WROW;
@@ -62,12 +65,12 @@ __device__ __forceinline__ void qkv_store_m(const QKVStore& e, int m, int n, flo
     e.kv.pool[kv_off(e.kv, page, e.layer, which, j / kHeadDim, pos % kPage) + (j % kHeadDim)] = h;
 }
 
-template <int WT, int MT_, int WN_, int NSTG_>
+template <int WT, int MT_, int WN_, int NSTG_, int IT_>
 __global__ void __launch_bounds__(64 * WN_) k_mm_mma(DevW W, ActQ A, int M, const float* __restrict__ bias, int relu,
                                                 float* __restrict__ y, QKVStore qkv, int use_qkv) {
-    using C = Cfg<WT, MT_, WN_, NSTG_>;
+    using C = Cfg<WT, MT_, WN_, NSTG_, IT_>;
     constexpr int NSTG = C::NSTG;
-    constexpr int MT = C::MT, BM = C::BM, WROW = C::WROW, BN = C::BN, NT = C::NT;
+    constexpr int MT = C::MT, BM = C::BM, WROW = C::WROW, BN = C::BN, NT = C::NT, IT = C::IT;
     extern __shared__ __align__(16) uint8_t smem[];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int g = lane >> 2, t = lane & 3;
@@ -146,10 +149,10 @@ __global__ void __launch_bounds__(64 * WN_) k_mm_mma(DevW W, ActQ A, int M, cons
         cp_commit();
     };
 
-    float acc[2][MT][4], accm[2][MT][4];
-    int sa[2][MT][4], sm[2][MT][4];
+    float acc[IT][MT][4], accm[IT][MT][4];
+    int sa[IT][MT][4], sm[IT][MT][4];
 #pragma unroll
-    for (int i = 0; i < 2; ++i)
+    for (int i = 0; i < IT; ++i)
 #pragma unroll
         for (int j = 0; j < MT; ++j)
 #pragma unroll
@@ -176,10 +179,10 @@ __global__ void __launch_bounds__(64 * WN_) k_mm_mma(DevW W, ActQ A, int M, cons
         const uint8_t* x = sX(buf);
 #pragma unroll
         for (int blk = 0; blk < KB; ++blk) {
-            int af[2][4];
+            int af[IT][4];
 #pragma unroll
-            for (int i = 0; i < 2; ++i) {
-                const int r0 = wn * 32 + i * 16 + g;
+            for (int i = 0; i < IT; ++i) {
+                const int r0 = wn * (16 * IT) + i * 16 + g;
                 if (WT == W_Q8_0) {
                     af[i][0] = lds32(w + r0 * WROW + blk * 32 + t * 4);
                     af[i][1] = lds32(w + (r0 + 8) * WROW + blk * 32 + t * 4);
@@ -213,9 +216,9 @@ __global__ void __launch_bounds__(64 * WN_) k_mm_mma(DevW W, ActQ A, int M, cons
                 bf[j][0] = lds32(x + mr * XROW + blk * 32 + t * 4);
                 bf[j][1] = lds32(x + mr * XROW + blk * 32 + 16 + t * 4);
             }
-            int is[2][MT][4];
+            int is[IT][MT][4];
 #pragma unroll
-            for (int i = 0; i < 2; ++i)
+            for (int i = 0; i < IT; ++i)
 #pragma unroll
                 for (int j = 0; j < MT; ++j)
                     mma_s8(is[i][j], af[i][0], af[i][1], af[i][2], af[i][3], bf[j][0], bf[j][1]);
@@ -224,8 +227,8 @@ __global__ void __launch_bounds__(64 * WN_) k_mm_mma(DevW W, ActQ A, int M, cons
                 const uint8_t* scm = sScm(buf);
                 const int* bs = reinterpret_cast<const int*>(sDx(buf));
 #pragma unroll
-                for (int i = 0; i < 2; ++i) {
-                    const int nr = wn * 32 + i * 16 + g;
+                for (int i = 0; i < IT; ++i) {
+                    const int nr = wn * (16 * IT) + i * 16 + g;
                     const int sc0 = scm[nr * 16 + js], sc1 = scm[(nr + 8) * 16 + js];
                     const int mn0 = scm[nr * 16 + 8 + js], mn1 = scm[(nr + 8) * 16 + 8 + js];
 #pragma unroll
@@ -242,8 +245,8 @@ __global__ void __launch_bounds__(64 * WN_) k_mm_mma(DevW W, ActQ A, int M, cons
                 const float* dw = sDw(buf);
                 const float* dx = sDx(buf);
 #pragma unroll
-                for (int i = 0; i < 2; ++i) {
-                    const int nr = wn * 32 + i * 16 + g;
+                for (int i = 0; i < IT; ++i) {
+                    const int nr = wn * (16 * IT) + i * 16 + g;
                     const float w0 = dw[nr * KB + blk], w1 = dw[(nr + 8) * KB + blk];
 #pragma unroll
                     for (int j = 0; j < MT; ++j) {
@@ -261,8 +264,8 @@ __global__ void __launch_bounds__(64 * WN_) k_mm_mma(DevW W, ActQ A, int M, cons
             const float* dd = sDd(buf);
             const float* dx8 = sDx8(buf);
 #pragma unroll
-            for (int i = 0; i < 2; ++i) {
-                const int nr = wn * 32 + i * 16 + g;
+            for (int i = 0; i < IT; ++i) {
+                const int nr = wn * (16 * IT) + i * 16 + g;
                 const float dw0 = dd[2 * nr], dm0 = dd[2 * nr + 1], dw1 = dd[2 * (nr + 8)], dm1 = dd[2 * (nr + 8) + 1];
 #pragma unroll
                 for (int j = 0; j < MT; ++j) {
@@ -281,12 +284,12 @@ __global__ void __launch_bounds__(64 * WN_) k_mm_mma(DevW W, ActQ A, int M, cons
         }
     }
 #pragma unroll
-    for (int i = 0; i < 2; ++i)
+    for (int i = 0; i < IT; ++i)
 #pragma unroll
         for (int j = 0; j < MT; ++j)
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-                const int n = n0 + wn * 32 + i * 16 + g + ((e >> 1) << 3);
+                const int n = n0 + wn * (16 * IT) + i * 16 + g + ((e >> 1) << 3);
                 const int m = m0 + wm * (8 * MT) + j * 8 + 2 * t + (e & 1);
                 if (n < N && m < M) {
                     float v = (WT == W_Q4_K) ? __fadd_rn(acc[i][j][e], accm[i][j][e]) : acc[i][j][e];
@@ -298,20 +301,20 @@ __global__ void __launch_bounds__(64 * WN_) k_mm_mma(DevW W, ActQ A, int M, cons
             }
 }
 
-template <int WT, int MT, int WN = 4, int NSTG = 2>
+template <int WT, int MT, int WN = 4, int NSTG = 2, int IT = 2>
 static void launch_mma(const DevW& W, const ActQ& a, int M, const float* bias, int relu, float* y, const QKVStore* qkv,
                        cudaStream_t st) {
-    using C = Cfg<WT, MT, WN, NSTG>;
+    using C = Cfg<WT, MT, WN, NSTG, IT>;
     static bool configured = false;   // the attribute is per function; set once per process
     if (!configured) {
-        if (cudaFuncSetAttribute(k_mm_mma<WT, MT, WN, NSTG>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess)
+        if (cudaFuncSetAttribute(k_mm_mma<WT, MT, WN, NSTG, IT>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess)
             return;   // the launch below then fails and the caller's launch check reports it
         configured = true;
     }
     dim3 grid((W.N + C::BN - 1) / C::BN, (M + C::BM - 1) / C::BM);
     QKVStore q{};
     if (qkv) q = *qkv;
-    launch_k((k_mm_mma<WT, MT, WN, NSTG>), grid, dim3(C::NT), C::SMEM, st, W, a, M, bias, relu, y, q, qkv ? 1 : 0);
+    launch_k((k_mm_mma<WT, MT, WN, NSTG, IT>), grid, dim3(C::NT), C::SMEM, st, W, a, M, bias, relu, y, q, qkv ? 1 : 0);
 }
 
 bool matmul_mma(const DevW& W, const ActQ& a, int M, const float* bias, int relu, float* y, const QKVStore* qkv,
@@ -333,13 +336,22 @@ bool matmul_mma(const DevW& W, const ActQ& a, int M, const float* bias, int relu
 // per weight row.  16-row tiles also for 17-32 rows: the 512-wide projections then run on 32
 // CTAs instead of 16 (32 sessions: 1.66 -> 1.44 ms per decode step).  With few CTAs per SM the
 // K loop is latency-bound, so the ring keeps 5 stages (640 elements of K) in flight.
+// 16 weight rows per narrow CTA (T2SX_NARROW_W32=1: 32, two m16 tiles per warp).
+static bool narrow16() {
+    static const bool v = [] {
+        const char* e = getenv("T2SX_NARROW_W32");
+        return !(e && e[0] == '1');
+    }();
+    return v;
+}
+
 bool matmul_mma_narrow(const DevW& W, const ActQ& a, int M, const float* bias, int relu, float* y, const QKVStore* qkv,
                        cudaStream_t st) {
     if (W.K % (32 * KB) || M > 32) return false;
     switch (W.type) {
-        case W_Q8_0: launch_mma<W_Q8_0, 1, 1, 6>(W, a, M, bias, relu, y, qkv, st); return true;
-        case W_Q4_0: launch_mma<W_Q4_0, 1, 1, 6>(W, a, M, bias, relu, y, qkv, st); return true;
-        case W_Q4_K: launch_mma<W_Q4_K, 1, 1, 6>(W, a, M, bias, relu, y, qkv, st); return true;
+        case W_Q8_0: narrow16() ? launch_mma<W_Q8_0, 1, 1, 6, 1>(W, a, M, bias, relu, y, qkv, st) : launch_mma<W_Q8_0, 1, 1, 6>(W, a, M, bias, relu, y, qkv, st); return true;
+        case W_Q4_0: narrow16() ? launch_mma<W_Q4_0, 1, 1, 6, 1>(W, a, M, bias, relu, y, qkv, st) : launch_mma<W_Q4_0, 1, 1, 6>(W, a, M, bias, relu, y, qkv, st); return true;
+        case W_Q4_K: narrow16() ? launch_mma<W_Q4_K, 1, 1, 6, 1>(W, a, M, bias, relu, y, qkv, st) : launch_mma<W_Q4_K, 1, 1, 6>(W, a, M, bias, relu, y, qkv, st); return true;
     }
     return false;
 }
