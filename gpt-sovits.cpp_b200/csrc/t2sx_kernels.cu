@@ -1382,8 +1382,10 @@ void attention_decode(int T, const uint16_t* q16, Rows rows, KVView kv, int laye
         // for the 2048-row decode step)
         launch_k((k_attn_decode<4, false>), dim3(T * (kHeads / 4)), dim3(128), 0, st, q16, rows, kv, layer, scale, out, -1, qo);
         quantize_act(W_Q4_K, out, T, kD, qo, st);
-    } else if (T < pipe1_rows() && attn_split()) {
-        // very few rows: one head per CTA, four threads per position lane
+    } else if (T < pipe1_rows() && T <= kAttnLanes && attn_split()) {
+        // very few rows: one head per CTA, four threads per position lane (at most 32 rows: the
+        // positions of a pass are then at most one per position lane, which the kernel's early
+        // K/V fetch relies on)
         static bool configured = false;
         if (!configured) {
             cudaFuncSetAttribute(k_attn_decode_split, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
