@@ -677,8 +677,9 @@ static ActQ act_for(Work& w, const float* f32_input) {
 // The post-norm layers over T rows (block.cpp:513-637).  On entry w.x holds the input rows (f32)
 // and the activation buffer holds them in layer 0's QKV dot type; on exit w.x holds the output
 // rows and, when final_qtype >= 0, the activation buffer holds them in that dot type.  For one or
-// two rows the residual + LayerNorm runs in the last CTA of the preceding matmul; otherwise it is
-// its own kernel.
+// two rows the residual + LayerNorm runs at the start of the matmul that consumes it (Q8_0/Q4_0
+// QKV and FFN-up weights) or in the last CTA of the preceding matmul (other weight types);
+// otherwise it is its own kernel.
 // Rows up to which the residual + LayerNorm runs as the last CTA's tail of the preceding matmul
 // (T2SX_LN_TAIL_ROWS overrides; 0 = always a separate kernel).
 static int tail_rows() {

@@ -7,9 +7,10 @@
 
 namespace t2sx {
 
-// With T2SX_PDL=1 in the environment, kernels are launched with programmatic stream
-// serialization (PDL): each kernel lets its successor launch early and waits for its predecessor
-// before touching data that predecessor produced (see pdl_wait in t2sx_math.cuh).
+// With T2SX_PDL=1 in the environment, or inside a PdlScope(true) (the one- and two-row layer
+// chain), kernels are launched with programmatic stream serialization (PDL): a kernel may start
+// while its predecessor runs and waits for it before touching data it produced (see pdl_wait in
+// t2sx_math.cuh for what may be read before the wait).
 bool pdl_enabled();
 // Launches made on this host thread while a PdlScope(true) lives carry the attribute as well.
 struct PdlScope {
