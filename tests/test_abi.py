@@ -45,3 +45,31 @@ def test_weight_create_rejects_large_k(t2sx_mod):
     assert L.t2sx_weight_create(0, 8, buf, 1, K, ctypes.byref(h)) == t2sx_mod.ERR_INVALID
     assert b"K above 2048" in L.t2sx_last_error()
     assert not h.value
+
+
+def test_header_compiles_as_c_and_links(t2sx_mod, tmp_path):
+    """include/t2sx.h is a C header: a C99 program (the kind a cgo or plain-C caller writes) compiles
+    warning-free against it, links to the library and runs its host-side error paths without a GPU."""
+    import shutil
+    import subprocess
+    gcc = shutil.which("gcc")
+    assert gcc, "gcc is required to build the C program"
+    src = tmp_path / "abi_c.c"
+    src.write_text(
+        '#include <stdio.h>\n'
+        '#include "t2sx.h"\n'
+        'int main(void) {\n'
+        '    t2sx_model* m = 0;\n'
+        '    if (t2sx_version() != 1) return 1;\n'
+        '    if (t2sx_model_load(0, 0, &m) != T2SX_ERR_INVALID || m) return 2;\n'
+        '    puts(t2sx_last_error());\n'
+        '    return 0;\n'
+        '}\n')
+    exe = str(tmp_path / "abi_c")
+    pkg = os.path.dirname(t2sx_mod.LIB_PATH)
+    r = subprocess.run([gcc, "-std=c99", "-Wall", "-Wextra", "-Werror", "-pedantic", "-I", os.path.join(ROOT, "include"),
+                        str(src), "-L", pkg, "-lt2sx", f"-Wl,-rpath,{pkg}", "-o", exe], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    r = subprocess.run([exe], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0, (r.returncode, r.stdout, r.stderr)
+    assert r.stdout.strip()
