@@ -724,7 +724,11 @@ static bool ln_prologue_ok(const t2sx_model* m) {
     return true;
 }
 
-static void run_layers(t2sx_session* s, Work& w, int T, bool decode, int final_qtype) {
+// head / head_out (optional): the logits matmul that follows the layers.  Returns true when it
+// has been run here (the one- and two-row path with Q8_0/Q4_0 logits weights: the last layer's
+// second LayerNorm is its prologue); the caller runs it otherwise.
+static bool run_layers(t2sx_session* s, Work& w, int T, bool decode, int final_qtype, const DevW* head = nullptr,
+                       float* head_out = nullptr) {
     const t2sx_model* m = s->m;
     Rows rows = rows_of(s, w);
     KVView kv = kv_of(s);
@@ -738,6 +742,8 @@ static void run_layers(t2sx_session* s, Work& w, int T, bool decode, int final_q
         // The chain's kernels are launched programmatically (T2SX_PDL_SMALL=0 turns that off):
         // each fetches its weights (the attention its page numbers and earlier positions' K/V)
         // while its predecessor finishes.
+        const LayerD& Z = m->layers[nl - 1];
+        const bool fuse_head = head && head_out && head->K == kD && (head->type == W_Q8_0 || head->type == W_Q4_0);
         {
             PdlScope pdl(pdl_small());
             for (int l = 0; l < nl; ++l) {
@@ -766,10 +772,15 @@ static void run_layers(t2sx_session* s, Work& w, int T, bool decode, int final_q
                 e3.quant_in = true;
                 matmul(L.down, act_for(w, w.h), T, L.down_b, 0, w.f, s->st, e3);
             }
-        }   // (the final norm is launched without the attribute)
-        const LayerD& Z = m->layers[nl - 1];
+            if (fuse_head) {
+                LnIn nz;
+                nz.a = w.ln1; nz.b = w.f; nz.g = Z.ln2_w; nz.beta = Z.ln2_b; nz.y_out = w.x;
+                matmul_ln(*head, nz, T, nullptr, 0, head_out, nullptr, s->st);
+            }
+        }   // (the final norm alone is launched without the attribute)
+        if (fuse_head) return true;
         residual_layernorm(T, w.ln1, w.f, Z.ln2_w, Z.ln2_b, 1e-5f, w.x, final_qtype, act_of(w), s->st);
-        return;
+        return false;
     }
     for (int l = 0; l < nl; ++l) {
         const LayerD& L = m->layers[l];
@@ -809,6 +820,7 @@ static void run_layers(t2sx_session* s, Work& w, int T, bool decode, int final_q
             residual_layernorm(T, w.ln1, w.f, L.ln2_w, L.ln2_b, 1e-5f, w.x, next_q, act_of(w), s->st);
         }
     }
+    return false;
 }
 
 static void free_session(t2sx_session* s) {
@@ -1148,8 +1160,8 @@ static void enqueue_step(t2sx_session* s) {
     Rows rows = rows_of(s, w);
     embed_decode(T, w.row_slot, s->token_in, s->n_pos, s->audio_off, m->audio16, m->audio32, m->audio_rows, s->pe, s->slot_size,
                  m->alpha_audio, rows, w.x, m->layers[0].qkv.type, act_of(w), s->st);
-    run_layers(s, w, T, true, m->lm_head.type);
-    matmul(m->lm_head, act_for(w, w.x), T, nullptr, 0, w.logits, s->st);
+    if (!run_layers(s, w, T, true, m->lm_head.type, &m->lm_head, w.logits))
+        matmul(m->lm_head, act_for(w, w.x), T, nullptr, 0, w.logits, s->st);
     run_sampler(s, T, w.logits, w.row_slot, s->seen, w.tok, w.greedy);
     advance(T, w.row_slot, w.tok, s->token_in, s->n_pos, s->seen, s->V, s->ring, s->ring_len, s->ring_step, s->st);
 }
