@@ -398,6 +398,8 @@ extern "C" int t2sx_model_load(const char* path, int32_t device, t2sx_model** ou
         return fail(T2SX_ERR_FORMAT, "unsupported T2S shape d=%u heads=%u (this build: d=512, 16 heads)", m->hp[1], m->hp[2]);
     const int nl = (int)m->hp[4], ff = (int)m->hp[3], V = (int)m->hp[5];
     if (nl <= 0 || nl > 256 || ff <= 0 || ff % 256 || V <= 0) return fail(T2SX_ERR_FORMAT, "bad hparams");
+    // the few-row matmul keeps a row's 32-element block sums in shared memory (at most 64)
+    if (ff > 2048) return fail(T2SX_ERR_FORMAT, "unsupported FFN width %d (this build: at most 2048)", ff);
     auto need = [&](const std::string& n, int64_t ne0, int64_t ne1, const GTensor** t) -> int {
         auto it = g.t.find(n);
         if (it == g.t.end()) return fail(T2SX_ERR_FORMAT, "tensor '%s' not found in GGUF", n.c_str());

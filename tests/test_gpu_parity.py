@@ -154,6 +154,17 @@ def test_decode_full_model_bs1_bit_exact(t2sx_mod, orc):
     _run_pair(t2sx_mod, orc, path, [(128, 150, 0)], steps=64)
 
 
+def test_model_load_rejects_wide_ffn(t2sx_mod, tmp_path):
+    """A GGUF whose FFN is wider than 2048 (the bound of the few-row matmul's per-row block sums)
+    is refused at load with a format error, not run."""
+    _need_gpu()
+    import synth
+    path = synth.write_gguf(str(tmp_path / "wide_ffn.gguf"), 8, 5, n_layer=1, ff=2304)
+    with pytest.raises(t2sx_mod.T2SXError) as e:
+        t2sx_mod.Model(path)
+    assert e.value.code == t2sx_mod.ERR_FORMAT and "FFN width 2304" in str(e.value)
+
+
 def test_slot_reuse_and_errors(t2sx_mod):
     _need_gpu()
     import synth
