@@ -359,3 +359,18 @@ def test_extract_latent_matches_float64(orc):
     clear = (top2[:, 1] - top2[:, 0]) > 1e-3 * np.abs(top2[:, 1]).clip(1)
     assert clear.sum() > To // 2
     assert np.array_equal(got[clear], want[clear])
+
+
+def test_power_of_two_scaling_matches_division():
+    """The LayerNorm means divide a double sum by d_model = 512; the kernels multiply by 2^-9
+    instead.  Both are the same real number rounded once, so the bits agree, subnormal results
+    included."""
+    rng = np.random.default_rng(0)
+    x = np.concatenate([
+        rng.standard_normal(200_000) * 10.0 ** rng.integers(-30, 30, 200_000),
+        np.ldexp(rng.random(50_000) + 0.5, rng.integers(-1074, -1000, 50_000)),   # results in the subnormal range
+        np.array([0.0, -0.0, np.inf, -np.inf, 5e-324, -5e-324, 1.7976931348623157e308]),
+    ]).astype(np.float64)
+    a = x / 512.0
+    b = x * (1.0 / 512.0)
+    assert np.array_equal(a.view(np.uint64), b.view(np.uint64))
