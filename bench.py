@@ -30,6 +30,17 @@ sys.path.insert(0, os.path.join(ROOT, "oracle"))
 
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 
+# the arithmetic of each weight format's matmuls (the activation rows are converted to the
+# weight's dot type first) and of the KV cache
+DTYPES = {
+    "q4_k": "int8xint8->int32 per 32-block, f32 fold per 256-block (Q4_K weights x Q8_K rows); f16 KV",
+    "q4_0": "int8xint8->int32 per 32-block, f32 fold (Q4_0 weights x Q8_0 rows); f16 KV",
+    "q8_0": "int8xint8->int32 per 32-block, f32 fold (Q8_0 weights x Q8_0 rows); f16 KV",
+    "q5_0": "int8xint8->int32 per 32-block, f32 fold (Q5_0 weights x Q8_0 rows); f16 KV",
+    "f16": "f16xf16->f32 (F16 weights x f16 rows); f16 KV",
+    "f32": "f32; f16 KV",
+}
+
 
 def load_peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
@@ -184,9 +195,14 @@ def run_ours(args):
         return shard.sum_over_ranks(v, device="cuda")
 
     # ---- warm-up: W host-driven steps (also captures the step graph) ----
+    # the token streams of the first n_par sessions (prefill token, then every warm-up and timed
+    # step) are kept for the step-by-step comparison with the CPU oracle after the timed region
+    n_par = min(args.parity_sessions, per) if rank == 0 else 0
+    par_tokens = [first[:n_par].copy()]
     cur = first.copy()
     for _ in range(W):
         cur = sess.decode_step_host(cur, want_tokens=True)
+        par_tokens.append(cur[:n_par].copy())
     n_kernels = sess.graph_kernels()
     ctx_before = np.array([sess.slot_n_pos(i) for i in range(per)], dtype=np.int64)
     prof_start = sess.profile_step(iters=10)
@@ -203,6 +219,7 @@ def run_ours(args):
         t0 = time.perf_counter()
         for _ in range(K):
             cur = sess.decode_step_host(cur, want_tokens=True)
+            par_tokens.append(cur[:n_par].copy())
             ms = sess.last_decode_ms()
             step_ms.append(ms)
             dev_ms += ms
@@ -223,15 +240,25 @@ def run_ours(args):
     attn_bytes = float((ctx_now * 2048).sum() + per * (512 * 2 + 512 * 4))
     attn_gbs = attn_bytes / (prof["attention_kernel"] * 1e-3) / 1e9
     # DRAM bytes per algorithmic byte of this kernel, from one ncu capture (dram__bytes_read.sum +
-    # dram__bytes_write.sum = 189.98 MB for 186.91 MB algorithmic, 256 sessions at context 353,
-    # profiles/k_attn_decode_256sessions.md); the full launch is too large to capture, so its
-    # traffic is that ratio times its algorithmic bytes (the kernel streams each byte once).
+    # dram__bytes_write.sum = 189.98 MB for 186.91 MB algorithmic, 256 sessions at context 353);
+    # the full launch is too large to capture, so its traffic is that ratio times its algorithmic
+    # bytes (the kernel streams each byte once).
     ATTN_DRAM_PER_ALGO_BYTE = 189.981184 / 186.908672
 
-    # ---- CPU baseline (rank 0, N=1 only): the oracle on the host cores, bounded sample ----
-    cpu = None
-    if world == 1 and not args.no_cpu:
-        cpu = cpu_baseline(args.workload, path, args.cpu_sessions, args.cpu_steps)
+    # ---- the bs=1 decode step (the other half of the metric), measured in the same run ----
+    bs1 = None
+    if rank == 0 and args.workload != "bs1_q8_0" and not args.no_bs1:
+        bs1 = bs1_step(local, args.bs1_steps)
+
+    # ---- CPU oracle (rank 0): token parity of the first sessions over all W + K steps; at N=1
+    # its last steps are also the timed CPU baseline (bounded sample) ----
+    cpu = parity = None
+    if rank == 0 and not args.no_cpu:
+        cpu, ref_tok = oracle_streams(args.workload, path, n_par, W + K,
+                                      timed_steps=args.cpu_steps)
+        parity = parity_report(np.stack(par_tokens), ref_tok)
+        if world > 1:
+            cpu = None
 
     peaks, peak_kind = load_peaks()
     if rank == 0:
@@ -248,7 +275,7 @@ def run_ours(args):
             "higher_is_better": True,
             "scaling": "strong",
             "vs_baseline": None,
-            "dtype": "int8xint8->f32 (Q4_K weights), f16 KV",
+            "dtype": DTYPES[w["wtype"]],
             "data": "synthetic (seeded N(0,0.02) weights, uniform ids, N(0,1) BERT features)",
             "config": {
                 "workload": args.workload,
@@ -286,8 +313,11 @@ def run_ours(args):
             "kernel_ms": {k: round(v, 4) for k, v in prof.items()},
             "kernel_ms_at_start": {k: round(v, 4) for k, v in prof_start.items()},
             "clocks": clocks,
-            "first_tokens": [int(t) for t in first[:4]],
         }
+        if parity is not None:
+            line["parity"] = parity
+        if bs1 is not None:
+            line["bs1"] = bs1
         if cpu is not None:
             line["cpu_baseline"] = cpu
         print(json.dumps(line))
@@ -298,16 +328,18 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
-def cpu_baseline(workload, path, n_sessions, n_steps, warm=2):
-    """The oracle (CPU restatement of the reference arithmetic) on the host cores: prefill of
-    `n_sessions` prompts of the workload (untimed), then `n_steps` timed decode steps."""
+def oracle_streams(workload, path, n_sessions, n_steps, timed_steps=None):
+    """The oracle (CPU restatement of the reference arithmetic) on all host cores: prefill of the
+    first `n_sessions` prompts of the workload (untimed), then `n_steps` greedy decode steps.
+    Returns (cpu_baseline dict timed over the last `timed_steps` steps, tokens int32
+    [n_steps + 1][n_sessions]: the prefill token, then one row per decode step)."""
     import oracle
     import synth
     cores = os.cpu_count() or 1
     oracle.set_threads(cores)
     m = oracle.Model(path)
     lengths = synth.workload_lengths(workload)[:n_sessions]
-    cap = max(tt + tp for tt, tp, _ in lengths) + n_steps + warm + 2
+    cap = max(tt + tp for tt, tp, _ in lengths) + n_steps + 2
     s = oracle.Session(m, len(lengths), cap)
     cur = []
     for i, (tt, tp, seed) in enumerate(lengths):
@@ -316,15 +348,68 @@ def cpu_baseline(workload, path, n_sessions, n_steps, warm=2):
         cur.append(s.prefill(i, x, tp)[0])
     slots = np.arange(len(lengths))
     cur = np.array(cur, dtype=np.int32)
+    toks = [cur.copy()]
+    timed = n_steps if timed_steps is None else min(timed_steps, n_steps)
+    t0 = None
+    for k in range(n_steps):
+        if k == n_steps - timed:
+            t0 = time.perf_counter()
+        cur, _ = s.decode(slots, cur)
+        toks.append(cur.copy())
+    dt = time.perf_counter() - t0 if t0 is not None else float("nan")
+    s.close()
+    m.close()
+    cpu = {"value": round(len(lengths) * timed / dt, 3), "unit": "tokens/s", "cores": cores, "kind": "port",
+           "sample": f"{len(lengths)} sessions of {workload}, {timed} timed greedy decode steps after prefill "
+                     f"and {n_steps - timed} untimed ones (oracle restatement; ggml is absent from the "
+                     f"reference snapshot)"}
+    return cpu, np.stack(toks)
+
+
+def bs1_step(device, steps, warm=5):
+    """The bs=1 decode step of the reference's one-session workload (Q8_0 weights seed 0, 128
+    phonemes + 150 prompt tokens, greedy, EOS masked) on this GPU: `warm` untimed steps, then
+    `steps` steps through t2sx_decode_step_host, each timed on the device (CUDA events around
+    the step graph) and on the host (token in, step, token out).  Returns the p50 of both."""
+    import synth
+    import t2sx
+    w = synth.WORKLOADS["bs1_q8_0"]
+    path = synth.ensure_gguf(w["wtype"], w["seed"], n_layer=24)
+    (tt, tp, seed), = synth.workload_lengths("bs1_q8_0")
+    model = t2sx.Model(path, device=device)
+    sess = t2sx.Session(model, 1, tt + tp + warm + steps + 1, repetition_penalty=1.0, eos_mask=True)
+    ph, bert, sem = synth.session_inputs(seed, tt, tp)
+    x = sess.embed_prefill(ph, bert, sem)
+    cur = sess.prefill([0], [tt + tp], [tp], x)
     for _ in range(warm):
-        cur, _ = s.decode(slots, cur)
-    t0 = time.perf_counter()
-    for _ in range(n_steps):
-        cur, _ = s.decode(slots, cur)
-    dt = time.perf_counter() - t0
-    return {"value": round(len(lengths) * n_steps / dt, 3), "unit": "tokens/s", "cores": cores, "kind": "port",
-            "sample": f"{len(lengths)} sessions of {workload}, {n_steps} decode steps after prefill "
-                      f"(oracle restatement; ggml is absent from the reference snapshot)"}
+        cur = sess.decode_step_host(cur, want_tokens=True)
+    ctx0 = sess.slot_n_pos(0)
+    dev, host = [], []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        cur = sess.decode_step_host(cur, want_tokens=True)
+        host.append((time.perf_counter() - t0) * 1e3)
+        dev.append(sess.last_decode_ms())
+    ctx1 = sess.slot_n_pos(0)
+    n_kernels = sess.graph_kernels()
+    sess.close()
+    model.close()
+    return {"workload": "bs1_q8_0", "p50_step_ms": round(float(np.median(dev)), 4),
+            "p50_e2e_step_ms": round(float(np.median(host)), 4), "steps": steps, "warmup": warm,
+            "context": [int(ctx0), int(ctx1)], "kernels_per_step": int(n_kernels),
+            "how": "one session; device ms = CUDA events around the step graph; e2e = host wall clock of "
+                   "t2sx_decode_step_host (token in, step, token out)"}
+
+
+def parity_report(gpu_tokens, ref_tokens):
+    """Step-by-step comparison of GPU and oracle token streams ([steps + 1][sessions], row 0 the
+    prefill token)."""
+    n = min(len(gpu_tokens), len(ref_tokens))
+    g, r = np.asarray(gpu_tokens[:n]), np.asarray(ref_tokens[:n])
+    diff = np.nonzero((g != r).any(axis=1))[0]
+    return {"sessions": int(g.shape[1]), "steps": int(n - 1), "tokens_equal": bool(diff.size == 0),
+            "first_mismatch_step": None if diff.size == 0 else int(diff[0]),
+            "checked": "prefill token and every decode step (warm-up and timed) against the CPU oracle"}
 
 
 # ------------------------------------------------------------------------------------------------
@@ -373,7 +458,7 @@ def run_reference(args):
         "higher_is_better": True,
         "scaling": "strong",
         "vs_baseline": None,
-        "dtype": "int8xint8->f32 (Q4_K weights), f16 KV",
+        "dtype": DTYPES[w["wtype"]],
         "data": "synthetic",
         "config": {"workload": args.workload, "sessions_timed": n_sess, "weights": w["wtype"]},
         "cpu_baseline": {"value": round(value, 3), "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample},
@@ -535,6 +620,10 @@ def main():
     ap.add_argument("--cpu-sessions", type=int, default=8)
     ap.add_argument("--cpu-steps", type=int, default=20)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--parity-sessions", type=int, default=8,
+                    help="sessions whose token streams are compared with the CPU oracle (rank 0)")
+    ap.add_argument("--no-bs1", action="store_true", help="skip the bs=1 step measurement")
+    ap.add_argument("--bs1-steps", type=int, default=200)
     ap.add_argument("--sweep", choices=["matmul", "attention"], default=None,
                     help="isolated kernel sweep instead of the decode workload (--steps = timed iterations)")
     ap.add_argument("--formats", default="q8_0,q4_0,q4_k,f16")

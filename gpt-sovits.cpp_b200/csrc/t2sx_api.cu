@@ -400,6 +400,8 @@ extern "C" int t2sx_model_load(const char* path, int32_t device, t2sx_model** ou
     if (nl <= 0 || nl > 256 || ff <= 0 || ff % 256 || V <= 0) return fail(T2SX_ERR_FORMAT, "bad hparams");
     // the few-row matmul keeps a row's 32-element block sums in shared memory (at most 64)
     if (ff > 2048) return fail(T2SX_ERR_FORMAT, "unsupported FFN width %d (this build: at most 2048)", ff);
+    // the full sampler sorts a row's logits in shared memory (2048 entries)
+    if (V > 2048) return fail(T2SX_ERR_FORMAT, "unsupported vocabulary size %d (this build: at most 2048)", V);
     auto need = [&](const std::string& n, int64_t ne0, int64_t ne1, const GTensor** t) -> int {
         auto it = g.t.find(n);
         if (it == g.t.end()) return fail(T2SX_ERR_FORMAT, "tensor '%s' not found in GGUF", n.c_str());
@@ -488,7 +490,8 @@ extern "C" int t2sx_model_load(const char* path, int32_t device, t2sx_model** ou
     m->alpha_audio = scalar(aa);
     m->wtypes[1] = lm->type; m->wtypes[2] = ae->type; m->wtypes[3] = bw->type;
 
-    CK(cudaSetDevice(device));
+    DeviceGuard dg_;
+    CK(dg_.set(device));
     char* base = nullptr;
     CK(cudaMalloc(&base, ar.used));
     m->arena = base;
@@ -522,7 +525,9 @@ extern "C" int t2sx_model_load(const char* path, int32_t device, t2sx_model** ou
 }
 
 static void release_model(t2sx_model* m) {
-    if (m->arena) { cudaSetDevice(m->device); cudaFree(m->arena); }
+    DeviceGuard dg_;
+    dg_.set(m->device);
+    if (m->arena) cudaFree(m->arena);
     delete m;
 }
 
@@ -827,7 +832,8 @@ static bool run_layers(t2sx_session* s, Work& w, int T, bool decode, int final_q
 
 static void free_session(t2sx_session* s) {
     if (!s) return;
-    cudaSetDevice(s->device);
+    DeviceGuard dg_;
+    dg_.set(s->device);
     if (s->st) cudaStreamSynchronize(s->st);
     if (s->graph) cudaGraphExecDestroy(s->graph);
     if (s->host_graph) cudaGraphExecDestroy(s->host_graph);
@@ -859,7 +865,8 @@ extern "C" int t2sx_session_create(const t2sx_model* m, uint32_t n_slots, uint32
     *out = nullptr;
     if (n_slots == 0 || slot_size == 0) return fail(T2SX_ERR_INVALID, "t2sx_session_create: n_batch and slot_size must be > 0");
     if (n_slots > (1u << 20) || slot_size > (1u << 20)) return fail(T2SX_ERR_INVALID, "t2sx_session_create: sizes too large");
-    CK(cudaSetDevice(m->device));
+    DeviceGuard dg_;
+    CK(dg_.set(m->device));
     t2sx_session* s = new t2sx_session();
     s->m = m;
     s->device = m->device;
@@ -946,7 +953,8 @@ static void rebuild_active(t2sx_session* s) {
 
 extern "C" int t2sx_session_slot_release(t2sx_session* s, int32_t slot) {
     if (!s || slot < 0 || slot >= s->n_slots) return fail(T2SX_ERR_INVALID, "t2sx_session_slot_release: bad slot %d", slot);
-    CK(cudaSetDevice(s->m->device));
+    DeviceGuard dg_;
+    CK(dg_.set(s->m->device));
     CK(cudaStreamSynchronize(s->st));
     for (int p = 0; p < s->pages_per_slot; ++p) {
         int32_t& pg = s->ptab_h[(size_t)slot * s->pages_per_slot + p];
@@ -974,7 +982,9 @@ extern "C" int t2sx_embed_prefill(t2sx_session* s, const int32_t* phones, const 
     if (T > s->slot_size) return fail(T2SX_ERR_INVALID, "t2sx_embed_prefill: %d rows exceed slot_size %d (PE table)", T, s->slot_size);
     for (int i = 0; i < T_text; ++i) if (phones[i] < 0 || phones[i] >= m->text_rows) return fail(T2SX_ERR_INVALID, "phoneme id %d out of range", phones[i]);
     for (int i = 0; i < T_prompt; ++i) if (sem[i] < 0 || sem[i] >= m->audio_rows) return fail(T2SX_ERR_INVALID, "semantic id %d out of range", sem[i]);
-    CK(cudaSetDevice(m->device));
+    DeviceGuard dg_;
+    CK(dg_.set(m->device));
+    ErrScope es_(s->err);   // bounded-wait failures of this call's kernels land here
     int rc = work_alloc(s->pre, T_text > 0 ? (T_text * 2 > T ? T_text * 2 : T) : T, s->V, s->ff);
     if (rc) return rc;
     Work& w = s->pre;
@@ -1003,6 +1013,7 @@ static int check_err_flag(t2sx_session* s) {
     if (e) {
         const int32_t z = 0;
         CK(cudaMemcpy(s->err, &z, 4, cudaMemcpyHostToDevice));
+        if (e == 3) return fail(T2SX_ERR_TIMEOUT, "a tensor-core matmul gave up waiting; the pass's outputs are NaN");
         return fail(T2SX_ERR_BOUNDS, "a slot ran past its KV capacity");
     }
     return T2SX_OK;
@@ -1072,7 +1083,9 @@ extern "C" int t2sx_prefill(t2sx_session* s, int32_t n, const int32_t* slots, co
         if (rc0) return rc0;
     }
     const t2sx_model* m = s->m;
-    CK(cudaSetDevice(m->device));
+    DeviceGuard dg_;
+    CK(dg_.set(m->device));
+    ErrScope es_(s->err);   // bounded-wait failures of this call's kernels land here
     int rc;
     if ((rc = assign_pages(s, n, slots))) return rc;
     // process slots in chunks of at most kChunk rows
@@ -1226,7 +1239,9 @@ static int launch_steps(t2sx_session* s, int n_steps) {
 extern "C" int t2sx_decode_async(t2sx_session* s, int32_t n_steps) {
     if (!s || n_steps < 0) return fail(T2SX_ERR_INVALID, "t2sx_decode_async: bad arguments");
     if (n_steps == 0) return T2SX_OK;
-    CK(cudaSetDevice(s->m->device));
+    DeviceGuard dg_;
+    CK(dg_.set(s->m->device));
+    ErrScope es_(s->err);   // bounded-wait failures of this call's kernels land here
     {
         const cudaError_t stale = cudaGetLastError();
         if (stale != cudaSuccess) return fail(T2SX_ERR_CUDA, "pending CUDA error before decode: %s", cudaGetErrorString(stale));
@@ -1239,7 +1254,8 @@ extern "C" int t2sx_decode_async(t2sx_session* s, int32_t n_steps) {
 
 extern "C" int t2sx_synchronize(t2sx_session* s) {
     if (!s) return fail(T2SX_ERR_INVALID, "null session");
-    CK(cudaSetDevice(s->m->device));
+    DeviceGuard dg_;
+    CK(dg_.set(s->m->device));
     CK(cudaStreamSynchronize(s->st));
     CK(cudaEventElapsedTime(&s->last_ms, s->ev0, s->ev1));
     return check_err_flag(s);
@@ -1248,7 +1264,9 @@ extern "C" int t2sx_synchronize(t2sx_session* s) {
 extern "C" int t2sx_decode(t2sx_session* s, int32_t n_steps, int32_t* tokens_out) {
     if (!s || n_steps < 0) return fail(T2SX_ERR_INVALID, "t2sx_decode: bad arguments");
     if (n_steps == 0) return T2SX_OK;
-    CK(cudaSetDevice(s->m->device));
+    DeviceGuard dg_;
+    CK(dg_.set(s->m->device));
+    ErrScope es_(s->err);   // bounded-wait failures of this call's kernels land here
     {
         const cudaError_t stale = cudaGetLastError();
         if (stale != cudaSuccess) return fail(T2SX_ERR_CUDA, "pending CUDA error before decode: %s", cudaGetErrorString(stale));
@@ -1317,7 +1335,9 @@ static int build_host_graph(t2sx_session* s) {
 
 extern "C" int t2sx_decode_step_host(t2sx_session* s, const int32_t* tokens_in, int32_t* tokens_out) {
     if (!s) return fail(T2SX_ERR_INVALID, "null session");
-    CK(cudaSetDevice(s->m->device));
+    DeviceGuard dg_;
+    CK(dg_.set(s->m->device));
+    ErrScope es_(s->err);   // bounded-wait failures of this call's kernels land here
     {
         const cudaError_t stale = cudaGetLastError();
         if (stale != cudaSuccess) return fail(T2SX_ERR_CUDA, "pending CUDA error before decode: %s", cudaGetErrorString(stale));
@@ -1383,7 +1403,9 @@ extern "C" int t2sx_flex_step(t2sx_session* s, int32_t n_dec, const int32_t* dec
     for (int i = 0; i < n_pre; ++i) T64 += n_query[i];
     if (T64 > kChunk) return fail(T2SX_ERR_INVALID, "t2sx_flex_step: %lld rows in one pass (at most %lld)", (long long)T64, (long long)kChunk);
     const int T = (int)T64, ns = n_dec + n_pre;
-    CK(cudaSetDevice(m->device));
+    DeviceGuard dg_;
+    CK(dg_.set(m->device));
+    ErrScope es_(s->err);   // bounded-wait failures of this call's kernels land here
     {
         const cudaError_t stale = cudaGetLastError();
         if (stale != cudaSuccess) return fail(T2SX_ERR_CUDA, "pending CUDA error before the pass: %s", cudaGetErrorString(stale));
@@ -1458,7 +1480,8 @@ extern "C" int t2sx_active_slots(t2sx_session* s, int32_t* slots, int32_t* n) {
 
 extern "C" int t2sx_read_logits(t2sx_session* s, float* out, int32_t max_rows, int32_t* rows) {
     if (!s || !out) return fail(T2SX_ERR_INVALID, "null argument");
-    CK(cudaSetDevice(s->m->device));
+    DeviceGuard dg_;
+    CK(dg_.set(s->m->device));
     CK(cudaStreamSynchronize(s->st));
     const int n = s->last_rows < max_rows ? s->last_rows : max_rows;
     if (!s->last_logits) return fail(T2SX_ERR_STATE, "no logits yet");
@@ -1470,7 +1493,8 @@ extern "C" int t2sx_read_logits(t2sx_session* s, float* out, int32_t max_rows, i
 extern "C" int t2sx_read_kv(t2sx_session* s, int32_t slot, int32_t layer, int32_t which, uint16_t* out) {
     if (!s || !out || slot < 0 || slot >= s->n_slots || layer < 0 || layer >= s->n_layer || (which != 0 && which != 1))
         return fail(T2SX_ERR_INVALID, "t2sx_read_kv: bad arguments");
-    CK(cudaSetDevice(s->m->device));
+    DeviceGuard dg_;
+    CK(dg_.set(s->m->device));
     CK(cudaStreamSynchronize(s->st));
     const int n = s->n_pos_h[slot];
     std::vector<uint16_t> page((size_t)kHeads * kPage * kHeadDim);
@@ -1489,7 +1513,8 @@ extern "C" int t2sx_read_kv(t2sx_session* s, int32_t slot, int32_t layer, int32_
 extern "C" int t2sx_set_seen(t2sx_session* s, int32_t slot, const uint8_t* seen) {
     if (!s || !seen || slot < 0 || slot >= s->n_slots) return fail(T2SX_ERR_INVALID, "t2sx_set_seen: bad arguments");
     if (!s->seen) return T2SX_OK;  // repetition penalty disabled: nothing to track
-    CK(cudaSetDevice(s->m->device));
+    DeviceGuard dg_;
+    CK(dg_.set(s->m->device));
     CK(cudaMemcpyAsync(s->seen + (size_t)slot * s->V, seen, s->V, cudaMemcpyHostToDevice, s->st));
     CK(cudaStreamSynchronize(s->st));
     return T2SX_OK;
@@ -1506,7 +1531,9 @@ extern "C" int t2sx_decode_graph_kernels(t2sx_session* s, int32_t* n) {
 extern "C" int t2sx_profile_step(t2sx_session* s, int32_t iters, float* ms) {
     if (!s || !ms || iters <= 0) return fail(T2SX_ERR_INVALID, "t2sx_profile_step: bad arguments");
     if (!s->graph) return fail(T2SX_ERR_STATE, "t2sx_profile_step: run a decode step first");
-    CK(cudaSetDevice(s->m->device));
+    DeviceGuard dg_;
+    CK(dg_.set(s->m->device));
+    ErrScope es_(s->err);   // bounded-wait failures of this call's kernels land here
     const t2sx_model* m = s->m;
     Work& w = s->dec;
     const int T = (int)s->active.size();
@@ -1544,7 +1571,8 @@ extern "C" int t2sx_profile_step(t2sx_session* s, int32_t iters, float* ms) {
 
 extern "C" int t2sx_set_exp_noise(t2sx_session* s, const float* noise, int32_t rows) {
     if (!s || rows < 0 || rows > s->n_slots) return fail(T2SX_ERR_INVALID, "t2sx_set_exp_noise: bad arguments");
-    CK(cudaSetDevice(s->m->device));
+    DeviceGuard dg_;
+    CK(dg_.set(s->m->device));
     const bool on = noise != nullptr && rows > 0;
     if (on) {
         if (!s->noise) CK(cudaMalloc(&s->noise, (size_t)s->n_slots * s->V * 4));
@@ -1558,7 +1586,8 @@ extern "C" int t2sx_set_exp_noise(t2sx_session* s, const float* noise, int32_t r
 extern "C" int t2sx_read_greedy(t2sx_session* s, int32_t* out, int32_t max_rows, int32_t* rows) {
     if (!s || !out) return fail(T2SX_ERR_INVALID, "null argument");
     if (!s->last_greedy) return fail(T2SX_ERR_STATE, "no pass has run yet");
-    CK(cudaSetDevice(s->m->device));
+    DeviceGuard dg_;
+    CK(dg_.set(s->m->device));
     CK(cudaStreamSynchronize(s->st));
     const int n = s->last_rows < max_rows ? s->last_rows : max_rows;
     CK(cudaMemcpy(out, s->last_greedy, (size_t)n * 4, cudaMemcpyDeviceToHost));
@@ -1581,6 +1610,7 @@ struct t2sx_weight {
     DevW w;
     void* act = nullptr;
     int64_t act_rows = 0;
+    int32_t* err = nullptr;   // device error word of the calls on this weight (see t2sx_weight_sync)
 };
 
 extern "C" int t2sx_weight_create(int32_t device, int32_t type, const void* host_bytes, int64_t N, int64_t K, t2sx_weight** out) {
@@ -1588,7 +1618,8 @@ extern "C" int t2sx_weight_create(int32_t device, int32_t type, const void* host
     if (type == W_Q4_K ? K % 256 : K % 32) return fail(T2SX_ERR_INVALID, "K not a multiple of the block size");
     // the few-row kernel keeps one row's 32-element block sums in shared memory (64 of them)
     if (K > 2048) return fail(T2SX_ERR_INVALID, "t2sx_weight_create: K above 2048 is not supported");
-    CK(cudaSetDevice(device));
+    DeviceGuard dg_;
+    CK(dg_.set(device));
     Arena ar;
     WOff wo;
     if (!repack_weight(type, (const uint8_t*)host_bytes, N, K, ar, wo)) return fail(T2SX_ERR_FORMAT, "unsupported type %d", type);
@@ -1600,6 +1631,11 @@ extern "C" int t2sx_weight_create(int32_t device, int32_t type, const void* host
         if (e != cudaSuccess) { cudaFree(w->mem); return fail(T2SX_ERR_CUDA, "upload: %s", cudaGetErrorString(e)); }
     }
     w->w = resolve(wo, w->mem);
+    if (cudaMalloc(&w->err, 4) != cudaSuccess || cudaMemset(w->err, 0, 4) != cudaSuccess) {
+        cudaFree(w->mem);
+        if (w->err) cudaFree(w->err);
+        return fail(T2SX_ERR_OOM, "t2sx_weight_create: error word");
+    }
     *out = w.release();
     return T2SX_OK;
 }
@@ -1610,15 +1646,41 @@ int t2sx_set_error(int code, const char* msg) { return fail(code, "%s", msg); }
 
 extern "C" void t2sx_weight_free(t2sx_weight* w) {
     if (!w) return;
-    cudaSetDevice(w->device);
+    DeviceGuard dg_;
+    dg_.set(w->device);
     if (w->mem) cudaFree(w->mem);
     if (w->act) cudaFree(w->act);
+    if (w->err) cudaFree(w->err);
     delete w;
+}
+
+int32_t* t2sx_weight_err_of(const t2sx_weight* w) { return w->err; }
+
+extern "C" int t2sx_weight_sync(t2sx_weight* w, void* stream) {
+    if (!w) return fail(T2SX_ERR_INVALID, "t2sx_weight_sync: null weight");
+    DeviceGuard dg_;
+    CK(dg_.set(w->device));
+    CK(cudaStreamSynchronize((cudaStream_t)stream));
+    int32_t e = 0;
+    CK(cudaMemcpy(&e, w->err, 4, cudaMemcpyDeviceToHost));
+    if (e) {
+        CK(cudaMemset(w->err, 0, 4));
+        return fail(T2SX_ERR_TIMEOUT, "a tensor-core matmul on this weight gave up waiting; its outputs are NaN");
+    }
+    return T2SX_OK;
+}
+
+extern "C" int t2sx_test_set_tc_wait_cycles(int64_t cycles) {
+    if (cycles < 0) return fail(T2SX_ERR_INVALID, "t2sx_test_set_tc_wait_cycles: negative bound");
+    set_tc_test_wait_cycles((long long)cycles);
+    return T2SX_OK;
 }
 
 extern "C" int t2sx_matmul(t2sx_weight* w, const float* x, int64_t M, const float* bias, float* y, void* stream) {
     if (!w || !x || !y || M <= 0 || M > (1 << 24)) return fail(T2SX_ERR_INVALID, "t2sx_matmul: bad arguments");
-    CK(cudaSetDevice(w->device));
+    DeviceGuard dg_;
+    CK(dg_.set(w->device));
+    ErrScope es_(w->err);   // bounded-wait failures of this call's kernels land here
     cudaStream_t st = (cudaStream_t)stream;
     const int64_t K = w->w.K;
     if (w->act_rows < M) {
@@ -1647,7 +1709,9 @@ extern "C" int t2sx_matmul(t2sx_weight* w, const float* x, int64_t M, const floa
 extern "C" int t2sx_extract_latent(t2sx_session* s, const float* hubert, int32_t T, int32_t* codes_out) {
     if (!s || !hubert || !codes_out || T < 2 || T > (1 << 20)) return fail(T2SX_ERR_INVALID, "t2sx_extract_latent: bad arguments");
     const t2sx_model* m = s->m;
-    CK(cudaSetDevice(m->device));
+    DeviceGuard dg_;
+    CK(dg_.set(m->device));
+    ErrScope es_(s->err);   // bounded-wait failures of this call's kernels land here
     const int C = 768, K = 2 * C, NC = m->n_codes;
     const int To = (T - 2) / 2 + 1;
     // one scratch allocation: frames, im2col rows, their dot-type copy, conv output, scores, codes

@@ -7,6 +7,7 @@
 #include "t2sx_math.cuh"
 #include "t2sx_kv.cuh"
 
+#include <atomic>
 #include <cstdlib>
 
 namespace t2sx {
@@ -25,6 +26,15 @@ bool pdl_enabled() {
 
 PdlScope::PdlScope(bool on) : prev(t_pdl_scope) { t_pdl_scope = prev || on; }
 PdlScope::~PdlScope() { t_pdl_scope = prev; }
+
+static thread_local int32_t* t_err_word = nullptr;
+int32_t* current_err_word() { return t_err_word; }
+ErrScope::ErrScope(int32_t* word) : prev(t_err_word) { t_err_word = word; }
+ErrScope::~ErrScope() { t_err_word = prev; }
+
+static std::atomic<long long> g_tc_test_wait{0};
+long long tc_test_wait_cycles() { return g_tc_test_wait.load(std::memory_order_relaxed); }
+void set_tc_test_wait_cycles(long long cycles) { g_tc_test_wait.store(cycles > 0 ? cycles : 0, std::memory_order_relaxed); }
 
 // ============================================================================================
 // activation quantisation
@@ -1342,11 +1352,11 @@ void attention_rows(int T, int row0, const int2* groups, int n_groups, const uin
 // row's page numbers; the kernel's limit is raised once.
 template <int HPC>
 static size_t attn_pipe_smem(const KVView& kv) {
-    static bool configured = false;
-    if (!configured) {
-        cudaFuncSetAttribute(k_attn_decode<HPC, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-        configured = true;
-    }
+    static PerDeviceOnce setup;   // the limit is raised once on each device that launches it
+    setup.ensure([](int, int*) {
+        return cudaFuncSetAttribute(k_attn_decode<HPC, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) ==
+               cudaSuccess;
+    });
     return (size_t)(16 / HPC) * 8 * (32 * HPC) * 16 + (size_t)kv.max_pages * 4;
 }
 
@@ -1386,11 +1396,11 @@ void attention_decode(int T, const uint16_t* q16, Rows rows, KVView kv, int laye
         // very few rows: one head per CTA, four threads per position lane (at most 32 rows: the
         // positions of a pass are then at most one per position lane, which the kernel's early
         // K/V fetch relies on)
-        static bool configured = false;
-        if (!configured) {
-            cudaFuncSetAttribute(k_attn_decode_split, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-            configured = true;
-        }
+        static PerDeviceOnce setup;
+        setup.ensure([](int, int*) {
+            return cudaFuncSetAttribute(k_attn_decode_split, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) ==
+                   cudaSuccess;
+        });
         const size_t smem = (size_t)kQD * 2 * 128 * 16 + (10 * 128 + 32) * 4 + (size_t)kv.max_pages * 4;
         launch_k(k_attn_decode_split, dim3(T * kHeads), dim3(128), smem, st, q16, rows, kv, layer, scale, out, qtype, qo);
     } else if (T < pipe1_rows()) {

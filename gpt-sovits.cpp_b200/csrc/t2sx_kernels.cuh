@@ -3,6 +3,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <mutex>
 #include <utility>
 
 namespace t2sx {
@@ -19,6 +20,63 @@ struct PdlScope {
     PdlScope(const PdlScope&) = delete;
     PdlScope& operator=(const PdlScope&) = delete;
     bool prev;
+};
+
+// Makes `dev` the calling thread's current CUDA device for the lifetime of the guard and puts the
+// caller's device back afterwards, so an entry point never changes the device a host thread
+// works on (a host may keep other models on other devices in the same thread).
+struct DeviceGuard {
+    DeviceGuard() = default;
+    DeviceGuard(const DeviceGuard&) = delete;
+    DeviceGuard& operator=(const DeviceGuard&) = delete;
+    cudaError_t set(int dev) {
+        cudaError_t e = cudaGetDevice(&prev);
+        if (e != cudaSuccess) return e;
+        if (prev == dev) return cudaSuccess;
+        e = cudaSetDevice(dev);
+        restore = (e == cudaSuccess);
+        return e;
+    }
+    ~DeviceGuard() {
+        if (restore) cudaSetDevice(prev);
+    }
+    int prev = 0;
+    bool restore = false;
+};
+
+// Device error word of the entry point running on this host thread (the session's flag, or the
+// isolated weight's): kernels that can give up a bounded wait store a code there.  An ErrScope
+// sets it for the launches made (or captured) while it lives.
+int32_t* current_err_word();
+struct ErrScope {
+    explicit ErrScope(int32_t* word);
+    ~ErrScope();
+    ErrScope(const ErrScope&) = delete;
+    ErrScope& operator=(const ErrScope&) = delete;
+    int32_t* prev;
+};
+// Wait bound (clock cycles) of the tensor-core matmul's barrier waits for launches made from now
+// on; 0 = the built-in bound (about one second).  Set only through the test hook of the C ABI.
+long long tc_test_wait_cycles();
+void set_tc_test_wait_cycles(long long cycles);
+
+// One-time set-up per device (function attributes such as the dynamic shared-memory limit apply
+// to the device that is current when they are set): ensure() runs setup(dev, &value) once for the
+// current device, under a mutex, and reports whether it succeeded; value is what setup stored.
+struct PerDeviceOnce {
+    static constexpr int kMaxDevices = 64;
+    template <class F>
+    bool ensure(F&& setup, int* value_out = nullptr) {
+        int dev = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return false;
+        std::lock_guard<std::mutex> lk(mu);
+        if (state[dev] == 0) state[dev] = setup(dev, &value[dev]) ? 1 : -1;
+        if (value_out) *value_out = value[dev];
+        return state[dev] == 1;
+    }
+    std::mutex mu;
+    signed char state[kMaxDevices] = {};   // 0 not yet, 1 usable, -1 set-up failed
+    int value[kMaxDevices] = {};
 };
 
 template <typename... KArgs, typename... Args>

@@ -67,7 +67,8 @@ struct t2sx_kvcache {
 
 static void kv_release(t2sx_kvcache* c) {
     if (!c) return;
-    cudaSetDevice(c->device);
+    DeviceGuard dg_;
+    dg_.set(c->device);
     if (c->st) cudaStreamSynchronize(c->st);
     cudaFree(c->pool); cudaFree(c->ptab); cudaFree(c->cap); cudaFree(c->err); cudaFree(c->stage); cudaFree(c->rows_mem);
     if (c->st) cudaStreamDestroy(c->st);
@@ -78,7 +79,8 @@ extern "C" int t2sx_kvcache_create(int32_t device, int32_t n_seqs, int32_t max_l
     if (!out || n_seqs <= 0 || max_len <= 0 || (int64_t)n_seqs * max_len > (int64_t)1 << 31)
         return t2sx_set_error(T2SX_ERR_INVALID, "t2sx_kvcache_create: bad arguments");
     *out = nullptr;
-    KCK(cudaSetDevice(device));
+    DeviceGuard dg_;
+    KCK(dg_.set(device));
     std::unique_ptr<t2sx_kvcache, void (*)(t2sx_kvcache*)> c(new t2sx_kvcache(), kv_release);
     c->device = device; c->n_seqs = n_seqs; c->max_len = max_len;
     c->pages_per_seq = (max_len + kPage - 1) / kPage;
@@ -108,7 +110,8 @@ extern "C" int t2sx_kvcache_write(t2sx_kvcache* c, int32_t seq, int32_t pos0, in
                                   const uint16_t* v) {
     if (!c || !k || !v || seq < 0 || seq >= c->n_seqs || pos0 < 0 || len <= 0 || (int64_t)pos0 + len > c->max_len)
         return t2sx_set_error(T2SX_ERR_INVALID, "t2sx_kvcache_write: bad arguments");
-    KCK(cudaSetDevice(c->device));
+    DeviceGuard dg_;
+    KCK(dg_.set(c->device));
     const size_t row = (size_t)kHeads * kHeadDim;
     if (c->stage_rows < (size_t)len) {
         KCK(cudaStreamSynchronize(c->st));
@@ -159,7 +162,8 @@ static int kv_rows(t2sx_kvcache* c, int32_t n, const int32_t* seqs, const int32_
 static int kv_attn(t2sx_kvcache* c, int32_t n, const int32_t* seqs, const int32_t* lens, const uint16_t* q, float* out,
                    void* stream, bool grouped) {
     if (!c || n <= 0 || !seqs || !lens || !q || !out) return t2sx_set_error(T2SX_ERR_INVALID, "attention: bad arguments");
-    KCK(cudaSetDevice(c->device));
+    DeviceGuard dg_;
+    KCK(dg_.set(c->device));
     cudaStream_t st = (cudaStream_t)stream;
     Rows rows;
     int rc = kv_rows(c, n, seqs, lens, &rows, st);

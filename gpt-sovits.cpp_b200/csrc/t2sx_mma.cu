@@ -305,12 +305,12 @@ template <int WT, int MT, int WN = 4, int NSTG = 2, int IT = 2>
 static void launch_mma(const DevW& W, const ActQ& a, int M, const float* bias, int relu, float* y, const QKVStore* qkv,
                        cudaStream_t st) {
     using C = Cfg<WT, MT, WN, NSTG, IT>;
-    static bool configured = false;   // the attribute is per function; set once per process
-    if (!configured) {
-        if (cudaFuncSetAttribute(k_mm_mma<WT, MT, WN, NSTG, IT>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess)
-            return;   // the launch below then fails and the caller's launch check reports it
-        configured = true;
-    }
+    static PerDeviceOnce setup;   // the shared-memory limit, set once on each device that launches it
+    if (!setup.ensure([](int, int*) {
+            return cudaFuncSetAttribute(k_mm_mma<WT, MT, WN, NSTG, IT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        C::SMEM) == cudaSuccess;
+        }))
+        return;   // the launch below is skipped and the caller's launch check reports the failure
     dim3 grid((W.N + C::BN - 1) / C::BN, (M + C::BM - 1) / C::BM);
     QKVStore q{};
     if (qkv) q = *qkv;

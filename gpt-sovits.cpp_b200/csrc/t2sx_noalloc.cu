@@ -40,20 +40,23 @@ void* g_scratch_ptr[kMaxDevices] = {};   // device address of g_noalloc_scratch,
 int32_t t2sx_weight_device_of(const t2sx_weight* w);
 const DevW* t2sx_weight_devw_of(const t2sx_weight* w);
 int t2sx_set_error(int code, const char* msg);
+int32_t* t2sx_weight_err_of(const t2sx_weight* w);
 
 extern "C" int t2sx_matmul_noalloc(t2sx_weight* w, const float* x_dev, int64_t M, const float* bias_dev, float* y_dev,
                                    void* stream) {
     if (!w || !x_dev || !y_dev || M <= 0) return t2sx_set_error(T2SX_ERR_INVALID, "t2sx_matmul_noalloc: bad arguments");
     const int32_t dev = t2sx_weight_device_of(w);
     const DevW* W = t2sx_weight_devw_of(w);
-    if ((int64_t)W->K * M > (int64_t)T2SX_NOALLOC_MAX_ELEMS) {
+    // M is bounded before the product is formed, so M * K cannot overflow
+    if (M > (int64_t)T2SX_NOALLOC_MAX_ELEMS / W->K) {
         char msg[160];
-        snprintf(msg, sizeof(msg), "t2sx_matmul_noalloc: M*K = %lld exceeds the fixed scratch of %d activation elements",
-                 (long long)((int64_t)W->K * M), (int)T2SX_NOALLOC_MAX_ELEMS);
+        snprintf(msg, sizeof(msg), "t2sx_matmul_noalloc: M = %lld rows of K = %d exceed the fixed scratch of %d activation elements",
+                 (long long)M, W->K, (int)T2SX_NOALLOC_MAX_ELEMS);
         return t2sx_set_error(T2SX_ERR_INVALID, msg);
     }
     if (dev < 0 || dev >= kMaxDevices) return t2sx_set_error(T2SX_ERR_INVALID, "t2sx_matmul_noalloc: device index out of range");
-    if (cudaSetDevice(dev) != cudaSuccess) return t2sx_set_error(T2SX_ERR_CUDA, "t2sx_matmul_noalloc: cudaSetDevice failed");
+    DeviceGuard dg_;   // the caller's current device is restored on return
+    if (dg_.set(dev) != cudaSuccess) return t2sx_set_error(T2SX_ERR_CUDA, "t2sx_matmul_noalloc: cudaSetDevice failed");
     void* base = nullptr;
     {
         // One-time set-up per device, done by the first call on that device with the device
@@ -69,6 +72,7 @@ extern "C" int t2sx_matmul_noalloc(t2sx_weight* w, const float* x_dev, int64_t M
         base = g_scratch_ptr[dev];
     }
     cudaStream_t st = (cudaStream_t)stream;
+    ErrScope es_(t2sx_weight_err_of(w));   // the weight's error word (allocated with the weight)
     uint8_t* p = (uint8_t*)base;
     ActQ a;
     a.q = (int8_t*)p;

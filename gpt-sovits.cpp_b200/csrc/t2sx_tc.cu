@@ -71,8 +71,9 @@ constexpr int SMEM = 1024 + NS * STAGE + OUT_BYTES + DX_BYTES + KVB_BYTES + BAR_
 constexpr int kMagic = 0x4B400000;
 constexpr float kMagicF = 12582912.0f;
 constexpr long long kSpinCycles = 2000000000LL;   // bound of one wait (~1 s at 1.9 GHz)
-
-__device__ int g_tc_timeouts = 0;   // number of CTAs that gave up waiting (stays 0)
+// Value the kernel stores into its error word when a CTA gave up waiting (the session's bounds
+// checks store 1 into the same word).
+constexpr int kErrTimeout = 3;
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -94,8 +95,9 @@ __device__ __forceinline__ bool bar_try(uint32_t bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
-// Wait for the phase of the given parity; false when the CTA aborted or the wait ran out.
-__device__ __forceinline__ bool bar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
+// Wait for the phase of the given parity; false when the CTA aborted or the wait ran out after
+// `limit` cycles (kSpinCycles unless a test shortened it).
+__device__ __forceinline__ bool bar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag, long long limit) {
     long long t0 = 0;
     for (uint32_t it = 0;; ++it) {
         if (bar_try(bar, parity)) return true;
@@ -103,7 +105,7 @@ __device__ __forceinline__ bool bar_wait(uint32_t bar, uint32_t parity, volatile
             if (*abort_flag) return false;
             const long long now = clock64();
             if (t0 == 0) t0 = now;
-            else if (now - t0 > kSpinCycles) { *abort_flag = 1; return false; }
+            else if (now - t0 > limit) { *abort_flag = 1; return false; }
         }
     }
 }
@@ -226,7 +228,7 @@ __device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
 __global__ void __launch_bounds__(THREADS, 1)
 k_mm_tc_q4k(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
             const __grid_constant__ CUtensorMap tmY, DevW W, ActQ A, int M, const float* __restrict__ bias, int relu,
-            float* __restrict__ y, QKVStore qkv, int use_qkv, int tstore) {
+            float* __restrict__ y, QKVStore qkv, int use_qkv, int tstore, int32_t* err, long long spin) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     float* out_tile = (float*)(smem + NS * STAGE);
@@ -291,7 +293,7 @@ k_mm_tc_q4k(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUt
                     const int n0 = (t % tiles_n) * BM, m0 = (t / tiles_n) * BN;
                     for (int h = 0; h < 2 * nsb; ++h, ++stg) {
                         const int ss = stg % NS;
-                        if (!bar_wait(empty0 + 8 * ss, ((stg / NS) & 1) ^ 1, abort_flag)) { aborted = true; break; }
+                        if (!bar_wait(empty0 + 8 * ss, ((stg / NS) & 1) ^ 1, abort_flag, spin)) { aborted = true; break; }
                         const uint32_t fb = full0 + 8 * ss;
                         bar_expect_tx(fb, STAGE);
                         const uint32_t st = smem_u32(smem + ss * STAGE);
@@ -318,12 +320,12 @@ k_mm_tc_q4k(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUt
                 for (int t = blockIdx.x; t < n_tiles && !aborted; t += gridDim.x) {
                     for (int sb = 0; sb < nsb && !aborted; ++sb, ++gsb) {
                         const int buf = gsb % NBUF;
-                        if (!bar_wait(tempty0 + 8 * buf, ((gsb / NBUF) & 1) ^ 1, abort_flag)) { aborted = true; break; }
+                        if (!bar_wait(tempty0 + 8 * buf, ((gsb / NBUF) & 1) ^ 1, abort_flag, spin)) { aborted = true; break; }
                         tc_fence_after();
                         const uint32_t dcol = tmem + (uint32_t)(buf * BUF_COLS + p * BN);
                         for (int h = 0; h < 2; ++h, ++stg) {
                             const int ss = stg % NS;
-                            if (!bar_wait(full0 + 8 * ss, (stg / NS) & 1, abort_flag)) { aborted = true; break; }
+                            if (!bar_wait(full0 + 8 * ss, (stg / NS) & 1, abort_flag, spin)) { aborted = true; break; }
                             tc_fence_after();
                             // descriptor start addresses advance in 16-byte units in the low bits
                             const uint64_t dst = d0 + (uint64_t)((ss * STAGE) >> 4);
@@ -373,7 +375,7 @@ k_mm_tc_q4k(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUt
                     xd = mok ? A.d[(size_t)mt * nsb + sb + 1] : 0.0f;
                 }
                 const int buf = gsb % NBUF;
-                const bool ok = bar_wait(tfull0 + 8 * buf, (gsb / NBUF) & 1, abort_flag);
+                const bool ok = bar_wait(tfull0 + 8 * buf, (gsb / NBUF) & 1, abort_flag, spin);
                 if (__any_sync(0xffffffffu, !ok)) { aborted = true; break; }   // also reconverges the warp
                 tc_fence_after();
                 const uint32_t tb = tl + (uint32_t)(buf * BUF_COLS);
@@ -495,10 +497,7 @@ k_mm_tc_q4k(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUt
     __syncwarp();
     tc_fence_before();
     __syncthreads();
-    if (*abort_flag && tid == 0) {
-        atomicAdd(&g_tc_timeouts, 1);
-        if (use_qkv && qkv.rows.err) atomicExch(qkv.rows.err, 3);
-    }
+    if (*abort_flag && tid == 0 && err) atomicExch(err, kErrTimeout);
     if (warp == 0) {
         __syncwarp();
         tc_fence_after();
@@ -551,19 +550,16 @@ bool make_map(CUtensorMap* map, const void* base, int K, int rows, int box_rows)
 
 bool launch_q4k(const DevW& W, const ActQ& a, int M, const float* bias, int relu, float* y, const QKVStore* qkv,
                 cudaStream_t st) {
-    static bool configured = false, usable = false;
-    static int n_sm = 0;
-    if (!configured) {
-        configured = true;
-        // the setmaxnreg split assumes exactly kLaunchRegs registers per thread at launch
+    // per device: the setmaxnreg split assumes exactly kLaunchRegs registers per thread at launch;
+    // the shared-memory limit is set on that device; value = its SM count
+    static PerDeviceOnce setup;
+    int n_sm = 0;
+    const bool usable = setup.ensure([](int dev, int* sms) {
         cudaFuncAttributes fa;
         if (cudaFuncGetAttributes(&fa, k_mm_tc_q4k) != cudaSuccess || fa.numRegs != kLaunchRegs) return false;
         if (cudaFuncSetAttribute(k_mm_tc_q4k, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM) != cudaSuccess) return false;
-        int dev = 0;
-        if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
-            return false;
-        usable = true;
-    }
+        return cudaDeviceGetAttribute(sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && *sms > 0;
+    }, &n_sm);
     if (!usable) return false;
     CUtensorMap mw, mx;
     if (!make_map(&mw, W.tcw, W.K, PLANES * W.tc_npad, BM) || !make_map(&mx, a.q, W.K, M, BN)) return false;
@@ -577,6 +573,11 @@ bool launch_q4k(const DevW& W, const ActQ& a, int M, const float* bias, int relu
     std::memset(&my, 0, sizeof(my));
     const int tstore = qkv ? (make_out_map(&my, qkv->q16, kD, M, 2) ? 1 : 0) : (make_out_map(&my, y, W.N, M, 4) ? 1 : 0);
     if (qkv && !tstore) return false;
+    // where a CTA that gives up waiting reports it: the error word of the entry point that
+    // launched (or captured) this launch; the wait bound, unless a test shortened it
+    int32_t* err = current_err_word();
+    const long long test_spin = tc_test_wait_cycles();
+    const long long spin = test_spin > 0 ? test_spin : kSpinCycles;
     // Programmatic dependent launch (T2SX_PDL_TC=0 turns it off): the set-up before the kernel's
     // griddepcontrol.wait (barriers, TMEM allocation and start pattern, descriptor prefetch) runs
     // while the preceding kernel drains.  A CTA of this kernel fills an SM, so it never shares
@@ -594,10 +595,10 @@ bool launch_q4k(const DevW& W, const ActQ& a, int M, const float* bias, int relu
         cfg.attrs = attr;
         cfg.numAttrs = 1;
         const int uq = qkv ? 1 : 0;
-        cudaLaunchKernelEx(&cfg, k_mm_tc_q4k, mw, mx, my, W, a, M, bias, relu, y, q, uq, tstore);
+        cudaLaunchKernelEx(&cfg, k_mm_tc_q4k, mw, mx, my, W, a, M, bias, relu, y, q, uq, tstore, err, spin);
     } else {
         launch_k(k_mm_tc_q4k, dim3(grid), dim3(THREADS), (size_t)SMEM, st, mw, mx, my, W, a, M, bias, relu, y, q, qkv ? 1 : 0,
-                 tstore);
+                 tstore, err, spin);
     }
     return true;
 }

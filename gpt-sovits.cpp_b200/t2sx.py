@@ -17,7 +17,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libt2sx.so")
 
-OK, ERR_INVALID, ERR_IO, ERR_FORMAT, ERR_CUDA, ERR_OOM, ERR_STATE, ERR_BOUNDS = range(8)
+OK, ERR_INVALID, ERR_IO, ERR_FORMAT, ERR_CUDA, ERR_OOM, ERR_STATE, ERR_BOUNDS, ERR_TIMEOUT = range(9)
 F32, F16, Q4_0, Q8_0, Q4_K = 0, 1, 2, 8, 12
 
 # Every symbol include/t2sx.h declares: (restype, argtypes).
@@ -57,6 +57,8 @@ SIGNATURES = {
     "t2sx_weight_free": (None, [_P]),
     "t2sx_matmul": (C.c_int, [_P, _P, _I64, _P, _P, _P]),
     "t2sx_matmul_noalloc": (C.c_int, [_P, _P, _I64, _P, _P, _P]),
+    "t2sx_weight_sync": (C.c_int, [_P, _P]),
+    "t2sx_test_set_tc_wait_cycles": (C.c_int, [_I64]),
     "t2sx_kvcache_create": (C.c_int, [_I, _I, _I, _P]),
     "t2sx_kvcache_free": (None, [_P]),
     "t2sx_kvcache_write": (C.c_int, [_P, _I, _I, _I, _P, _P]),
@@ -105,6 +107,12 @@ def _ck(rc):
 
 def _p(a):
     return None if a is None else C.c_void_p(a.ctypes.data)
+
+
+def test_set_tc_wait_cycles(cycles: int):
+    """Test hook: the tensor-core matmul's wait bound in clock cycles for later launches (0 = the
+    built-in bound of about one second)."""
+    _ck(lib().t2sx_test_set_tc_wait_cycles(int(cycles)))
 
 
 def device_count() -> int:
@@ -337,6 +345,11 @@ class Weight:
         """Same result as matmul(), using the library's fixed scratch instead of allocating."""
         _ck(lib().t2sx_matmul_noalloc(self.h, C.c_void_p(x_ptr), M, None if bias_ptr is None else C.c_void_p(bias_ptr),
                                       C.c_void_p(y_ptr), C.c_void_p(stream)))
+
+    def sync(self, stream: int = 0):
+        """Waits for the stream; raises T2SXError(ERR_TIMEOUT) if a matmul on this weight gave up
+        a bounded wait since the last check (its outputs are then NaN)."""
+        _ck(lib().t2sx_weight_sync(self.h, C.c_void_p(stream)))
 
     def close(self):
         if self.h:

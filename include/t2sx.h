@@ -34,6 +34,7 @@ extern "C" {
 #define T2SX_ERR_OOM 5       /* device memory exhausted */
 #define T2SX_ERR_STATE 6     /* illegal slot transition (reference aborts via GGML_ASSERT) */
 #define T2SX_ERR_BOUNDS 7    /* a slot ran past its capacity (device-side check) */
+#define T2SX_ERR_TIMEOUT 8   /* a tensor-core matmul gave up a bounded wait (about 1 s); its outputs are NaN */
 
 typedef struct t2sx_model t2sx_model;
 typedef struct t2sx_session t2sx_session;
@@ -176,9 +177,19 @@ T2SX_API int t2sx_weight_create(int32_t device, int32_t ggml_type, const void* h
                        int64_t K, t2sx_weight** out);
 T2SX_API void t2sx_weight_free(t2sx_weight* w);
 /* y[M][N] = x[M][K] . W^T (+ bias[N]) on device pointers, with ggml-CPU semantics (activation
- * rows converted to the weight's dot type).  `stream` is a cudaStream_t (0 = legacy default). */
+ * rows converted to the weight's dot type).  `stream` is a cudaStream_t (0 = legacy default).
+ * Asynchronous: a failure inside the kernels (a tensor-core wait that ran out) is reported by
+ * t2sx_weight_sync. */
 T2SX_API int t2sx_matmul(t2sx_weight* w, const float* x_dev, int64_t M, const float* bias_dev, float* y_dev,
                 void* stream);
+/* Waits for `stream` and reports whether a matmul on this weight since the last check gave up a
+ * bounded wait (T2SX_ERR_TIMEOUT; its outputs are NaN); clears that state.  The reference has no
+ * counterpart (ggml's CPU kernels do not wait on anything). */
+T2SX_API int t2sx_weight_sync(t2sx_weight* w, void* stream);
+/* Test hook, no counterpart in the reference: the wait bound (clock cycles) of the tensor-core
+ * matmul for launches made (or graphs captured) from now on, so a test can make a wait run out
+ * and check the error path; 0 restores the built-in bound of about one second. */
+T2SX_API int t2sx_test_set_tc_wait_cycles(int64_t cycles);
 
 /* No counterpart in the reference (its ggml graphs allocate through the backend).  The same
  * matmul as t2sx_matmul, for callers that cannot allocate device memory at call time -- e.g. a

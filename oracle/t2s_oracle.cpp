@@ -355,15 +355,107 @@ static float qdot(int wtype, const uint8_t* w, int64_t K, const ActRow& a) {
     return acc;
 }
 
+// A quantised weight row unpacked once per matmul call into plain int8 values and per-block
+// scales, so the per-activation-row dot is a contiguous int8 x int8 loop.  The integer block sums
+// and the float fold (operands and order) are exactly those of qdot above; only the unpacking of
+// the nibbles / 5th bits / 6-bit scales moves out of the per-row loop.
+struct WRowX {
+    std::vector<int8_t> q;      // [K] element values (Q4_0: nibble - 8; Q5_0: 5-bit - 16; Q4_K: 0..15)
+    std::vector<float> dw;      // Q8_0/Q4_0/Q5_0: f16 block scale as f32 [K/32]
+    std::vector<int> sc, mn;    // Q4_K: 6-bit scale / min of each 32-element sub-block [K/32]
+    std::vector<float> d, dmin; // Q4_K: super-block d / dmin as f32 [K/256]
+};
+
+static void expand_row(int wtype, const uint8_t* w, int64_t K, WRowX& e) {
+    e.q.resize(K);
+    if (wtype == ORC_Q4_K) {
+        e.sc.resize(K / 32); e.mn.resize(K / 32); e.d.resize(K / 256); e.dmin.resize(K / 256);
+        for (int64_t b = 0; b < K / 256; ++b) {
+            const uint8_t* wb = w + b * 144;
+            e.d[b] = h2f(rd16(wb)); e.dmin[b] = h2f(rd16(wb + 2));
+            const uint8_t* qs = wb + 16;
+            for (int j = 0; j < 8; ++j) {
+                q4k_scale_min(wb + 4, j, e.sc[b * 8 + j], e.mn[b * 8 + j]);
+                const int c = j >> 1, sh = (j & 1) * 4;
+                for (int l = 0; l < 32; ++l) e.q[b * 256 + 32 * j + l] = (int8_t)((qs[32 * c + l] >> sh) & 0xF);
+            }
+        }
+        return;
+    }
+    e.dw.resize(K / 32);
+    for (int64_t b = 0; b < K / 32; ++b) {
+        int8_t* q = &e.q[b * 32];
+        if (wtype == ORC_Q8_0) {
+            const uint8_t* wb = w + b * 34;
+            e.dw[b] = h2f(rd16(wb));
+            memcpy(q, wb + 2, 32);
+        } else if (wtype == ORC_Q4_0) {
+            const uint8_t* wb = w + b * 18;
+            e.dw[b] = h2f(rd16(wb));
+            for (int i = 0; i < 16; ++i) { q[i] = (int8_t)((wb[2 + i] & 0xF) - 8); q[16 + i] = (int8_t)((wb[2 + i] >> 4) - 8); }
+        } else {   // Q5_0
+            const uint8_t* wb = w + b * 22;
+            e.dw[b] = h2f(rd16(wb));
+            for (int i = 0; i < 32; ++i) q[i] = (int8_t)q5_0_value(wb, i);
+        }
+    }
+}
+
+static inline int dot32_i8(const int8_t* a, const int8_t* b) {
+    int s = 0;
+    for (int i = 0; i < 32; ++i) s += (int)a[i] * (int)b[i];
+    return s;
+}
+
+static float qdot_x(int wtype, const WRowX& e, int64_t K, const ActRow& a) {
+    if (wtype == ORC_Q4_K) {
+        float acc_a = 0.0f, acc_m = 0.0f;
+        for (int64_t b = 0; b < K / 256; ++b) {
+            const BlkQ8K& x = a.q8k[b];
+            int sumi_a = 0, sumi_m = 0;
+            for (int j = 0; j < 8; ++j) {
+                const int isum = dot32_i8(&e.q[b * 256 + 32 * j], &x.qs[32 * j]);
+                sumi_a += e.sc[b * 8 + j] * isum;
+                sumi_m += e.mn[b * 8 + j] * ((int)x.bsums[2 * j] + (int)x.bsums[2 * j + 1]);
+            }
+            const float d = x.d * e.d[b];
+            const float dmin = -x.d * e.dmin[b];
+            acc_a = fmaf(d, (float)sumi_a, acc_a);
+            acc_m = fmaf(dmin, (float)sumi_m, acc_m);
+        }
+        return acc_a + acc_m;
+    }
+    float acc = 0.0f;
+    for (int64_t b = 0; b < K / 32; ++b) {
+        const int isum = dot32_i8(&e.q[b * 32], a.q8[b].qs);
+        const float dd = e.dw[b] * a.q8[b].d;
+        acc = fmaf(dd, (float)isum, acc);
+    }
+    return acc;
+}
+
 int orc_matmul(int wtype, const void* w, int64_t N, int64_t K, const float* x, int64_t M, float* y) {
     const int64_t rb = orc_row_bytes(wtype, K);
     if (rb <= 0) return -1;
     std::vector<ActRow> acts(M);
     for (int64_t m = 0; m < M; ++m) prep_act(wtype, x + m * K, K, acts[m]);
-    #pragma omp parallel for schedule(static)
-    for (int64_t n = 0; n < N; ++n)
-        for (int64_t m = 0; m < M; ++m)
-            y[m * N + n] = qdot(wtype, (const uint8_t*)w + n * rb, K, acts[m]);
+    const bool quant = wtype == ORC_Q8_0 || wtype == ORC_Q4_0 || wtype == ORC_Q5_0 || wtype == ORC_Q4_K;
+    if (!quant || M < 2) {
+        #pragma omp parallel for schedule(static)
+        for (int64_t n = 0; n < N; ++n)
+            for (int64_t m = 0; m < M; ++m)
+                y[m * N + n] = qdot(wtype, (const uint8_t*)w + n * rb, K, acts[m]);
+        return 0;
+    }
+    #pragma omp parallel
+    {
+        WRowX e;
+        #pragma omp for schedule(static)
+        for (int64_t n = 0; n < N; ++n) {
+            expand_row(wtype, (const uint8_t*)w + n * rb, K, e);
+            for (int64_t m = 0; m < M; ++m) y[m * N + n] = qdot_x(wtype, e, K, acts[m]);
+        }
+    }
     return 0;
 }
 

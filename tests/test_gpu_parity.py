@@ -4,6 +4,8 @@ Every kernel reproduces the oracle's evaluation order, so the comparisons below 
 (array_equal on the raw bits), well inside the north-star tolerance for logits (1e-2 abs /
 1e-3 rel), and greedy token streams must be identical.
 """
+import os
+
 import numpy as np
 import pytest
 
@@ -147,11 +149,39 @@ def test_decode_repetition_penalty_bit_exact(t2sx_mod, orc):
 
 
 def test_decode_full_model_bs1_bit_exact(t2sx_mod, orc):
-    """The bs=1 Q8_0 workload shape (128 phonemes + 150 prompt tokens, 24 layers), 64 steps."""
+    """The one-session workload at its real size: Q8_0 weights seed 0, 24 layers, 128 phonemes +
+    150 prompt tokens, all 500 greedy steps (EOS masked); tokens, last logits and KV bit-exact."""
     _need_gpu()
     import synth
     path = synth.ensure_gguf("q8_0", 0, n_layer=24)
-    _run_pair(t2sx_mod, orc, path, [(128, 150, 0)], steps=64)
+    _run_pair(t2sx_mod, orc, path, synth.workload_lengths("bs1_q8_0"), steps=500)
+
+
+def test_decode_32_sessions_q4_0_full_size_bit_exact(t2sx_mod, orc):
+    """The 32-session workload at its real size: Q4_0 weights seed 1, 24 layers, 32 sessions with
+    phoneme lengths U[64,256] and prompt lengths U[50,300] (inputs from seed 1 + session), all 500
+    greedy steps on the GPU in one call; every step's tokens, the last logits and the KV equal
+    the oracle's."""
+    _need_gpu()
+    import synth
+    orc.set_threads(os.cpu_count() or 1)
+    path = synth.ensure_gguf("q4_0", 1, n_layer=24)
+    lengths = synth.workload_lengths("bs32_q4_0")
+    assert len(lengths) == 32
+    _run_pair(t2sx_mod, orc, path, lengths, steps=500)
+
+
+def test_decode_many_rows_q4_k_24_layers_bit_exact(t2sx_mod, orc):
+    """Many rows on the 24-layer Q4_K model (seed 3, the box-scale workload's weights): 96
+    sessions, so every matmul of the step runs on the tcgen05 kernel (64 rows and more) and the
+    attention on the many-row kernel; short ragged prompts keep the oracle's share small."""
+    _need_gpu()
+    import synth
+    orc.set_threads(os.cpu_count() or 1)
+    path = synth.ensure_gguf("q4_k", 3, n_layer=24)
+    rng = np.random.default_rng(96)
+    lengths = [(int(rng.integers(8, 40)), int(rng.integers(4, 30)), 5000 + i) for i in range(96)]
+    _run_pair(t2sx_mod, orc, path, lengths, steps=40)
 
 
 def test_model_load_rejects_wide_ffn(t2sx_mod, tmp_path):
@@ -163,6 +193,17 @@ def test_model_load_rejects_wide_ffn(t2sx_mod, tmp_path):
     with pytest.raises(t2sx_mod.T2SXError) as e:
         t2sx_mod.Model(path)
     assert e.value.code == t2sx_mod.ERR_FORMAT and "FFN width 2304" in str(e.value)
+
+
+def test_model_load_rejects_large_vocabulary(t2sx_mod, tmp_path):
+    """A semantic vocabulary above 2048 (the sampler sorts a row's logits in a 2048-entry shared
+    array) is refused at load with a format error, before any kernel runs."""
+    _need_gpu()
+    import synth
+    path = synth.write_gguf(str(tmp_path / "big_vocab.gguf"), 8, 5, n_layer=1, vocab=2049, eos=2048)
+    with pytest.raises(t2sx_mod.T2SXError) as e:
+        t2sx_mod.Model(path)
+    assert e.value.code == t2sx_mod.ERR_FORMAT and "vocabulary size 2049" in str(e.value)
 
 
 def test_slot_reuse_and_errors(t2sx_mod):
@@ -531,3 +572,56 @@ def test_flex_step_errors(t2sx_mod):
         assert e.value.code == code, args
     assert s.slot_n_pos(0) == 11 and s.slot_n_pos(1) == 10 and s.slot_n_pos(2) == 0
     s.close(); m.close()
+
+
+def test_tc_wait_timeout_reported_and_recovered(t2sx_mod, orc):
+    """The tensor-core matmul's barrier waits are bounded.  With the bound cut to one cycle (test
+    hook) its CTAs give up, drain the copies they issued, free their TMEM and store NaN, and the
+    failure reaches the host as T2SX_ERR_TIMEOUT: through t2sx_weight_sync for the isolated matmul
+    and through the call's status for a session prefill.  With the bound restored, the same
+    weight and a new session give bit-exact results again: the GPU context stays usable."""
+    _need_gpu()
+    import synth
+    T = t2sx_mod
+    N, K, M = 512, 2048, 256            # Q4_K, 64 rows and more: the tcgen05 kernel
+    wt, wb = _weights("q4_k", N, K, seed=77)
+    x = np.random.default_rng(77).standard_normal((M, K), dtype=np.float32)
+    ref = orc.matmul(wt, wb.reshape(-1), N, K, x)
+    w = T.Weight(wt, wb, N, K)
+    xd = torch.from_numpy(x).cuda()
+    yd = torch.zeros((M, N), dtype=torch.float32, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    path = synth.ensure_gguf("q4_k", 7, n_layer=2)
+    m = T.Model(path)
+    lengths = [(20, 12, 41 + i) for i in range(4)]   # 128 prefill rows: the tcgen05 kernel
+    prompts = [synth.session_inputs(seed, tt, tp) for tt, tp, seed in lengths]
+    try:
+        T.test_set_tc_wait_cycles(1)
+        w.matmul(xd.data_ptr(), M, yd.data_ptr(), stream=stream)
+        with pytest.raises(T.T2SXError) as e:
+            w.sync(stream)
+        assert e.value.code == T.ERR_TIMEOUT
+        assert np.isnan(yd.cpu().numpy()).any()
+        s = T.Session(m, 4, 64, repetition_penalty=1.0, eos_mask=True)
+        xs = np.concatenate([s.embed_prefill(*p) for p in prompts])
+        with pytest.raises(T.T2SXError) as e:
+            s.prefill(np.arange(4), [tt + tp for tt, tp, _ in lengths], [tp for _, tp, _ in lengths], xs)
+        assert e.value.code == T.ERR_TIMEOUT
+        s.close()
+    finally:
+        T.test_set_tc_wait_cycles(0)
+    w.sync(stream)                      # the state was cleared by the failed check
+    for _ in range(2):
+        yd.zero_()
+        w.matmul(xd.data_ptr(), M, yd.data_ptr(), stream=stream)
+        w.sync(stream)
+        assert same_bits(yd.cpu().numpy(), ref)
+    w.close()
+    s = T.Session(m, 4, 64, repetition_penalty=1.0, eos_mask=True)
+    om = orc.Model(path)
+    os_ = orc.Session(om, 4, 64)
+    xs = [om.embed_prefill(*p) for p in prompts]
+    first = s.prefill(np.arange(4), [tt + tp for tt, tp, _ in lengths], [tp for _, tp, _ in lengths], np.concatenate(xs))
+    assert list(first) == [os_.prefill(i, xs[i], lengths[i][1])[0] for i in range(4)]
+    s.close()
+    m.close()
