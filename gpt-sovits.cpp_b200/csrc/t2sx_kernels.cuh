@@ -55,8 +55,10 @@ struct ErrScope {
     ErrScope& operator=(const ErrScope&) = delete;
     int32_t* prev;
 };
-// Wait bound (clock cycles) of the tensor-core matmul's barrier waits for launches made from now
-// on; 0 = the built-in bound (about one second).  Set only through the test hook of the C ABI.
+// Test stall of the tensor-core matmul for launches made from now on: cycles > 0 bounds its
+// barrier waits by `cycles` and makes its fold warps first wait on a barrier that nothing
+// completes (so the error path runs); 0 = normal operation with the built-in bound (about one
+// second).  Set only through the test hook of the C ABI.
 long long tc_test_wait_cycles();
 void set_tc_test_wait_cycles(long long cycles);
 

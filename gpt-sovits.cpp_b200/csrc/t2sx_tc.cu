@@ -64,7 +64,8 @@ constexpr int STAGE = PLANES * A_PLANE + B_TILE;
 constexpr int DX_BYTES = EPI_WARPS * 32 * 4;  // per epilogue warp: its 32 columns' activation scale
 constexpr int OUT_BYTES = BN * BM * 4;        // finished output tile, [BN activation rows][BM] f32
 constexpr int KVB_BYTES = BN * 8;             // per activation row of the tile: its K/V cache base offset
-constexpr int BAR_BYTES = 8 * (2 * NS + 2 * NBUF + 1) + 16;
+// ring full/empty, TMEM full/empty, MMA done, and one barrier nothing arrives on (test stall)
+constexpr int BAR_BYTES = 8 * (2 * NS + 2 * NBUF + 2) + 16;
 constexpr int SMEM = 1024 + NS * STAGE + OUT_BYTES + DX_BYTES + KVB_BYTES + BAR_BYTES;
 // TMEM accumulators start at this bit pattern: the MMA adds the integer dot S to it and the
 // result, read as a float, is 12582912 + S exactly (|S| < 2^22), so float(S) is one subtraction.
@@ -228,17 +229,17 @@ __device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
 __global__ void __launch_bounds__(THREADS, 1)
 k_mm_tc_q4k(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX,
             const __grid_constant__ CUtensorMap tmY, DevW W, ActQ A, int M, const float* __restrict__ bias, int relu,
-            float* __restrict__ y, QKVStore qkv, int use_qkv, int tstore, int32_t* err, long long spin) {
+            float* __restrict__ y, QKVStore qkv, int use_qkv, int tstore, int32_t* err, long long spin, int test_stall) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     float* out_tile = (float*)(smem + NS * STAGE);
     float* dx_base = (float*)(smem + NS * STAGE + OUT_BYTES);
     long long* kvb = (long long*)(smem + NS * STAGE + OUT_BYTES + DX_BYTES);
     uint64_t* bars = (uint64_t*)(smem + NS * STAGE + OUT_BYTES + DX_BYTES + KVB_BYTES);
-    uint32_t* tmem_holder = (uint32_t*)(bars + 2 * NS + 2 * NBUF + 1);
+    uint32_t* tmem_holder = (uint32_t*)(bars + 2 * NS + 2 * NBUF + 2);
     volatile int* abort_flag = (volatile int*)(tmem_holder + 1);
     const uint32_t full0 = smem_u32(bars), empty0 = full0 + 8 * NS, tfull0 = empty0 + 8 * NS,
-                   tempty0 = tfull0 + 8 * NBUF, done_bar = tempty0 + 8 * NBUF;
+                   tempty0 = tfull0 + 8 * NBUF, done_bar = tempty0 + 8 * NBUF, stall_bar = done_bar + 8;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (tid == 0) {   // the producer's first copies need both descriptors
@@ -253,6 +254,7 @@ k_mm_tc_q4k(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUt
         for (int i = 0; i < NS; ++i) { bar_init(full0 + 8 * i, 1); bar_init(empty0 + 8 * i, PLANES); }
         for (int i = 0; i < NBUF; ++i) { bar_init(tfull0 + 8 * i, PLANES); bar_init(tempty0 + 8 * i, EPI_WARPS); }
         bar_init(done_bar, PLANES);
+        bar_init(stall_bar, 1);   // no thread ever arrives on it
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     }
@@ -375,7 +377,10 @@ k_mm_tc_q4k(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUt
                     xd = mok ? A.d[(size_t)mt * nsb + sb + 1] : 0.0f;
                 }
                 const int buf = gsb % NBUF;
-                const bool ok = bar_wait(tfull0 + 8 * buf, (gsb / NBUF) & 1, abort_flag, spin);
+                // test_stall (test hook only): the first wait is on a barrier that nothing completes,
+                // so it runs out after `spin` cycles and the abort path below is taken
+                bool ok = !(test_stall && gsb == 0) || bar_wait(stall_bar, 0, abort_flag, spin);
+                ok = ok && bar_wait(tfull0 + 8 * buf, (gsb / NBUF) & 1, abort_flag, spin);
                 if (__any_sync(0xffffffffu, !ok)) { aborted = true; break; }   // also reconverges the warp
                 tc_fence_after();
                 const uint32_t tb = tl + (uint32_t)(buf * BUF_COLS);
@@ -578,6 +583,7 @@ bool launch_q4k(const DevW& W, const ActQ& a, int M, const float* bias, int relu
     int32_t* err = current_err_word();
     const long long test_spin = tc_test_wait_cycles();
     const long long spin = test_spin > 0 ? test_spin : kSpinCycles;
+    const int stall = test_spin > 0 ? 1 : 0;
     // Programmatic dependent launch (T2SX_PDL_TC=0 turns it off): the set-up before the kernel's
     // griddepcontrol.wait (barriers, TMEM allocation and start pattern, descriptor prefetch) runs
     // while the preceding kernel drains.  A CTA of this kernel fills an SM, so it never shares
@@ -595,10 +601,10 @@ bool launch_q4k(const DevW& W, const ActQ& a, int M, const float* bias, int relu
         cfg.attrs = attr;
         cfg.numAttrs = 1;
         const int uq = qkv ? 1 : 0;
-        cudaLaunchKernelEx(&cfg, k_mm_tc_q4k, mw, mx, my, W, a, M, bias, relu, y, q, uq, tstore, err, spin);
+        cudaLaunchKernelEx(&cfg, k_mm_tc_q4k, mw, mx, my, W, a, M, bias, relu, y, q, uq, tstore, err, spin, stall);
     } else {
         launch_k(k_mm_tc_q4k, dim3(grid), dim3(THREADS), (size_t)SMEM, st, mw, mx, my, W, a, M, bias, relu, y, q, qkv ? 1 : 0,
-                 tstore, err, spin);
+                 tstore, err, spin, stall);
     }
     return true;
 }

@@ -110,8 +110,8 @@ def _p(a):
 
 
 def test_set_tc_wait_cycles(cycles: int):
-    """Test hook: the tensor-core matmul's wait bound in clock cycles for later launches (0 = the
-    built-in bound of about one second)."""
+    """Test hook: cycles > 0 makes later tensor-core matmul launches wait first on a barrier that
+    nothing completes, every wait bounded by `cycles` (their error path runs); 0 = normal."""
     _ck(lib().t2sx_test_set_tc_wait_cycles(int(cycles)))
 
 

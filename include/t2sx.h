@@ -186,9 +186,11 @@ T2SX_API int t2sx_matmul(t2sx_weight* w, const float* x_dev, int64_t M, const fl
  * bounded wait (T2SX_ERR_TIMEOUT; its outputs are NaN); clears that state.  The reference has no
  * counterpart (ggml's CPU kernels do not wait on anything). */
 T2SX_API int t2sx_weight_sync(t2sx_weight* w, void* stream);
-/* Test hook, no counterpart in the reference: the wait bound (clock cycles) of the tensor-core
- * matmul for launches made (or graphs captured) from now on, so a test can make a wait run out
- * and check the error path; 0 restores the built-in bound of about one second. */
+/* Test hook, no counterpart in the reference.  cycles > 0: tensor-core matmuls launched (or
+ * graphs captured) from now on first wait on a barrier that nothing completes, and every wait of
+ * theirs is bounded by `cycles` clock cycles, so the wait runs out and the error path is taken
+ * (outputs NaN, T2SX_ERR_TIMEOUT); 0 restores normal operation with the built-in bound of about
+ * one second. */
 T2SX_API int t2sx_test_set_tc_wait_cycles(int64_t cycles);
 
 /* No counterpart in the reference (its ggml graphs allocate through the backend).  The same

@@ -53,6 +53,8 @@ def lib():
             "orc_extract_latent": (I, [P, P, I, P]), "orc_read_kv": (I, [P, I, I, I, P]),
             "orc_sample": (I, [P, I, P, P, P, I, F, F, F, I, P, P]),
             "orc_decode_step2": (I, [P, I, P, P, P, P, I, F, F, F, I, P, P, P]),
+            "orc_session_set_mode": (I, [P, I, I]),
+            "orc_matmul_ggml": (I, [I, P, I64, I64, P, I64, P]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -74,6 +76,15 @@ def matmul(wtype: int, w_bytes: np.ndarray, N: int, K: int, x: np.ndarray) -> np
     x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1, K)
     y = np.empty((x.shape[0], N), dtype=np.float32)
     rc = lib().orc_matmul(wtype, ptr(np.ascontiguousarray(w_bytes)), N, K, ptr(x), x.shape[0], ptr(y))
+    assert rc == 0
+    return y
+
+
+def matmul_ggml(wtype: int, w_bytes: np.ndarray, N: int, K: int, x: np.ndarray) -> np.ndarray:
+    """The matmul with ggml's generic vec_dot folds instead of the canonical order."""
+    x = np.ascontiguousarray(x, dtype=np.float32).reshape(-1, K)
+    y = np.empty((x.shape[0], N), dtype=np.float32)
+    rc = lib().orc_matmul_ggml(wtype, ptr(np.ascontiguousarray(w_bytes)), N, K, ptr(x), x.shape[0], ptr(y))
     assert rc == 0
     return y
 
@@ -165,6 +176,14 @@ class Session:
         self.h = lib().orc_session_new(model.h, n_slots, capacity)
         if not self.h:
             raise RuntimeError("oracle session init failed")
+
+    def set_mode(self, ggml_order: bool | int = False, kv_f32: bool = False):
+        """Evaluation order (before the first prefill): ggml_order=True (or the operator mask 7;
+        1 matmuls, 2 LayerNorm, 4 attention) follows ggml's CPU operator definitions; kv_f32
+        keeps an F32 KV cache (the reference's default; implies the full ggml order)."""
+        mask = 7 if ggml_order is True else int(ggml_order)
+        if lib().orc_session_set_mode(self.h, mask, int(kv_f32)) != 0:
+            raise RuntimeError("oracle mode must be set before the first prefill")
 
     def prefill(self, slot: int, x: np.ndarray, T_prompt: int, eos_mask=True, want_logits=False, want_y=False):
         x = np.ascontiguousarray(x, dtype=np.float32)

@@ -434,12 +434,81 @@ static float qdot_x(int wtype, const WRowX& e, int64_t K, const ActRow& a) {
     return acc;
 }
 
-int orc_matmul(int wtype, const void* w, int64_t N, int64_t K, const float* x, int64_t M, float* y) {
+// ---- ggml-order dot products ---------------------------------------------------------------
+// The float folds of ggml's generic (scalar) vec_dot kernels, restated from their published
+// definitions: the same integer block sums as above, folded the way those kernels fold them.
+//   Q8_0 x Q8_0 : sumf += (float)sumi * (d_w * d_x)
+//   Q4_0 x Q8_0 : sumf += ((float)sumi * d_w) * d_x
+//   Q5_0 x Q8_0 : sumf += (d_w * d_x) * (float)sumi
+//   Q4_K x Q8_K : per super-block eight integer lane sums aux[l] (element e -> lane e % 8) of
+//                 scale_j * q_w * q_x; sums[l] += (d_w * d_x) * aux[l]; sumf -= (dmin_w * d_x) * sumi_m;
+//                 after the last super-block sumf += sums[0..7] in order
+//   F16 x F16   : double sum of the f32 products, rounded to f32 once
+//   F32 x F32   : double sum of the f32 products, rounded to f32 once
+// These are the ISA-independent forms; ggml's SIMD builds split the sums over vector lanes
+// differently per instruction set, so no single order is "the" ggml order.
+static float qdot_x_ggml(int wtype, const WRowX& e, int64_t K, const ActRow& a) {
+    if (wtype == ORC_Q4_K) {
+        float sums[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        float sumf = 0.0f;
+        for (int64_t b = 0; b < K / 256; ++b) {
+            const BlkQ8K& x = a.q8k[b];
+            int aux[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+            for (int j = 0; j < 8; ++j)
+                for (int l = 0; l < 32; ++l)
+                    aux[l & 7] += e.sc[b * 8 + j] * ((int)e.q[b * 256 + 32 * j + l] * (int)x.qs[32 * j + l]);
+            int sumi = 0;
+            for (int j = 0; j < 16; ++j) sumi += (int)x.bsums[j] * e.mn[b * 8 + j / 2];
+            const float d = e.d[b] * x.d;
+            for (int l = 0; l < 8; ++l) sums[l] = sums[l] + d * (float)aux[l];
+            const float dmin = e.dmin[b] * x.d;
+            sumf = sumf - dmin * (float)sumi;
+        }
+        for (int l = 0; l < 8; ++l) sumf = sumf + sums[l];
+        return sumf;
+    }
+    float sumf = 0.0f;
+    for (int64_t b = 0; b < K / 32; ++b) {
+        const float sumi = (float)dot32_i8(&e.q[b * 32], a.q8[b].qs);
+        const float dw = e.dw[b], dx = a.q8[b].d;
+        float t;
+        if (wtype == ORC_Q8_0) t = sumi * (dw * dx);
+        else if (wtype == ORC_Q4_0) t = (sumi * dw) * dx;
+        else t = (dw * dx) * sumi;   // Q5_0
+        sumf = sumf + t;
+    }
+    return sumf;
+}
+
+static float fdot_ggml(int wtype, const uint8_t* w, int64_t K, const ActRow& a) {
+    double sumf = 0.0;
+    for (int64_t k = 0; k < K; ++k) {
+        const float wv = (wtype == ORC_F16) ? h2f(rd16(w + 2 * k)) : ((const float*)w)[k];
+        sumf += (double)(wv * a.f[k]);
+    }
+    return (float)sumf;
+}
+
+static int matmul_impl(int wtype, const void* w, int64_t N, int64_t K, const float* x, int64_t M, float* y, int ggml_order) {
     const int64_t rb = orc_row_bytes(wtype, K);
     if (rb <= 0) return -1;
     std::vector<ActRow> acts(M);
     for (int64_t m = 0; m < M; ++m) prep_act(wtype, x + m * K, K, acts[m]);
     const bool quant = wtype == ORC_Q8_0 || wtype == ORC_Q4_0 || wtype == ORC_Q5_0 || wtype == ORC_Q4_K;
+    if (ggml_order) {
+        #pragma omp parallel
+        {
+            WRowX e;
+            #pragma omp for schedule(static)
+            for (int64_t n = 0; n < N; ++n) {
+                const uint8_t* wr = (const uint8_t*)w + n * rb;
+                if (quant) expand_row(wtype, wr, K, e);
+                for (int64_t m = 0; m < M; ++m)
+                    y[m * N + n] = quant ? qdot_x_ggml(wtype, e, K, acts[m]) : fdot_ggml(wtype, wr, K, acts[m]);
+            }
+        }
+        return 0;
+    }
     if (!quant || M < 2) {
         #pragma omp parallel for schedule(static)
         for (int64_t n = 0; n < N; ++n)
@@ -457,6 +526,13 @@ int orc_matmul(int wtype, const void* w, int64_t N, int64_t K, const float* x, i
         }
     }
     return 0;
+}
+
+int orc_matmul(int wtype, const void* w, int64_t N, int64_t K, const float* x, int64_t M, float* y) {
+    return matmul_impl(wtype, w, N, K, x, M, y, 0);
+}
+int orc_matmul_ggml(int wtype, const void* w, int64_t N, int64_t K, const float* x, int64_t M, float* y) {
+    return matmul_impl(wtype, w, N, K, x, M, y, 1);
 }
 
 // ============================================================================================
@@ -484,6 +560,19 @@ void orc_layernorm(const float* x, const float* g, const float* b, int n, float 
     const float var = (float)(lanes_sum(lane2) / (double)n);
     const float scale = 1.0f / sqrtf(var + eps);
     for (int i = 0; i < n; ++i) y[i] = (v[i] * scale) * g[i] + b[i];
+}
+
+// ggml_norm as its CPU kernel defines it: sequential double sums, mean and variance rounded to
+// f32, y = (x - mean) * (1/sqrtf(var + eps)); then ggml_mul by gamma and ggml_add of beta.
+static void layernorm_ggml(const float* x, const float* g, const float* b, int n, float eps, float* y) {
+    double sum = 0.0;
+    for (int i = 0; i < n; ++i) sum += (double)x[i];
+    const float mean = (float)(sum / (double)n);
+    double sum2 = 0.0;
+    for (int i = 0; i < n; ++i) { const float v = x[i] - mean; y[i] = v; sum2 += (double)(v * v); }
+    const float var = (float)(sum2 / (double)n);
+    const float scale = 1.0f / sqrtf(var + eps);
+    for (int i = 0; i < n; ++i) y[i] = (y[i] * scale) * g[i] + b[i];
 }
 
 // ============================================================================================
@@ -547,6 +636,42 @@ static void attn_decode_head(const float* q, const uint16_t* k, const uint16_t* 
     const AttnState& R = lane[0];
     const float inv = 1.0f / R.l;
     for (int d = 0; d < 32; ++d) out[d] = R.o[d] * inv;
+}
+
+// ggml_flash_attn_ext's CPU kernel for one query row and head, as it defines it: positions in
+// increasing order, score = double sum of the f32 products q_d * k_d rounded to f32, times the
+// scale; online softmax with libm expf (M running maximum, S running sum: S = S * ms + vs); the
+// V accumulator VKQ is f16 for an F16 cache (every rescale and every multiply-add rounded back to
+// f16) and f32 for an F32 cache; out = VKQ * (1/S).  q holds f16-rounded values for an F16 cache
+// and the raw f32 values for an F32 cache.  kf/vf: F32 cache rows (used when k16 is null).
+static void attn_head_ggml(const float* q, const uint16_t* k16, const uint16_t* v16, const float* kf, const float* vf,
+                           int L, int64_t stride, float* out) {
+    float M = -INFINITY, S = 0.0f;
+    uint16_t vkq16[32];
+    float vkq32[32];
+    for (int d = 0; d < 32; ++d) { vkq16[d] = 0; vkq32[d] = 0.0f; }
+    for (int i = 0; i < L; ++i) {
+        double acc = 0.0;
+        if (k16) for (int d = 0; d < 32; ++d) acc += (double)(q[d] * h2f(k16[i * stride + d]));
+        else for (int d = 0; d < 32; ++d) acc += (double)(q[d] * kf[i * stride + d]);
+        float s = (float)acc * kAttnScale;
+        s = s + 0.0f;   // the mask value of a visible position
+        const float Mold = M;
+        float ms = 1.0f, vs = 1.0f;
+        if (s > M) {
+            M = s;
+            ms = expf(Mold - M);
+            if (v16) for (int d = 0; d < 32; ++d) vkq16[d] = f2h(h2f(vkq16[d]) * ms);
+            else for (int d = 0; d < 32; ++d) vkq32[d] = vkq32[d] * ms;
+        } else {
+            vs = expf(s - M);
+        }
+        if (v16) for (int d = 0; d < 32; ++d) vkq16[d] = f2h(h2f(vkq16[d]) + h2f(v16[i * stride + d]) * vs);
+        else for (int d = 0; d < 32; ++d) vkq32[d] = vkq32[d] + vf[i * stride + d] * vs;
+        S = S * ms + vs;
+    }
+    const float inv = (S == 0.0f) ? 0.0f : 1.0f / S;
+    for (int d = 0; d < 32; ++d) out[d] = (v16 ? h2f(vkq16[d]) : vkq32[d]) * inv;
 }
 
 void orc_attn_decode(const float* q, const uint16_t* k, const uint16_t* v, int L, float* out) {
@@ -701,6 +826,12 @@ struct Session {
     std::vector<int> n_pos, audio_off;
     std::vector<std::vector<uint16_t>> K, V;   // [slot*L + layer] -> [cap][d]
     std::vector<float> pe;                     // [cap][d]
+    // evaluation order, per operator: bit 0 the matmul folds, bit 1 LayerNorm, bit 2 flash
+    // attention; a set bit follows ggml's CPU operator definition, a clear bit the canonical
+    // order above (what the CUDA kernels reproduce)
+    int ggml_order = 0;
+    int kv_f32 = 0;                            // 1: F32 KV cache (the reference's default type)
+    std::vector<std::vector<float>> Kf, Vf;    // F32 cache rows when kv_f32
 };
 
 static int g_threads = 0;
@@ -731,9 +862,22 @@ int orc_slot_release(void* sess, int slot) {
 
 int orc_slot_n_pos(void* sess, int slot) { return ((Session*)sess)->n_pos[slot]; }
 
-static void matmul_rows(const Tensor* W, const Tensor* bias, const float* x, int64_t M, float* y) {
+int orc_session_set_mode(void* sess, int ggml_order, int kv_f32) {
+    Session* S = (Session*)sess;
+    for (int i = 0; i < S->n_slots; ++i) if (S->n_pos[i] != 0) return -1;   // set before any prefill
+    S->ggml_order = (ggml_order & 7) | (kv_f32 ? 7 : 0);
+    S->kv_f32 = kv_f32 ? 1 : 0;
+    if (S->kv_f32 && S->Kf.empty()) {
+        const size_t n = S->K.size(), per = (size_t)S->cap * S->m->hp[1];
+        S->Kf.assign(n, std::vector<float>(per, 0.0f));
+        S->Vf.assign(n, std::vector<float>(per, 0.0f));
+    }
+    return 0;
+}
+
+static void matmul_rows(const Tensor* W, const Tensor* bias, const float* x, int64_t M, float* y, int ggml_order = 0) {
     const int64_t K = W->ne[0], N = W->ne[1];
-    orc_matmul(W->type, W->data, N, K, x, M, y);
+    matmul_impl(W->type, W->data, N, K, x, M, y, ggml_order);
     if (bias) {
         const float* b = fdata(bias);
         for (int64_t m = 0; m < M; ++m) for (int64_t n = 0; n < N; ++n) y[m * N + n] = y[m * N + n] + b[n];
@@ -749,32 +893,49 @@ static void forward_rows(Session* S, int64_t T, const int* slot, const int* pos,
     const int hd = d / H;
     std::vector<float> qkv((size_t)T * 3 * d), attn((size_t)T * d), o((size_t)T * d), r((size_t)T * d),
         ln1((size_t)T * d), h((size_t)T * F), f((size_t)T * d);
+    const int go = S->ggml_order & 1, go_norm = S->ggml_order & 2, go_attn = S->ggml_order & 4, f32kv = S->kv_f32;
+    auto norm = [&](const float* in, const Tensor* g, const Tensor* b, float* out) {
+        if (go_norm) layernorm_ggml(in, fdata(g), fdata(b), d, 1e-5f, out);
+        else orc_layernorm(in, fdata(g), fdata(b), d, 1e-5f, out);
+    };
     for (int li = 0; li < nl; ++li) {
         const Model::Layer& Lw = m->layers[li];
-        matmul_rows(Lw.qkv_w, Lw.qkv_b, x, T, qkv.data());
-        // set_rows: K and V to f16 in the cache
+        matmul_rows(Lw.qkv_w, Lw.qkv_b, x, T, qkv.data(), go);
+        // set_rows: K and V into the cache (f16, or f32 for an F32 cache)
         for (int64_t t = 0; t < T; ++t) {
-            uint16_t* kd = &S->K[(size_t)slot[t] * nl + li][(size_t)pos[t] * d];
-            uint16_t* vd = &S->V[(size_t)slot[t] * nl + li][(size_t)pos[t] * d];
-            for (int i = 0; i < d; ++i) { kd[i] = f2h(qkv[t * 3 * d + d + i]); vd[i] = f2h(qkv[t * 3 * d + 2 * d + i]); }
+            const size_t cs = (size_t)slot[t] * nl + li, off = (size_t)pos[t] * d;
+            for (int i = 0; i < d; ++i) {
+                const float kv_k = qkv[t * 3 * d + d + i], kv_v = qkv[t * 3 * d + 2 * d + i];
+                if (f32kv) { S->Kf[cs][off + i] = kv_k; S->Vf[cs][off + i] = kv_v; }
+                S->K[cs][off + i] = f2h(kv_k);
+                S->V[cs][off + i] = f2h(kv_v);
+            }
         }
         #pragma omp parallel for schedule(dynamic)
         for (int64_t th = 0; th < T * H; ++th) {
             const int64_t t = th / H; const int hh = (int)(th % H);
+            const size_t cs = (size_t)slot[t] * nl + li;
             float qh[32];
-            for (int i = 0; i < hd; ++i) qh[i] = h2f(f2h(qkv[t * 3 * d + hh * hd + i]));
-            const uint16_t* kb = &S->K[(size_t)slot[t] * nl + li][hh * hd];
-            const uint16_t* vb = &S->V[(size_t)slot[t] * nl + li][hh * hd];
-            attn_decode_head(qh, kb, vb, L[t], d, &attn[t * d + hh * hd]);
+            for (int i = 0; i < hd; ++i) {
+                const float qv = qkv[t * 3 * d + hh * hd + i];
+                qh[i] = f32kv ? qv : h2f(f2h(qv));   // an F16 cache takes an f16 query
+            }
+            float* o_th = &attn[t * d + hh * hd];
+            if (f32kv)
+                attn_head_ggml(qh, nullptr, nullptr, &S->Kf[cs][hh * hd], &S->Vf[cs][hh * hd], L[t], d, o_th);
+            else if (go_attn)
+                attn_head_ggml(qh, &S->K[cs][hh * hd], &S->V[cs][hh * hd], nullptr, nullptr, L[t], d, o_th);
+            else
+                attn_decode_head(qh, &S->K[cs][hh * hd], &S->V[cs][hh * hd], L[t], d, o_th);
         }
-        matmul_rows(Lw.out_w, Lw.out_b, attn.data(), T, o.data());
+        matmul_rows(Lw.out_w, Lw.out_b, attn.data(), T, o.data(), go);
         for (int64_t i = 0; i < T * d; ++i) r[i] = x[i] + o[i];
-        for (int64_t t = 0; t < T; ++t) orc_layernorm(&r[t * d], fdata(Lw.ln1_w), fdata(Lw.ln1_b), d, 1e-5f, &ln1[t * d]);
-        matmul_rows(Lw.up_w, Lw.up_b, ln1.data(), T, h.data());
+        for (int64_t t = 0; t < T; ++t) norm(&r[t * d], Lw.ln1_w, Lw.ln1_b, &ln1[t * d]);
+        matmul_rows(Lw.up_w, Lw.up_b, ln1.data(), T, h.data(), go);
         for (auto& v : h) v = (v > 0.0f) ? v : 0.0f;
-        matmul_rows(Lw.down_w, Lw.down_b, h.data(), T, f.data());
+        matmul_rows(Lw.down_w, Lw.down_b, h.data(), T, f.data(), go);
         for (int64_t i = 0; i < T * d; ++i) r[i] = ln1[i] + f[i];
-        for (int64_t t = 0; t < T; ++t) orc_layernorm(&r[t * d], fdata(Lw.ln2_w), fdata(Lw.ln2_b), d, 1e-5f, &x[t * d]);
+        for (int64_t t = 0; t < T; ++t) norm(&r[t * d], Lw.ln2_w, Lw.ln2_b, &x[t * d]);
     }
 }
 
@@ -895,7 +1056,7 @@ int orc_prefill(void* sess, int slot, const float* x, int nq, int T_prompt, int 
     forward_rows(S, nq, sl.data(), pos.data(), L.data(), xs.data());
     if (y_out) memcpy(y_out, xs.data(), sizeof(float) * xs.size());
     std::vector<float> logits(m->hp[5]);
-    matmul_rows(m->lm_head, nullptr, &xs[(size_t)(nq - 1) * d], 1, logits.data());
+    matmul_rows(m->lm_head, nullptr, &xs[(size_t)(nq - 1) * d], 1, logits.data(), S->ggml_order & 1);
     if (logits_out) memcpy(logits_out, logits.data(), sizeof(float) * logits.size());
     *token_out = pick_greedy(m, logits.data(), nullptr, 1.0f, eos_mask);
     S->n_pos[slot] = nq;
@@ -927,7 +1088,7 @@ static int decode_forward(Session* S, int n, const int32_t* slots, const int32_t
     }
     forward_rows(S, n, sl.data(), pos.data(), L.data(), x.data());
     logits.assign((size_t)n * V, 0.0f);
-    matmul_rows(m->lm_head, nullptr, x.data(), n, logits.data());
+    matmul_rows(m->lm_head, nullptr, x.data(), n, logits.data(), S->ggml_order & 1);
     for (int i = 0; i < n; ++i) S->n_pos[slots[i]] += 1;
     return 0;
 }

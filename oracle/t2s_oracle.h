@@ -73,6 +73,16 @@ int      orc_decode_step2(void* sess, int n, const int32_t* slots, const int32_t
                           float temperature, float rp, int eos_mask, int32_t* sampled_out,
                           int32_t* greedy_out, float* logits_out);
 int      orc_slot_n_pos(void* sess, int slot);
+// Evaluation order of the session (before its first prefill; -1 otherwise).  ggml_order is a
+// mask of operators that follow ggml's CPU operator definitions instead of the canonical order
+// the CUDA kernels reproduce: 1 the matmuls (generic vec_dot folds), 2 LayerNorm (sequential
+// double sums), 4 flash attention (per-query sequential fold, f16 V accumulator, libm expf); 7 =
+// all.  kv_f32 = 1 keeps an F32 KV cache (the reference's default kv_cache_type: f32 query and V
+// accumulator; implies 7).
+int      orc_session_set_mode(void* sess, int ggml_order, int kv_f32);
+// The matmul with ggml's generic vec_dot folds (see orc_session_set_mode).
+int      orc_matmul_ggml(int wtype, const void* w, int64_t N, int64_t K,
+                         const float* x, int64_t M, float* y);
 // Extract-latent codes of HuBERT frames f32 [T][768]: writes (T - 2) / 2 + 1 codes, returns that
 // count (-1 on a missing tensor or T < 2).
 int      orc_extract_latent(void* model, const float* hubert, int T, int32_t* codes_out);

@@ -575,11 +575,12 @@ def test_flex_step_errors(t2sx_mod):
 
 
 def test_tc_wait_timeout_reported_and_recovered(t2sx_mod, orc):
-    """The tensor-core matmul's barrier waits are bounded.  With the bound cut to one cycle (test
-    hook) its CTAs give up, drain the copies they issued, free their TMEM and store NaN, and the
-    failure reaches the host as T2SX_ERR_TIMEOUT: through t2sx_weight_sync for the isolated matmul
-    and through the call's status for a session prefill.  With the bound restored, the same
-    weight and a new session give bit-exact results again: the GPU context stays usable."""
+    """The tensor-core matmul's barrier waits are bounded.  The test hook makes each CTA's fold
+    warps first wait on a barrier that nothing completes, bounded by 100k cycles (about 50 us):
+    the wait runs out, the CTA gives up, drains the copies it issued, frees its TMEM and stores
+    NaN, and the failure reaches the host as T2SX_ERR_TIMEOUT -- through t2sx_weight_sync for
+    the isolated matmul and through the call's status for a session prefill.  With the hook off,
+    the same weight and a new session give bit-exact results again: the context stays usable."""
     _need_gpu()
     import synth
     T = t2sx_mod
@@ -596,7 +597,7 @@ def test_tc_wait_timeout_reported_and_recovered(t2sx_mod, orc):
     lengths = [(20, 12, 41 + i) for i in range(4)]   # 128 prefill rows: the tcgen05 kernel
     prompts = [synth.session_inputs(seed, tt, tp) for tt, tp, seed in lengths]
     try:
-        T.test_set_tc_wait_cycles(1)
+        T.test_set_tc_wait_cycles(100_000)
         w.matmul(xd.data_ptr(), M, yd.data_ptr(), stream=stream)
         with pytest.raises(T.T2SXError) as e:
             w.sync(stream)
