@@ -33,7 +33,8 @@ def nvcc() -> str:
 
 
 def sources():
-    return sorted(glob.glob(os.path.join(CSRC, "*.cu")))
+    """CUDA sources and the host C++ of the reference-compatible interface (t2s_session.cpp)."""
+    return sorted(glob.glob(os.path.join(CSRC, "*.cu")) + glob.glob(os.path.join(CSRC, "*.cpp")))
 
 
 def _stale(target, deps):
@@ -44,7 +45,8 @@ def _stale(target, deps):
 
 
 def build(force: bool = False, verbose: bool = False) -> str:
-    deps = sources() + glob.glob(os.path.join(CSRC, "*.cuh")) + [os.path.join(ROOT, "include", "t2sx.h"), __file__]
+    deps = (sources() + glob.glob(os.path.join(CSRC, "*.cuh")) + glob.glob(os.path.join(ROOT, "include", "*.h")) +
+            glob.glob(os.path.join(ROOT, "include", "gpt_sovits", "*.h")) + [__file__])
     if not force and not _stale(LIB, deps):
         return LIB
     objdir = os.path.join(HERE, "_build")

@@ -376,6 +376,9 @@ struct t2sx_model {
     const float* ssl_b = nullptr;
     const float* code_half_norm = nullptr;
     int n_codes = 0;
+    // GGUF type and shape of every tensor of the file (t2sx_model_tensor_info)
+    struct TInfo { int type; int nd; int64_t ne[4]; };
+    std::map<std::string, TInfo> tinfo;
 };
 
 static const float* fptr(char* base, size_t off) { return (const float*)(base + off); }
@@ -520,6 +523,10 @@ extern "C" int t2sx_model_load(const char* path, int32_t device, t2sx_model** ou
     m->ssl_b = fptr(base, sbo);
     m->code_half_norm = fptr(base, hno);
     m->n_codes = (int)cb->ne[1];
+    for (const auto& kv : g.t) {
+        t2sx_model::TInfo ti{kv.second.type, kv.second.nd, {kv.second.ne[0], kv.second.ne[1], kv.second.ne[2], kv.second.ne[3]}};
+        m->tinfo[kv.first] = ti;
+    }
     *out = m.release();
     return T2SX_OK;
 }
@@ -639,6 +646,8 @@ struct t2sx_session {
     int32_t* tail_ctr = nullptr;   // ticket of the last-CTA matmul tails (self-resetting)
     int last_rows = 0;             // rows of the last logits
     const float* last_logits = nullptr;
+    int last_hidden_rows = 0;      // rows of the last pass's final-layer output
+    const float* last_hidden = nullptr;
     const int32_t* last_greedy = nullptr;
     float* noise = nullptr;        // [n_slots][V] Exp(1) noise by sorted position (stochastic sampling)
     bool noise_on = false;
@@ -1133,6 +1142,8 @@ extern "C" int t2sx_prefill(t2sx_session* s, int32_t n, const int32_t* slots, co
         s->last_rows = ns;
         s->last_logits = w.logits;
         s->last_greedy = w.greedy;
+        s->last_hidden_rows = T;
+        s->last_hidden = w.x;
         xoff += rows;
         i0 = i1;
     }
@@ -1233,6 +1244,8 @@ static int launch_steps(t2sx_session* s, int n_steps) {
     s->last_rows = (int)s->active.size();
     s->last_logits = s->dec.logits;
     s->last_greedy = s->dec.greedy;
+    s->last_hidden_rows = (int)s->active.size();
+    s->last_hidden = s->dec.x;
     return T2SX_OK;
 }
 
@@ -1357,6 +1370,8 @@ extern "C" int t2sx_decode_step_host(t2sx_session* s, const int32_t* tokens_in, 
         s->last_rows = T;
         s->last_logits = s->dec.logits;
         s->last_greedy = s->dec.greedy;
+        s->last_hidden_rows = T;
+        s->last_hidden = s->dec.x;
         CK(cudaStreamSynchronize(s->st));
         memcpy(tokens_out, s->pin_out, (size_t)T * 4);
         CK(cudaEventElapsedTime(&s->last_ms, s->ev0, s->ev1));
@@ -1461,6 +1476,8 @@ extern "C" int t2sx_flex_step(t2sx_session* s, int32_t n_dec, const int32_t* dec
     s->last_rows = ns;
     s->last_logits = w.logits;
     s->last_greedy = w.greedy;
+    s->last_hidden_rows = T;
+    s->last_hidden = w.x;
     if ((rc = check_err_flag(s))) return rc;
     for (int i = 0; i < n_dec; ++i) s->n_pos_h[dec_slots[i]] += 1;
     for (int i = 0; i < n_pre; ++i)
@@ -1487,6 +1504,28 @@ extern "C" int t2sx_read_logits(t2sx_session* s, float* out, int32_t max_rows, i
     if (!s->last_logits) return fail(T2SX_ERR_STATE, "no logits yet");
     CK(cudaMemcpy(out, s->last_logits, (size_t)n * s->V * 4, cudaMemcpyDeviceToHost));
     if (rows) *rows = n;
+    return T2SX_OK;
+}
+
+extern "C" int t2sx_read_hidden(t2sx_session* s, float* out, int32_t max_rows, int32_t* rows) {
+    if (!s || !out || max_rows < 0) return fail(T2SX_ERR_INVALID, "t2sx_read_hidden: bad arguments");
+    DeviceGuard dg_;
+    CK(dg_.set(s->m->device));
+    CK(cudaStreamSynchronize(s->st));
+    if (!s->last_hidden) return fail(T2SX_ERR_STATE, "t2sx_read_hidden: no pass yet");
+    const int n = s->last_hidden_rows < max_rows ? s->last_hidden_rows : max_rows;
+    CK(cudaMemcpy(out, s->last_hidden, (size_t)n * kD * 4, cudaMemcpyDeviceToHost));
+    if (rows) *rows = n;
+    return T2SX_OK;
+}
+
+extern "C" int t2sx_model_tensor_info(const t2sx_model* m, const char* name, int32_t* type, int32_t* n_dims, int64_t* ne) {
+    if (!m || !name) return fail(T2SX_ERR_INVALID, "t2sx_model_tensor_info: null argument");
+    auto it = m->tinfo.find(name);
+    if (it == m->tinfo.end()) return fail(T2SX_ERR_INVALID, "t2sx_model_tensor_info: no tensor '%s' in the GGUF", name);
+    if (type) *type = it->second.type;
+    if (n_dims) *n_dims = it->second.nd;
+    if (ne) for (int i = 0; i < 4; ++i) ne[i] = it->second.ne[i];
     return T2SX_OK;
 }
 

@@ -58,6 +58,8 @@ SIGNATURES = {
     "t2sx_matmul": (C.c_int, [_P, _P, _I64, _P, _P, _P]),
     "t2sx_matmul_noalloc": (C.c_int, [_P, _P, _I64, _P, _P, _P]),
     "t2sx_weight_sync": (C.c_int, [_P, _P]),
+    "t2sx_read_hidden": (C.c_int, [_P, _P, _I, _P]),
+    "t2sx_model_tensor_info": (C.c_int, [_P, C.c_char_p, _P, _P, _P]),
     "t2sx_test_set_tc_wait_cycles": (C.c_int, [_I64]),
     "t2sx_kvcache_create": (C.c_int, [_I, _I, _I, _P]),
     "t2sx_kvcache_free": (None, [_P]),
@@ -288,6 +290,13 @@ class Session:
         rows = C.c_int32(0)
         _ck(lib().t2sx_read_logits(self.h, _p(out), max_rows, C.byref(rows)))
         return out[: rows.value]
+
+    def read_hidden(self, max_rows: int):
+        """Final-layer rows f32 [rows][d] of the last pass."""
+        out = np.empty((max_rows, self.model.d), dtype=np.float32)
+        n = C.c_int32(0)
+        _ck(lib().t2sx_read_hidden(self.h, _p(out), max_rows, C.byref(n)))
+        return out[:n.value]
 
     def read_kv(self, slot: int, layer: int, which: int):
         n = self.slot_n_pos(slot)

@@ -141,6 +141,15 @@ T2SX_API int t2sx_read_logits(t2sx_session* s, float* out, int32_t max_rows, int
 T2SX_API int t2sx_flex_step(t2sx_session* s, int32_t n_dec, const int32_t* dec_slots, const int32_t* dec_tokens,
                             int32_t n_pre, const int32_t* pre_slots, const int32_t* n_query, const int32_t* t_prompt,
                             const float* x, int32_t* tokens_out);
+/* Final-layer output rows f32 [rows][d] of the last pass (the flex graph's y, t2s.h:530): prefill
+ * and flex passes give every row of the pass in pass order (flex: the decode rows, then the
+ * prefill rows in call order; a prefill of more than 32768 rows keeps its last chunk only),
+ * decode steps one row per active slot. */
+T2SX_API int t2sx_read_hidden(t2sx_session* s, float* out, int32_t max_rows, int32_t* rows);
+/* GGUF type, number of dimensions and ne[4] of a named tensor of the loaded file (the shapes
+ * t2s_model_weights exposes, t2s.h:231-243; tests/t2s/test_t2s_loader.cpp:33-92). */
+T2SX_API int t2sx_model_tensor_info(const t2sx_model* model, const char* name, int32_t* type, int32_t* n_dims,
+                                    int64_t* ne);
 /* Cached f16 K (which=0) or V (which=1) of one slot and layer: out [n_pos][d] (uint16 bits). */
 T2SX_API int t2sx_read_kv(t2sx_session* s, int32_t slot, int32_t layer, int32_t which, uint16_t* out);
 /* Seen-token mask used by the repetition penalty (t2s_session_get_seen_mask, t2s.h:487): set
