@@ -152,6 +152,9 @@ def run_ours(args):
         dist.barrier()
     path = synth.ensure_gguf(w["wtype"], w["seed"], n_layer=24)
 
+    # roofline denominators this run measures itself: L2 read bandwidth and the int8 tensor rate
+    probes = measure_probes(local) if (rank == 0 and not args.no_probes) else None
+
     W, K = args.warmup, args.steps
     max_prompt = max(tt + tp for tt, tp, _ in mine)
     slot_size = max_prompt + W + K + 1
@@ -314,9 +317,28 @@ def run_ours(args):
             "kernel_ms_at_start": {k: round(v, 4) for k, v in prof_start.items()},
             "clocks": clocks,
         }
+        if probes is not None:
+            line["peaks_probe"] = probes
+            # the batched tcgen05 Q4_K matmul (QKV projection, one launch at this run's rows):
+            # algorithmic int8 ops 2*M*N*K per launch, the tensor core issues 3x that (three planes)
+            ops = 2.0 * per * 1536 * 512
+            tops = ops / (prof["mm_qkv"] * 1e-3) / 1e12
+            line["roofline_tc_qkv"] = {"kernel": "k_mm_tc_q4k (QKV, 1536 x 512)" if per >= 64 else "QKV matmul",
+                                       "bound": "tensor", "achieved": round(tops, 1), "unit": "TOP/s (int8)",
+                                       "peak": probes["i8_tensor_tops"], "frac": round(tops / probes["i8_tensor_tops"], 4),
+                                       "issued_frac": round(3 * tops / probes["i8_tensor_tops"], 4),
+                                       "rows": per, "launch_ms": round(prof["mm_qkv"], 4)}
         if parity is not None:
             line["parity"] = parity
         if bs1 is not None:
+            if probes is not None:
+                # bs=1 step: the Q8_0 weights (80,773,664 B) from L2 and the K/V prefix from HBM,
+                # 49,152 B per position at the steps' mean context
+                kv = 49152.0 * (bs1["context"][0] + bs1["context"][1]) / 2
+                t_min = 80773664 / (probes["l2_read_gbs"] * 1e9) + kv / (peaks["hbm_gbs"] * 1e9)
+                bs1["roofline"] = {"l2_bytes": 80773664, "hbm_bytes": int(kv), "bound_ms": round(t_min * 1e3, 4),
+                                   "frac": round(t_min * 1e3 / bs1["p50_step_ms"], 4),
+                                   "peaks": "l2_read_gbs of peaks_probe, hbm_gbs of MEASURED_PEAKS.json"}
             line["bs1"] = bs1
         if cpu is not None:
             line["cpu_baseline"] = cpu
@@ -364,6 +386,17 @@ def oracle_streams(workload, path, n_sessions, n_steps, timed_steps=None):
                      f"and {n_steps - timed} untimed ones (oracle restatement; ggml is absent from the "
                      f"reference snapshot)"}
     return cpu, np.stack(toks)
+
+
+def measure_probes(device):
+    """L2 read bandwidth (best of three L2-resident sizes) and the dense int8 tcgen05 rate (best
+    of one and two issuing threads per SM), measured by the library's own probe kernels."""
+    import t2sx
+    l2 = max(t2sx.probe_l2_read_gbs(device, mb << 20, 100) for mb in (16, 32, 48))
+    i8 = max(t2sx.probe_i8_mma_tops(device, 20000, k) for k in (1, 2))
+    return {"l2_read_gbs": round(l2, 1), "i8_tensor_tops": round(i8, 1),
+            "how": "t2sx_probe_l2_read: 16/32/48 MiB buffers streamed with ld.global.cg, 100 passes; "
+                   "t2sx_probe_i8_mma: tcgen05.mma.kind::i8 M128 N256 K32 from smem on every SM"}
 
 
 def bs1_step(device, steps, warm=5):
@@ -623,6 +656,7 @@ def main():
     ap.add_argument("--parity-sessions", type=int, default=8,
                     help="sessions whose token streams are compared with the CPU oracle (rank 0)")
     ap.add_argument("--no-bs1", action="store_true", help="skip the bs=1 step measurement")
+    ap.add_argument("--no-probes", action="store_true", help="skip the L2 / int8 tensor peak probes")
     ap.add_argument("--bs1-steps", type=int, default=200)
     ap.add_argument("--sweep", choices=["matmul", "attention"], default=None,
                     help="isolated kernel sweep instead of the decode workload (--steps = timed iterations)")

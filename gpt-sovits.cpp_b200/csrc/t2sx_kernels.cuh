@@ -202,6 +202,8 @@ bool matmul_ln(const DevW& W, const LnIn& ln, int M, const float* bias, int relu
 void matmul(const DevW& W, const ActQ& a, int M, const float* bias, int relu, float* y, cudaStream_t st,
             const Epi& epi = Epi());
 // tcgen05 path (TMA-fed, TMEM accumulators; Q4_K weights) for large M; false if not supported.
+// int8 tensor-core peak probe (t2sx_tc.cu): one launch on every SM; false if not launchable
+bool probe_i8_mma(int iters, int issuers, int32_t* err, cudaStream_t st, int* ctas);
 bool matmul_tc(const DevW& W, const ActQ& a, int M, const float* bias, int relu, float* y, const QKVStore* qkv,
                cudaStream_t st);
 // Rows from which matmul() takes the tcgen05 path (T2SX_TC_MIN_ROWS overrides).

@@ -609,7 +609,83 @@ bool launch_q4k(const DevW& W, const ActQ& a, int M, const float* bias, int relu
     return true;
 }
 
+// ---------------------------------------------------------------------------------------------
+// int8 tensor-core peak probe: each CTA (one per SM) issues tcgen05.mma.kind::i8 with M = 128,
+// N = 256, K = 32 from zero-filled shared-memory operands (the same 128-byte-swizzled K-major
+// layout as the matmul's stages), `issuers` threads per CTA into their own 256-column TMEM
+// accumulators, then waits (bounded) for the last MMA and frees TMEM.  The operands' values do
+// not change the instruction's cost.
+// ---------------------------------------------------------------------------------------------
+constexpr int PB_N = 256;
+constexpr int PB_A = BM * 128;     // 16 KB: 128 rows x 128 B (four K-steps of 32)
+constexpr int PB_B = PB_N * 128;   // 32 KB
+// more shared memory than two CTAs can share, so each SM runs one probe CTA
+constexpr int PB_SMEM = 120 * 1024;
+constexpr uint32_t kIdescProbe =
+    (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(PB_N >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+
+__global__ void __launch_bounds__(64, 1) k_probe_i8_mma(int iters, int issuers, int32_t* err) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint64_t* bar = (uint64_t*)(smem + PB_A + PB_B);
+    uint32_t* holder = (uint32_t*)(bar + 1);
+    const int tid = threadIdx.x, warp = tid >> 5;
+    for (int i = tid; i < (PB_A + PB_B) / 16; i += blockDim.x) reinterpret_cast<int4*>(smem)[i] = make_int4(0, 0, 0, 0);
+    if (tid == 0) {
+        bar_init(smem_u32(bar), (uint32_t)issuers);
+        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    }
+    if (warp == 0) {
+        __syncwarp();
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(holder)),
+                     "r"(TMEM_COLS) : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
+    }
+    fence_proxy_async_smem();   // the zeroed operands are read by the tensor core (async proxy)
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *holder;
+    if ((tid & 31) == 0 && warp < issuers) {
+        const uint64_t a0 = sdesc(smem_u32(smem)), b0 = sdesc(smem_u32(smem + PB_A));
+        const uint32_t d = tmem + (uint32_t)(warp * PB_N);
+        for (int it = 0; it < iters; ++it)
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+                tc_mma_i8(d, a0 + (uint64_t)((kk * 32) >> 4), b0 + (uint64_t)((kk * 32) >> 4), kIdescProbe,
+                          (it | kk) ? 1u : 0u);
+        tc_commit(smem_u32(bar));
+        const long long t0 = clock64();
+        bool done = false;
+        while (!(done = bar_try(smem_u32(bar), 0)) && clock64() - t0 < kSpinCycles) {}
+        if (!done && err) atomicExch(err, kErrTimeout);
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        __syncwarp();
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+    }
+}
+
 }  // namespace tc
+
+// One launch of the probe on every SM of the current device; *ctas = CTAs launched.
+bool probe_i8_mma(int iters, int issuers, int32_t* err, cudaStream_t st, int* ctas) {
+    if (iters <= 0 || issuers < 1 || issuers > 2) return false;
+    static PerDeviceOnce setup;
+    int n_sm = 0;
+    if (!setup.ensure([](int dev, int* sms) {
+            if (cudaFuncSetAttribute(tc::k_probe_i8_mma, cudaFuncAttributeMaxDynamicSharedMemorySize, tc::PB_SMEM) != cudaSuccess)
+                return false;
+            return cudaDeviceGetAttribute(sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && *sms > 0;
+        }, &n_sm))
+        return false;
+    tc::k_probe_i8_mma<<<n_sm, 64, tc::PB_SMEM, st>>>(iters, issuers, err);
+    if (ctas) *ctas = n_sm;
+    return cudaGetLastError() == cudaSuccess;
+}
 
 bool matmul_tc(const DevW& W, const ActQ& a, int M, const float* bias, int relu, float* y, const QKVStore* qkv,
                cudaStream_t st) {

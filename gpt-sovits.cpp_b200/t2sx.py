@@ -58,6 +58,8 @@ SIGNATURES = {
     "t2sx_matmul": (C.c_int, [_P, _P, _I64, _P, _P, _P]),
     "t2sx_matmul_noalloc": (C.c_int, [_P, _P, _I64, _P, _P, _P]),
     "t2sx_weight_sync": (C.c_int, [_P, _P]),
+    "t2sx_probe_l2_read": (C.c_int, [_I, _I64, _I, _P]),
+    "t2sx_probe_i8_mma": (C.c_int, [_I, _I, _I, _P]),
     "t2sx_read_hidden": (C.c_int, [_P, _P, _I, _P]),
     "t2sx_model_tensor_info": (C.c_int, [_P, C.c_char_p, _P, _P, _P]),
     "t2sx_test_set_tc_wait_cycles": (C.c_int, [_I64]),
@@ -115,6 +117,20 @@ def test_set_tc_wait_cycles(cycles: int):
     """Test hook: cycles > 0 makes later tensor-core matmul launches wait first on a barrier that
     nothing completes, every wait bounded by `cycles` (their error path runs); 0 = normal."""
     _ck(lib().t2sx_test_set_tc_wait_cycles(int(cycles)))
+
+
+def probe_l2_read_gbs(device: int = 0, bytes_: int = 32 << 20, iters: int = 200) -> float:
+    """Measured L2 read bandwidth (GB/s) of an L2-resident buffer."""
+    v = C.c_double(0)
+    _ck(lib().t2sx_probe_l2_read(device, bytes_, iters, C.byref(v)))
+    return v.value
+
+
+def probe_i8_mma_tops(device: int = 0, iters: int = 20000, issuers: int = 1) -> float:
+    """Measured dense int8 tcgen05 rate (TOP/s)."""
+    v = C.c_double(0)
+    _ck(lib().t2sx_probe_i8_mma(device, iters, issuers, C.byref(v)))
+    return v.value
 
 
 def device_count() -> int:

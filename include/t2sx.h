@@ -214,6 +214,15 @@ T2SX_API int t2sx_test_set_tc_wait_cycles(int64_t cycles);
 T2SX_API int t2sx_matmul_noalloc(t2sx_weight* w, const float* x_dev, int64_t M, const float* bias_dev,
                                  float* y_dev, void* stream);
 
+/* ---- roofline denominators measured on the device (no counterpart in the reference) ----
+ * L2 read bandwidth in GB/s: a zero-filled buffer of `bytes` (1 MiB .. 1 GiB; resident in L2 when
+ * it fits) streamed `iters` times with 16-byte loads cached in L2 only, after three warm passes. */
+T2SX_API int t2sx_probe_l2_read(int32_t device, int64_t bytes, int32_t iters, double* gbs);
+/* Dense int8 tensor-core rate in TOP/s (10^12 integer multiply-adds x 2 per second): every SM
+ * issues `iters` x 4 tcgen05.mma.kind::i8 instructions of M = 128, N = 256, K = 32 from shared
+ * memory, from `issuers` (1 or 2) threads into separate TMEM accumulators. */
+T2SX_API int t2sx_probe_i8_mma(int32_t device, int32_t iters, int32_t issuers, double* tops);
+
 /* ---- isolated batched attention over a paged f16 KV cache (one layer) ----
  * The attention step of t2s_attention_block_forward (src/t2s/block.cpp:575-608) on a stand-alone
  * cache, with the decode and prefill kernels of the step: softmax(q . k^T / sqrt(32)) . v per head

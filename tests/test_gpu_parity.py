@@ -626,3 +626,14 @@ def test_tc_wait_timeout_reported_and_recovered(t2sx_mod, orc):
     assert list(first) == [os_.prefill(i, xs[i], lengths[i][1])[0] for i in range(4)]
     s.close()
     m.close()
+
+
+def test_roofline_probes_measure_the_device(t2sx_mod):
+    """The measured roofline denominators: an L2-resident 32 MiB buffer reads faster than the
+    HBM copy bandwidth, and the dense int8 tcgen05 loop runs at a rate of the B200's class
+    (nominal 4.5 POP/s)."""
+    _need_gpu()
+    l2 = t2sx_mod.probe_l2_read_gbs(0, 32 << 20, 50)
+    tops = t2sx_mod.probe_i8_mma_tops(0, 4000, 1)
+    assert 6000.0 < l2 < 100000.0, l2
+    assert 500.0 < tops < 10000.0, tops
