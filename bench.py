@@ -392,10 +392,10 @@ def measure_probes(device):
     """L2 read bandwidth (best of three L2-resident sizes) and the dense int8 tcgen05 rate (best
     of one and two issuing threads per SM), measured by the library's own probe kernels."""
     import t2sx
-    l2 = max(t2sx.probe_l2_read_gbs(device, mb << 20, 100) for mb in (16, 32, 48))
+    l2 = max(t2sx.probe_l2_read_gbs(device, mb << 20, 100) for mb in (8, 16, 32, 48))
     i8 = max(t2sx.probe_i8_mma_tops(device, 20000, k) for k in (1, 2))
     return {"l2_read_gbs": round(l2, 1), "i8_tensor_tops": round(i8, 1),
-            "how": "t2sx_probe_l2_read: 16/32/48 MiB buffers streamed with ld.global.cg, 100 passes; "
+            "how": "t2sx_probe_l2_read: 8/16/32/48 MiB buffers streamed with ld.global.cg, 100 passes; "
                    "t2sx_probe_i8_mma: tcgen05.mma.kind::i8 M128 N256 K32 from smem on every SM"}
 
 

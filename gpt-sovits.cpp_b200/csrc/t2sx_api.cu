@@ -1546,7 +1546,7 @@ extern "C" int t2sx_read_kv(t2sx_session* s, int32_t slot, int32_t layer, int32_
             for (int h = 0; h < kHeads; ++h)
                 memcpy(out + (size_t)i * kD + h * kHeadDim, &page[((size_t)h * kPage + (i - p0)) * kHeadDim], kHeadDim * 2);
     }
-    return n;
+    return T2SX_OK;
 }
 
 extern "C" int t2sx_set_seen(t2sx_session* s, int32_t slot, const uint8_t* seen) {

@@ -15,22 +15,23 @@ int t2sx_set_error(int code, const char* msg);
 
 namespace {
 
-// Grid-stride read of n16 16-byte words with ld.global.cg (cached in L2 only), four independent
+// Grid-stride read of n16 16-byte words with ld.global.cg (cached in L2 only), eight independent
 // loads in flight per thread; the xor of everything read decides a store that never happens
 // for the zero-filled buffer, so the loads are kept.
 __global__ void __launch_bounds__(256) k_l2_read(const int4* __restrict__ p, int64_t n16, int* __restrict__ sink) {
+    constexpr int U = 8;
     int x = 0;
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
     int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    for (; i + 3 * stride < n16; i += 4 * stride) {
-        int4 v[4];
+    for (; i + (U - 1) * stride < n16; i += U * stride) {
+        int4 v[U];
 #pragma unroll
-        for (int u = 0; u < 4; ++u)
+        for (int u = 0; u < U; ++u)
             asm volatile("ld.global.cg.v4.s32 {%0, %1, %2, %3}, [%4];\n"
                          : "=r"(v[u].x), "=r"(v[u].y), "=r"(v[u].z), "=r"(v[u].w)
                          : "l"(p + i + u * stride));
 #pragma unroll
-        for (int u = 0; u < 4; ++u) x ^= v[u].x ^ v[u].y ^ v[u].z ^ v[u].w;
+        for (int u = 0; u < U; ++u) x ^= v[u].x ^ v[u].y ^ v[u].z ^ v[u].w;
     }
     for (; i < n16; i += stride) {
         int4 v;

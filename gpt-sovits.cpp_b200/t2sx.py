@@ -317,9 +317,7 @@ class Session:
     def read_kv(self, slot: int, layer: int, which: int):
         n = self.slot_n_pos(slot)
         out = np.zeros((max(n, 1), self.model.d), dtype=np.uint16)
-        rc = lib().t2sx_read_kv(self.h, slot, layer, which, _p(out))
-        if rc < 0 or rc != n:
-            _ck(rc if rc > 0 else ERR_INVALID)
+        _ck(lib().t2sx_read_kv(self.h, slot, layer, which, _p(out)))
         return out[:n]
 
     def set_exp_noise(self, noise):

@@ -150,7 +150,8 @@ T2SX_API int t2sx_read_hidden(t2sx_session* s, float* out, int32_t max_rows, int
  * t2s_model_weights exposes, t2s.h:231-243; tests/t2s/test_t2s_loader.cpp:33-92). */
 T2SX_API int t2sx_model_tensor_info(const t2sx_model* model, const char* name, int32_t* type, int32_t* n_dims,
                                     int64_t* ne);
-/* Cached f16 K (which=0) or V (which=1) of one slot and layer: out [n_pos][d] (uint16 bits). */
+/* Cached f16 K (which=0) or V (which=1) of one slot and layer: out [n_pos][d] (uint16 bits),
+ * n_pos = t2sx_session_slot_n_pos. */
 T2SX_API int t2sx_read_kv(t2sx_session* s, int32_t slot, int32_t layer, int32_t which, uint16_t* out);
 /* Seen-token mask used by the repetition penalty (t2s_session_get_seen_mask, t2s.h:487): set
  * one slot's mask (uint8 [vocab], nonzero = seen).  The device marks every sampled token. */
