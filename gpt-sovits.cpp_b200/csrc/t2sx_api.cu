@@ -733,6 +733,18 @@ static bool pdl_small() {
     return v;
 }
 
+// Rows up to which the general layer chain is launched programmatically as well (T2SX_PDL_ROWS;
+// 0 = only the one- and two-row chain): its split-K matmuls fetch their weight slices and the
+// split attention its page numbers and earlier positions' K/V before waiting on the predecessor.
+// 32 sessions, Q4_0, 500 steps: 1.029 -> 0.889 ms per step.
+static int pdl_rows() {
+    static const int v = [] {
+        const char* e = getenv("T2SX_PDL_ROWS");
+        return e ? atoi(e) : 32;
+    }();
+    return v;
+}
+
 // The LayerNorm-prologue matmuls take Q8_0/Q4_0 QKV and FFN-up weights (Q5_0 is held as Q8_0).
 static bool ln_prologue_ok(const t2sx_model* m) {
     for (const LayerD& L : m->layers)
@@ -798,6 +810,7 @@ static bool run_layers(t2sx_session* s, Work& w, int T, bool decode, int final_q
         residual_layernorm(T, w.ln1, w.f, Z.ln2_w, Z.ln2_b, 1e-5f, w.x, final_qtype, act_of(w), s->st);
         return false;
     }
+    PdlScope pdl(T <= pdl_rows());
     for (int l = 0; l < nl; ++l) {
         const LayerD& L = m->layers[l];
         const int next_q = (l + 1 < nl) ? m->layers[l + 1].qkv.type : final_qtype;

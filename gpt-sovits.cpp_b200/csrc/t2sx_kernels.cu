@@ -1104,7 +1104,8 @@ __global__ void __launch_bounds__(32 * HPC) k_attn_decode(const uint16_t* __rest
 // order, so all four threads hold the same score and run the same online update (m, l) on their
 // own 8 dims of o.  The merge keeps the butterfly partners 16, 8, 4, 2, 1 (the first two between
 // warps, through shared memory) and the merge formula, so the row equals the one-warp kernel's.
-constexpr int kQD = 16;   // positions per lane in flight
+constexpr int kQD = 16;   // positions per lane in flight (fewer than 4 rows)
+constexpr int kQD32 = 8;  // 4-32 rows: 32 KB rings, so that all (row, head) CTAs are resident at once
 
 __device__ __forceinline__ void st_update8(float& m, float& l, float (&o)[8], float s, const float (&v)[8]) {
     if (s > m) {
@@ -1140,12 +1141,13 @@ __device__ __forceinline__ void unpack8(const uint4& u, float (&out)[8]) {
     }
 }
 
+template <int QD>
 __global__ void __launch_bounds__(128) k_attn_decode_split(const uint16_t* __restrict__ q16, Rows rows, KVView kv, int layer,
                                                           float scale, float* __restrict__ out, int qtype, ActQ qo) {
     extern __shared__ __align__(16) uint8_t dsm[];
     // [slot][K | V][thread] 16-byte chunks, then the merge exchange (10 floats per thread), the
     // output head, and the row's page numbers
-    float* s_x = reinterpret_cast<float*>(dsm + kQD * 2 * 128 * 16);
+    float* s_x = reinterpret_cast<float*>(dsm + QD * 2 * 128 * 16);
     float* s_val = s_x + 10 * 128;
     int32_t* s_pt = reinterpret_cast<int32_t*>(s_val + 32);
     const int r = blockIdx.x / kHeads, h = blockIdx.x % kHeads;
@@ -1174,7 +1176,7 @@ __global__ void __launch_bounds__(128) k_attn_decode_split(const uint16_t* __res
     auto issue = [&](int k) {
         if (k < nk && !(early && new_last && k == nk - 1)) {
             const uint16_t* kp = kvb + (size_t)s_pt[k >> 1] * kPageElems + (k & 1) * (kAttnLanes * kHeadDim);
-            uint8_t* dst = dsm + (size_t)(k % kQD) * 2 * 128 * 16 + tid * 16;
+            uint8_t* dst = dsm + (size_t)(k % QD) * 2 * 128 * 16 + tid * 16;
             cp_async16(dst, kp, true);
             cp_async16(dst + 128 * 16, kp + kHalfPageElems, true);
         }
@@ -1183,26 +1185,26 @@ __global__ void __launch_bounds__(128) k_attn_decode_split(const uint16_t* __res
     // positions in pairs: the two scores are independent chains (computed side by side), the two
     // updates run in position order; each pair refills the two slots the previous pair read
 #pragma unroll
-    for (int k = 0; k < kQD - 2; ++k) issue(k);
+    for (int k = 0; k < QD - 2; ++k) issue(k);
     early = false;
     pdl_wait();
     pdl_trigger();
     float q[8];
     unpack8(*reinterpret_cast<const uint4*>(q16 + (size_t)r * kD + h * kHeadDim + 8 * j), q);
-    if (new_last && nk - 1 < kQD - 2) {   // its slot was committed empty above: read it now
+    if (new_last && nk - 1 < QD - 2) {   // its slot was committed empty above: read it now
         const int k = nk - 1;
         const uint16_t* kp = kvb + (size_t)s_pt[k >> 1] * kPageElems + (k & 1) * (kAttnLanes * kHeadDim);
-        uint8_t* dst = dsm + (size_t)(k % kQD) * 2 * 128 * 16 + tid * 16;
+        uint8_t* dst = dsm + (size_t)(k % QD) * 2 * 128 * 16 + tid * 16;
         *reinterpret_cast<uint4*>(dst) = __ldcg(reinterpret_cast<const uint4*>(kp));
         *reinterpret_cast<uint4*>(dst + 128 * 16) = __ldcg(reinterpret_cast<const uint4*>(kp + kHalfPageElems));
     }
     for (int k = 0; k < nk; k += 2) {
         asm volatile("" ::: "memory");   // the previous pair's reads of those slots stay before the refill
-        issue(k + kQD - 2);
-        issue(k + kQD - 1);
-        cp_wait<kQD - 2>();
-        const uint8_t* src0 = dsm + (size_t)(k % kQD) * 2 * 128 * 16 + tid * 16;
-        const uint8_t* src1 = dsm + (size_t)((k + 1) % kQD) * 2 * 128 * 16 + tid * 16;
+        issue(k + QD - 2);
+        issue(k + QD - 1);
+        cp_wait<QD - 2>();
+        const uint8_t* src0 = dsm + (size_t)(k % QD) * 2 * 128 * 16 + tid * 16;
+        const uint8_t* src1 = dsm + (size_t)((k + 1) % QD) * 2 * 128 * 16 + tid * 16;
         float k0[8], k1[8];
         unpack8(*reinterpret_cast<const uint4*>(src0), k0);
         unpack8(*reinterpret_cast<const uint4*>(src1), k1);
@@ -1379,6 +1381,16 @@ static bool attn_split() {
     return v;
 }
 
+// 4-32 rows (not Q4_K, whose Q8_K output spans eight heads): the four-threads-per-lane kernel as
+// well (T2SX_ATTN_SPLIT32=0: two heads per CTA, one warp per head).
+static bool attn_split32() {
+    static const bool v = [] {
+        const char* e = getenv("T2SX_ATTN_SPLIT32");
+        return !(e && e[0] == '0');
+    }();
+    return v;
+}
+
 void attention_decode(int T, const uint16_t* q16, Rows rows, KVView kv, int layer, float scale, float* out, int qtype,
                       ActQ qo, cudaStream_t st) {
     if (T <= 0) return;
@@ -1398,11 +1410,20 @@ void attention_decode(int T, const uint16_t* q16, Rows rows, KVView kv, int laye
         // K/V fetch relies on)
         static PerDeviceOnce setup;
         setup.ensure([](int, int*) {
-            return cudaFuncSetAttribute(k_attn_decode_split, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) ==
+            return cudaFuncSetAttribute(k_attn_decode_split<kQD>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) ==
                    cudaSuccess;
         });
         const size_t smem = (size_t)kQD * 2 * 128 * 16 + (10 * 128 + 32) * 4 + (size_t)kv.max_pages * 4;
-        launch_k(k_attn_decode_split, dim3(T * kHeads), dim3(128), smem, st, q16, rows, kv, layer, scale, out, qtype, qo);
+        launch_k(k_attn_decode_split<kQD>, dim3(T * kHeads), dim3(128), smem, st, q16, rows, kv, layer, scale, out, qtype, qo);
+    } else if (T >= pipe1_rows() && T <= kAttnLanes && attn_split32()) {
+        // 4-32 rows: the same kernel with 8 positions per lane in flight
+        static PerDeviceOnce setup;
+        setup.ensure([](int, int*) {
+            return cudaFuncSetAttribute(k_attn_decode_split<kQD32>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) ==
+                   cudaSuccess;
+        });
+        const size_t smem = (size_t)kQD32 * 2 * 128 * 16 + (10 * 128 + 32) * 4 + (size_t)kv.max_pages * 4;
+        launch_k(k_attn_decode_split<kQD32>, dim3(T * kHeads), dim3(128), smem, st, q16, rows, kv, layer, scale, out, qtype, qo);
     } else if (T < pipe1_rows()) {
         // very few rows: one head per CTA, 16 positions per lane in flight
         launch_k((k_attn_decode<1, true>), dim3(T * kHeads), dim3(32), attn_pipe_smem<1>(kv), st, q16, rows, kv, layer, scale, out, qtype, qo);

@@ -345,8 +345,258 @@ static bool narrow16() {
     return v;
 }
 
+// ---------------------------------------------------------------------------------------------
+// Split-K tiles for few activation rows (8-32): a CTA computes 16 weight rows x 16 activation rows.
+// Its NW warps each take a contiguous range of K blocks (a multiple of 4, so a Q4_K range is a
+// whole half or whole super-block), stage that range for all 32 rows with cp.async into their own
+// slice of shared memory -- every byte of the tile in flight at once, no CTA-wide barrier before
+// the MMAs -- and store the exact per-block integer dots (one mma.sync.m16n8k32 per block and
+// 8-row half).  After one barrier each thread folds its output over all blocks of K in increasing
+// order, the canonical fold of the kernels above:
+//   Q8_0 / Q4_0: acc = fma(dw_b * dx_b, (float)isum_b, acc)
+//   Q4_K:        per super-block sa = sum_j sc_j isum_j, sm = sum_j mn_j bsum_j (integers), then
+//                acc = fma(dx * d, (float)sa, acc), accm = fma(-dx * dmin, (float)sm, accm)
+// The weight slices are requested before griddepcontrol.wait (they are constants), the
+// activations after it.
+// ---------------------------------------------------------------------------------------------
+namespace sk {
+constexpr int BN = 16, BM = 16;   // weight rows, activation rows per CTA
+constexpr int OUT = BN * BM;      // outputs per CTA = ints per block in the dot array
+
+struct Layout {
+    int nb, nsb, wrow, xrow, srow;   // blocks, super-blocks; row strides (bytes, bytes, floats)
+    int off_x, off_dw, off_dx, off_dd, off_scm, off_dx8, off_is, bytes;
+};
+// Shared-memory layout for a weight of type wt with K columns.  Row strides are padded so that
+// the fragment loads of the 8 rows a warp reads at once fall into distinct banks.
+__host__ __device__ inline Layout layout(int wt, int K) {
+    Layout L{};
+    L.nb = K / 32;
+    L.nsb = K / 256;
+    L.wrow = (wt == W_Q8_0 ? K : K / 2) + 16;
+    L.xrow = K + 16;
+    L.srow = L.nb + 4;
+    int o = BN * L.wrow;
+    L.off_x = o;   o += BM * L.xrow;
+    L.off_dw = o;  o += (wt == W_Q4_K ? 0 : BN * L.srow * 4);
+    L.off_dx = o;  o += BM * L.srow * 4;                           // Q4_K: the int sub-block sums
+    L.off_dd = o;  o += (wt == W_Q4_K ? BN * (2 * L.nsb + 1) * 4 : 0);   // d, dmin [n][sb][2] (+1 pad)
+    o = (o + 15) & ~15;
+    L.off_scm = o; o += (wt == W_Q4_K ? BN * (L.nsb + 1) * 16 : 0);      // [n][sb][16]: scales, mins (+16 B pad)
+    L.off_dx8 = o; o += (wt == W_Q4_K ? BM * (L.nsb + 1) * 4 : 0);       // Q8_K row scale [m][sb] (+1 pad)
+    o = (o + 15) & ~15;
+    L.off_is = o;  o += L.nb * OUT * 4;
+    L.bytes = o;
+    return L;
+}
+}  // namespace sk
+
+template <int WT, int NW>
+__global__ void __launch_bounds__(32 * NW) k_mm_sk(DevW W, ActQ A, int M, const float* __restrict__ bias, int relu,
+                                                   float* __restrict__ y, QKVStore qkv, int use_qkv) {
+    constexpr int NT = 32 * NW;
+    constexpr int BW = (WT == W_Q8_0) ? 32 : 16;   // weight bytes per 32-element block
+    extern __shared__ __align__(16) uint8_t smem[];
+    const int N = W.N, K = W.K;
+    const sk::Layout L = sk::layout(WT, K);
+    const int nb = L.nb, nsb = L.nsb;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    const int n0 = blockIdx.x * sk::BN, m0 = blockIdx.y * sk::BM;
+    const int chunk = nb / NW, b0 = warp * chunk;   // this warp's blocks [b0, b0 + chunk)
+    uint8_t* sW = smem;
+    uint8_t* sX = smem + L.off_x;
+    float* sDw = reinterpret_cast<float*>(smem + L.off_dw);
+    float* sDx = reinterpret_cast<float*>(smem + L.off_dx);
+    int* sBs = reinterpret_cast<int*>(smem + L.off_dx);
+    float* sDd = reinterpret_cast<float*>(smem + L.off_dd);
+    uint8_t* sScm = smem + L.off_scm;
+    float* sDx8 = reinterpret_cast<float*>(smem + L.off_dx8);
+    int* sIs = reinterpret_cast<int*>(smem + L.off_is);
+
+    // ---- weight slices of this warp's blocks (constants: before the wait) ----
+    {
+        const int cpr = chunk * BW / 16;   // 16-byte pieces per row
+        const uint8_t* wsrc = (WT == W_Q8_0) ? reinterpret_cast<const uint8_t*>(W.q8) : W.q4;
+        const int wrow_g = (WT == W_Q8_0) ? K : K / 2;
+        for (int i = lane; i < sk::BN * cpr; i += 32) {
+            const int r = i / cpr, c = i % cpr, n = n0 + r;
+            const bool ok = n < N;
+            cp_async16(sW + r * L.wrow + b0 * BW + c * 16, ok ? (const void*)(wsrc + (size_t)n * wrow_g + b0 * BW + c * 16) : (const void*)wsrc, ok);
+        }
+        if (WT != W_Q4_K) {
+            const int spr = chunk / 4;
+            for (int i = lane; i < sk::BN * spr; i += 32) {
+                const int r = i / spr, c = i % spr, n = n0 + r;
+                const bool ok = n < N;
+                cp_async16(sDw + r * L.srow + b0 + c * 4, ok ? (const void*)(W.d + (size_t)n * nb + b0 + c * 4) : (const void*)W.d, ok);
+            }
+        } else {   // scales of the super-blocks whose first block is in this warp's range
+            for (int sb = (b0 + 7) >> 3; sb * 8 < b0 + chunk; ++sb)
+                for (int r = lane; r < sk::BN; r += 32) {
+                    const int n = n0 + r;
+                    const bool ok = n < N;
+                    cp_async16(sScm + (r * (nsb + 1) + sb) * 16, ok ? (const void*)(W.scm + ((size_t)n * nsb + sb) * 16) : (const void*)W.scm, ok);
+                    cp_async4(sDd + r * (2 * nsb + 1) + 2 * sb, ok ? (const void*)(W.d + (size_t)n * nsb + sb) : (const void*)W.d, ok);
+                    cp_async4(sDd + r * (2 * nsb + 1) + 2 * sb + 1, ok ? (const void*)(W.dmin + (size_t)n * nsb + sb) : (const void*)W.dmin, ok);
+                }
+        }
+    }
+    pdl_wait();
+    pdl_trigger();
+    // ---- activation slices ----
+    {
+        const int cpr = chunk * 2;   // 32 int8 per block
+        for (int i = lane; i < sk::BM * cpr; i += 32) {
+            const int r = i / cpr, c = i % cpr, m = m0 + r;
+            const bool ok = m < M;
+            cp_async16(sX + r * L.xrow + b0 * 32 + c * 16, ok ? (const void*)(A.q + (size_t)m * K + b0 * 32 + c * 16) : (const void*)A.q, ok);
+        }
+        const int spr = chunk / 4;
+        for (int i = lane; i < sk::BM * spr; i += 32) {
+            const int r = i / spr, c = i % spr, m = m0 + r;
+            const bool ok = m < M;
+            if (WT == W_Q4_K)
+                cp_async16(sBs + r * L.srow + b0 + c * 4, ok ? (const void*)(A.bs + (size_t)m * nb + b0 + c * 4) : (const void*)A.bs, ok);
+            else
+                cp_async16(sDx + r * L.srow + b0 + c * 4, ok ? (const void*)(A.d + (size_t)m * nb + b0 + c * 4) : (const void*)A.d, ok);
+        }
+        if (WT == W_Q4_K) {
+            for (int sb = (b0 + 7) >> 3; sb * 8 < b0 + chunk; ++sb)
+                for (int r = lane; r < sk::BM; r += 32) {
+                    const int m = m0 + r;
+                    const bool ok = m < M;
+                    cp_async4(sDx8 + r * (nsb + 1) + sb, ok ? (const void*)(A.d + (size_t)m * nsb + sb) : (const void*)A.d, ok);
+                }
+        }
+    }
+    cp_commit();
+    cp_wait<0>();
+    __syncwarp();
+
+    // ---- exact block dots of this warp's range ----
+    for (int b = b0; b < b0 + chunk; ++b) {
+        int af[4];
+        const uint8_t* wr0 = sW + g * L.wrow;
+        const uint8_t* wr1 = sW + (g + 8) * L.wrow;
+        if (WT == W_Q8_0) {
+            af[0] = lds32(wr0 + b * 32 + t * 4);
+            af[1] = lds32(wr1 + b * 32 + t * 4);
+            af[2] = lds32(wr0 + b * 32 + 16 + t * 4);
+            af[3] = lds32(wr1 + b * 32 + 16 + t * 4);
+        } else if (WT == W_Q4_0) {
+            const int w0 = lds32(wr0 + b * 16 + t * 4);
+            const int w1 = lds32(wr1 + b * 16 + t * 4);
+            af[0] = __vsub4(w0 & 0x0F0F0F0F, 0x08080808);
+            af[1] = __vsub4(w1 & 0x0F0F0F0F, 0x08080808);
+            af[2] = __vsub4((w0 >> 4) & 0x0F0F0F0F, 0x08080808);
+            af[3] = __vsub4((w1 >> 4) & 0x0F0F0F0F, 0x08080808);
+        } else {
+            // sub-block js of super-block sb: 32-byte chunk js >> 1 of the super-block's 128 bytes,
+            // low nibbles for even js, high for odd
+            const int sb = b >> 3, js = b & 7;
+            const int off = sb * 128 + (js >> 1) * 32, sh = (js & 1) * 4;
+            af[0] = (lds32(wr0 + off + t * 4) >> sh) & 0x0F0F0F0F;
+            af[1] = (lds32(wr1 + off + t * 4) >> sh) & 0x0F0F0F0F;
+            af[2] = (lds32(wr0 + off + 16 + t * 4) >> sh) & 0x0F0F0F0F;
+            af[3] = (lds32(wr1 + off + 16 + t * 4) >> sh) & 0x0F0F0F0F;
+        }
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+            const uint8_t* xr = sX + (j * 8 + g) * L.xrow + b * 32;
+            int is[4];
+            mma_s8(is, af[0], af[1], af[2], af[3], lds32(xr + t * 4), lds32(xr + 16 + t * 4));
+#pragma unroll
+            for (int e = 0; e < 4; ++e) sIs[b * sk::OUT + (j * 4 + e) * 32 + lane] = is[e];
+        }
+    }
+    __syncthreads();
+
+    // ---- ordered fold, one output per thread (two with 4 warps) ----
+    for (int o = tid; o < sk::OUT; o += NT) {
+        const int je = o >> 5, l = o & 31;
+        const int j = je >> 2, e = je & 3;
+        const int nl = (l >> 2) + ((e >> 1) << 3), ml = j * 8 + 2 * (l & 3) + (e & 1);
+        const int n = n0 + nl, m = m0 + ml;
+        float v;
+        if (WT == W_Q4_K) {
+            float acc = 0.0f, accm = 0.0f;
+            const int4* scm = reinterpret_cast<const int4*>(sScm) + nl * (nsb + 1);
+            const int* bs = sBs + ml * L.srow;
+            for (int sb = 0; sb < nsb; ++sb) {
+                const int4 sc4 = scm[sb];   // bytes 0-7: the sub-block scales, 8-15: the mins
+                const uint32_t sw[4] = {(uint32_t)sc4.x, (uint32_t)sc4.y, (uint32_t)sc4.z, (uint32_t)sc4.w};
+                int sa = 0, sm = 0;
+#pragma unroll
+                for (int js = 0; js < 8; ++js) {
+                    sa += (int)((sw[js >> 2] >> (8 * (js & 3))) & 0xFFu) * sIs[(sb * 8 + js) * sk::OUT + o];
+                    sm += (int)((sw[2 + (js >> 2)] >> (8 * (js & 3))) & 0xFFu) * bs[sb * 8 + js];
+                }
+                const float xv = sDx8[ml * (nsb + 1) + sb];
+                const float wv = sDd[nl * (2 * nsb + 1) + 2 * sb], mv = sDd[nl * (2 * nsb + 1) + 2 * sb + 1];
+                acc = __fmaf_rn(__fmul_rn(xv, wv), (float)sa, acc);
+                accm = __fmaf_rn(__fmul_rn(-xv, mv), (float)sm, accm);
+            }
+            v = __fadd_rn(acc, accm);
+        } else {
+            float acc = 0.0f;
+            const float* dw = sDw + nl * L.srow;
+            const float* dx = sDx + ml * L.srow;
+#pragma unroll 8
+            for (int b = 0; b < nb; ++b) acc = __fmaf_rn(__fmul_rn(dw[b], dx[b]), i2f_small(sIs[b * sk::OUT + o]), acc);
+            v = acc;
+        }
+        if (n < N && m < M) {
+            if (bias) v = __fadd_rn(v, bias[n]);
+            if (relu) v = (v > 0.0f) ? v : 0.0f;
+            if (use_qkv) qkv_store_m(qkv, m, n, v);
+            else y[(size_t)m * N + n] = v;
+        }
+    }
+}
+
+// Split-K tiles for 8-32 rows (T2SX_SPLITK=0: the narrow ring kernel below instead).
+static bool splitk_on() {
+    static const bool v = [] {
+        const char* e = getenv("T2SX_SPLITK");
+        return !(e && e[0] == '0');
+    }();
+    return v;
+}
+
+template <int WT, int NW>
+static void launch_sk(const DevW& W, const ActQ& a, int M, const float* bias, int relu, float* y, const QKVStore* qkv,
+                      cudaStream_t st, int smem) {
+    static PerDeviceOnce setup;   // the shared-memory limit for the largest K (2048), once per device
+    if (!setup.ensure([](int, int*) {
+            return cudaFuncSetAttribute(k_mm_sk<WT, NW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        sk::layout(WT, 2048).bytes) == cudaSuccess;
+        }))
+        return;   // the launch below is skipped and the caller's launch check reports the failure
+    const dim3 grid((W.N + sk::BN - 1) / sk::BN, (M + sk::BM - 1) / sk::BM);
+    QKVStore q{};
+    if (qkv) q = *qkv;
+    launch_k((k_mm_sk<WT, NW>), grid, dim3(32 * NW), (size_t)smem, st, W, a, M, bias, relu, y, q, qkv ? 1 : 0);
+}
+
+static bool matmul_sk(const DevW& W, const ActQ& a, int M, const float* bias, int relu, float* y, const QKVStore* qkv,
+                      cudaStream_t st) {
+    const int nb = W.K / 32;
+    if (W.K % 128 || W.K > 2048 || M > 32) return false;
+    const int nw = (nb % 32 == 0) ? 8 : (nb % 16 == 0 ? 4 : 0);   // chunk = nb / nw, a multiple of 4
+    if (!nw) return false;
+    const int smem = sk::layout(W.type, W.K).bytes;
+    switch (W.type) {
+        case W_Q8_0: nw == 8 ? launch_sk<W_Q8_0, 8>(W, a, M, bias, relu, y, qkv, st, smem) : launch_sk<W_Q8_0, 4>(W, a, M, bias, relu, y, qkv, st, smem); return true;
+        case W_Q4_0: nw == 8 ? launch_sk<W_Q4_0, 8>(W, a, M, bias, relu, y, qkv, st, smem) : launch_sk<W_Q4_0, 4>(W, a, M, bias, relu, y, qkv, st, smem); return true;
+        case W_Q4_K: nw == 8 ? launch_sk<W_Q4_K, 8>(W, a, M, bias, relu, y, qkv, st, smem) : launch_sk<W_Q4_K, 4>(W, a, M, bias, relu, y, qkv, st, smem); return true;
+    }
+    return false;
+}
+
 bool matmul_mma_narrow(const DevW& W, const ActQ& a, int M, const float* bias, int relu, float* y, const QKVStore* qkv,
                        cudaStream_t st) {
+    if (splitk_on() && matmul_sk(W, a, M, bias, relu, y, qkv, st)) return true;
     if (W.K % (32 * KB) || M > 32) return false;
     switch (W.type) {
         case W_Q8_0: narrow16() ? launch_mma<W_Q8_0, 1, 1, 6, 1>(W, a, M, bias, relu, y, qkv, st) : launch_mma<W_Q8_0, 1, 1, 6>(W, a, M, bias, relu, y, qkv, st); return true;
