@@ -564,19 +564,21 @@ static bool splitk_on() {
     return v;
 }
 
+// false: nothing launched (the shared-memory limit could not be set); the caller falls back
 template <int WT, int NW>
-static void launch_sk(const DevW& W, const ActQ& a, int M, const float* bias, int relu, float* y, const QKVStore* qkv,
+static bool launch_sk(const DevW& W, const ActQ& a, int M, const float* bias, int relu, float* y, const QKVStore* qkv,
                       cudaStream_t st, int smem) {
-    static PerDeviceOnce setup;   // the shared-memory limit for the largest K (2048), once per device
+    static PerDeviceOnce setup;   // the shared-memory limit for the largest K (2048: 140 KB), once per device
     if (!setup.ensure([](int, int*) {
             return cudaFuncSetAttribute(k_mm_sk<WT, NW>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         sk::layout(WT, 2048).bytes) == cudaSuccess;
         }))
-        return;   // the launch below is skipped and the caller's launch check reports the failure
+        return false;
     const dim3 grid((W.N + sk::BN - 1) / sk::BN, (M + sk::BM - 1) / sk::BM);
     QKVStore q{};
     if (qkv) q = *qkv;
     launch_k((k_mm_sk<WT, NW>), grid, dim3(32 * NW), (size_t)smem, st, W, a, M, bias, relu, y, q, qkv ? 1 : 0);
+    return true;
 }
 
 static bool matmul_sk(const DevW& W, const ActQ& a, int M, const float* bias, int relu, float* y, const QKVStore* qkv,
@@ -587,9 +589,9 @@ static bool matmul_sk(const DevW& W, const ActQ& a, int M, const float* bias, in
     if (!nw) return false;
     const int smem = sk::layout(W.type, W.K).bytes;
     switch (W.type) {
-        case W_Q8_0: nw == 8 ? launch_sk<W_Q8_0, 8>(W, a, M, bias, relu, y, qkv, st, smem) : launch_sk<W_Q8_0, 4>(W, a, M, bias, relu, y, qkv, st, smem); return true;
-        case W_Q4_0: nw == 8 ? launch_sk<W_Q4_0, 8>(W, a, M, bias, relu, y, qkv, st, smem) : launch_sk<W_Q4_0, 4>(W, a, M, bias, relu, y, qkv, st, smem); return true;
-        case W_Q4_K: nw == 8 ? launch_sk<W_Q4_K, 8>(W, a, M, bias, relu, y, qkv, st, smem) : launch_sk<W_Q4_K, 4>(W, a, M, bias, relu, y, qkv, st, smem); return true;
+        case W_Q8_0: return nw == 8 ? launch_sk<W_Q8_0, 8>(W, a, M, bias, relu, y, qkv, st, smem) : launch_sk<W_Q8_0, 4>(W, a, M, bias, relu, y, qkv, st, smem);
+        case W_Q4_0: return nw == 8 ? launch_sk<W_Q4_0, 8>(W, a, M, bias, relu, y, qkv, st, smem) : launch_sk<W_Q4_0, 4>(W, a, M, bias, relu, y, qkv, st, smem);
+        case W_Q4_K: return nw == 8 ? launch_sk<W_Q4_K, 8>(W, a, M, bias, relu, y, qkv, st, smem) : launch_sk<W_Q4_K, 4>(W, a, M, bias, relu, y, qkv, st, smem);
     }
     return false;
 }

@@ -129,6 +129,20 @@ def test_decode_small_model_bit_exact(t2sx_mod, orc, fmt):
     _run_pair(t2sx_mod, orc, path, lengths, steps=70)
 
 
+@pytest.mark.parametrize("n", [12, 24])
+@pytest.mark.parametrize("fmt", ["q8_0", "q5_0", "q4_0", "q4_k", "f16"])
+def test_decode_8_to_32_sessions_bit_exact(t2sx_mod, orc, fmt, n):
+    """8-32 rows per step: split-K matmul tiles (16 activation rows per tile, partly filled), the
+    four-threads-per-lane attention, programmatic launches, and for Q8_0/Q4_0 FFN weights the up
+    projection's Q8_0 epilogue feeding the down projection."""
+    _need_gpu()
+    import synth
+    path = synth.ensure_gguf(fmt, 7, n_layer=2)
+    rng = np.random.default_rng(40 + n)
+    lengths = [(int(rng.integers(8, 70)), int(rng.integers(2, 60)), 100 + i) for i in range(n)]
+    _run_pair(t2sx_mod, orc, path, lengths, steps=40)
+
+
 @pytest.mark.parametrize("n", [1, 2])
 @pytest.mark.parametrize("fmt", ["q8_0", "q5_0", "q4_0", "q4_k", "f16"])
 def test_decode_one_or_two_sessions_bit_exact(t2sx_mod, orc, fmt, n):
