@@ -24,6 +24,14 @@ bool pdl_enabled() {
     return on || t_pdl_scope;
 }
 
+bool pdl_aux() {
+    static const bool v = [] {
+        const char* e = getenv("T2SX_PDL_AUX");
+        return e && e[0] == '1';
+    }();
+    return v;
+}
+
 PdlScope::PdlScope(bool on) : prev(t_pdl_scope) { t_pdl_scope = prev || on; }
 PdlScope::~PdlScope() { t_pdl_scope = prev; }
 
@@ -1015,7 +1023,8 @@ __device__ __forceinline__ void attn_finish(AttnState& st, int r, int hg, int wa
 // ends with the same state and lane d owns output dim d.  The output row is written in the
 // out-projection's dot type (a Q8_0 block is one head, a Q8_K block the CTA's eight heads), or
 // as f32 when qtype < 0.
-template <int HPC, bool PIPE>
+// F32DOT: the score chain on converted f32 values instead of the f16 pairs (the same value).
+template <int HPC, bool PIPE, bool F32DOT = false>
 __global__ void __launch_bounds__(32 * HPC) k_attn_decode(const uint16_t* __restrict__ q16, Rows rows, KVView kv, int layer,
                                                           float scale, float* __restrict__ out, int qtype, ActQ qo) {
     pdl_wait();
@@ -1030,18 +1039,29 @@ __global__ void __launch_bounds__(32 * HPC) k_attn_decode(const uint16_t* __rest
     const int lane = threadIdx.x & 31;
     const int s = rows.slot[r];
     const int L = rows.L[r];
-    float q[kHeadDim];
-    load_row32(q16 + (size_t)r * kD + h * kHeadDim, q);
+    uint32_t q[kHeadDim / 2];   // the f16 query as packed pairs (the score's mixed-precision fma chain)
+    load_row32_h(q16 + (size_t)r * kD + h * kHeadDim, q);
     AttnState st;
     st_empty(st);
     const int32_t* pt = kv.ptab + (size_t)s * kv.max_pages;
-    if (!PIPE) {
+    if (!PIPE && F32DOT) {
+        float qf[kHeadDim];
+        load_row32(q16 + (size_t)r * kD + h * kHeadDim, qf);
         for (int i = lane; i < L; i += kAttnLanes) {
             const int page = pt[i / kPage];
             float k[kHeadDim], v[kHeadDim];
             load_row32(kv.pool + kv_off(kv, page, layer, 0, h, i % kPage), k);
             load_row32(kv.pool + kv_off(kv, page, layer, 1, h, i % kPage), v);
-            st_update(st, __fmul_rn(dot32(q, k), scale), v);
+            st_update(st, __fmul_rn(dot32(qf, k), scale), v);
+        }
+    } else if (!PIPE) {
+        for (int i = lane; i < L; i += kAttnLanes) {
+            const int page = pt[i / kPage];
+            uint32_t k[kHeadDim / 2];
+            float v[kHeadDim];
+            load_row32_h(kv.pool + kv_off(kv, page, layer, 0, h, i % kPage), k);
+            load_row32(kv.pool + kv_off(kv, page, layer, 1, h, i % kPage), v);
+            st_update(st, __fmul_rn(dot32_h(q, k), scale), v);
         }
     }
     if (PIPE) {
@@ -1086,10 +1106,11 @@ __global__ void __launch_bounds__(32 * HPC) k_attn_decode(const uint16_t* __rest
                 kr[c] = *reinterpret_cast<const uint4*>(src + c * NT * 16);
                 vr[c] = *reinterpret_cast<const uint4*>(src + (4 + c) * NT * 16);
             }
-            float k32[kHeadDim], v32[kHeadDim];
-            unpack_row32(kr, k32);
+            uint32_t kw[kHeadDim / 2];
+            float v32[kHeadDim];
+            words16(kr, kw);
             unpack_row32(vr, v32);
-            st_update(st, __fmul_rn(dot32(q, k32), scale), v32);
+            st_update(st, __fmul_rn(dot32_h(q, kw), scale), v32);
         }
         cp_wait<0>();
     }
@@ -1170,11 +1191,12 @@ __global__ void __launch_bounds__(128) k_attn_decode_split(const uint16_t* __res
     const unsigned gmask = 0xFu << (4 * a);                  // the four threads of the lane
     // position vl + 32k lies in page k / 2 at vl + 32 (k & 1)
     const uint16_t* kvb = kv_head_base(kv, layer, h) + vl * kHeadDim + 8 * j;
-    // this lane's last position is among the ones being appended (at most one per lane: T < 32)
-    const bool new_last = nk > 0 && vl + kAttnLanes * (nk - 1) >= L - T;
+    // this lane's positions from step k_new on are among the last T, which the preceding QKV
+    // projection may be appending (with T <= 32 at most the lane's last position)
+    const int k_new = (L - T - vl <= 0) ? 0 : (L - T - vl + kAttnLanes - 1) / kAttnLanes;
     bool early = true;   // issuing before pdl_wait
     auto issue = [&](int k) {
-        if (k < nk && !(early && new_last && k == nk - 1)) {
+        if (k < nk && !(early && k >= k_new)) {
             const uint16_t* kp = kvb + (size_t)s_pt[k >> 1] * kPageElems + (k & 1) * (kAttnLanes * kHeadDim);
             uint8_t* dst = dsm + (size_t)(k % QD) * 2 * 128 * 16 + tid * 16;
             cp_async16(dst, kp, true);
@@ -1189,10 +1211,8 @@ __global__ void __launch_bounds__(128) k_attn_decode_split(const uint16_t* __res
     early = false;
     pdl_wait();
     pdl_trigger();
-    float q[8];
-    unpack8(*reinterpret_cast<const uint4*>(q16 + (size_t)r * kD + h * kHeadDim + 8 * j), q);
-    if (new_last && nk - 1 < QD - 2) {   // its slot was committed empty above: read it now
-        const int k = nk - 1;
+    const uint4 q4 = *reinterpret_cast<const uint4*>(q16 + (size_t)r * kD + h * kHeadDim + 8 * j);   // f16 pairs
+    for (int k = k_new; k < nk && k < QD - 2; ++k) {   // slots committed empty above: read them now
         const uint16_t* kp = kvb + (size_t)s_pt[k >> 1] * kPageElems + (k & 1) * (kAttnLanes * kHeadDim);
         uint8_t* dst = dsm + (size_t)(k % QD) * 2 * 128 * 16 + tid * 16;
         *reinterpret_cast<uint4*>(dst) = __ldcg(reinterpret_cast<const uint4*>(kp));
@@ -1205,15 +1225,14 @@ __global__ void __launch_bounds__(128) k_attn_decode_split(const uint16_t* __res
         cp_wait<QD - 2>();
         const uint8_t* src0 = dsm + (size_t)(k % QD) * 2 * 128 * 16 + tid * 16;
         const uint8_t* src1 = dsm + (size_t)((k + 1) % QD) * 2 * 128 * 16 + tid * 16;
-        float k0[8], k1[8];
-        unpack8(*reinterpret_cast<const uint4*>(src0), k0);
-        unpack8(*reinterpret_cast<const uint4*>(src1), k1);
+        // the 8-term chain j of each score on the f16 pairs (mixed-precision fma)
+        const uint4 k0 = *reinterpret_cast<const uint4*>(src0);
+        const uint4 k1 = *reinterpret_cast<const uint4*>(src1);
         float c0 = 0.0f, c1 = 0.0f;
-#pragma unroll
-        for (int d = 0; d < 8; ++d) {
-            c0 = __fmaf_rn(q[d], k0[d], c0);
-            c1 = __fmaf_rn(q[d], k1[d], c1);
-        }
+        c0 = fma_h2(q4.x, k0.x, c0); c1 = fma_h2(q4.x, k1.x, c1);
+        c0 = fma_h2(q4.y, k0.y, c0); c1 = fma_h2(q4.y, k1.y, c1);
+        c0 = fma_h2(q4.z, k0.z, c0); c1 = fma_h2(q4.z, k1.z, c1);
+        c0 = fma_h2(q4.w, k0.w, c0); c1 = fma_h2(q4.w, k1.w, c1);
         const float a0 = __fadd_rn(c0, __shfl_xor_sync(gmask, c0, 1));
         const float a1 = __fadd_rn(c1, __shfl_xor_sync(gmask, c1, 1));
         const float dot0 = __fadd_rn(a0, __shfl_xor_sync(gmask, a0, 2));
@@ -1292,8 +1311,8 @@ __global__ void __launch_bounds__(512, 1) k_attn_group(const int2* __restrict__ 
     __syncthreads();
     const int Lmax = s_lmax;
     const int32_t* pt = kv.ptab + (size_t)rows.slot[gr.x] * kv.max_pages;
-    float q[kHeadDim];
-    if (active) load_row32(q16 + (size_t)r * kD + h * kHeadDim, q);
+    uint32_t q[kHeadDim / 2] = {};   // the f16 query as packed pairs
+    if (active) load_row32_h(q16 + (size_t)r * kD + h * kHeadDim, q);
     AttnState st;
     st_empty(st);
     const int npg = (Lmax + kPage - 1) / kPage;
@@ -1323,10 +1342,11 @@ __global__ void __launch_bounds__(512, 1) k_attn_group(const int2* __restrict__ 
                     kr[c] = *reinterpret_cast<const uint4*>(&sm[buf][0][p * 64 + ((c ^ sw) << 4)]);
                     vr[c] = *reinterpret_cast<const uint4*>(&sm[buf][1][p * 64 + ((c ^ sw) << 4)]);
                 }
-                float k32[kHeadDim], v32[kHeadDim];
-                unpack_row32(kr, k32);
+                uint32_t kw[kHeadDim / 2];
+                float v32[kHeadDim];
+                words16(kr, kw);
                 unpack_row32(vr, v32);
-                st_update(st, __fmul_rn(dot32(q, k32), scale), v32);
+                st_update(st, __fmul_rn(dot32_h(q, kw), scale), v32);
             }
         }
         __syncthreads();   // this buffer is refilled in the next step
@@ -1381,6 +1401,16 @@ static bool attn_split() {
     return v;
 }
 
+// Rows up to which the many-row attention runs the score chain on converted f32 values rather than
+// on the f16 pairs (T2SX_ATTN_F32DOT_ROWS).  The f16-pair chain needs 96 instead of 114 registers,
+// so five CTAs fit an SM instead of four: at 512 and 2048 rows that is faster (72.6 vs 79.2 us,
+// 249.7 vs 261.6 us per launch), at 256 rows (6.9 CTAs per SM, two rounds either way) slower
+// (48.6 vs 44.1 us).
+static int attn_f32dot_rows() {
+    static const int v = [] { const char* e = getenv("T2SX_ATTN_F32DOT_ROWS"); return e ? atoi(e) : 384; }();
+    return v;
+}
+
 // 4-32 rows (not Q4_K, whose Q8_K output spans eight heads): the four-threads-per-lane kernel as
 // well (T2SX_ATTN_SPLIT32=0: two heads per CTA, one warp per head).
 static bool attn_split32() {
@@ -1402,7 +1432,11 @@ void attention_decode(int T, const uint16_t* q16, Rows rows, KVView kv, int laye
         // many rows: four heads per CTA with an f32 row, then the Q8_K conversion as its own pass
         // (eight-head CTAs that convert in place wait on two CTA barriers per row: 8.65 -> 8.39 ms
         // for the 2048-row decode step)
-        launch_k((k_attn_decode<4, false>), dim3(T * (kHeads / 4)), dim3(128), 0, st, q16, rows, kv, layer, scale, out, -1, qo);
+        if (T <= attn_f32dot_rows())
+            launch_k((k_attn_decode<4, false, true>), dim3(T * (kHeads / 4)), dim3(128), 0, st, q16, rows, kv, layer, scale, out, -1, qo);
+        else
+            launch_k((k_attn_decode<4, false>), dim3(T * (kHeads / 4)), dim3(128), 0, st, q16, rows, kv, layer, scale, out, -1, qo);
+        PdlScope pdl(pdl_aux());
         quantize_act(W_Q4_K, out, T, kD, qo, st);
     } else if (T < pipe1_rows() && T <= kAttnLanes && attn_split()) {
         // very few rows: one head per CTA, four threads per position lane (at most 32 rows: the
@@ -1429,6 +1463,8 @@ void attention_decode(int T, const uint16_t* q16, Rows rows, KVView kv, int laye
         launch_k((k_attn_decode<1, true>), dim3(T * kHeads), dim3(32), attn_pipe_smem<1>(kv), st, q16, rows, kv, layer, scale, out, qtype, qo);
     } else if (T < 64) {
         launch_k((k_attn_decode<2, true>), dim3(T * (kHeads / 2)), dim3(64), attn_pipe_smem<2>(kv), st, q16, rows, kv, layer, scale, out, qtype, qo);
+    } else if (T <= attn_f32dot_rows()) {
+        launch_k((k_attn_decode<4, false, true>), dim3(T * (kHeads / 4)), dim3(128), 0, st, q16, rows, kv, layer, scale, out, qtype, qo);
     } else {
         launch_k((k_attn_decode<4, false>), dim3(T * (kHeads / 4)), dim3(128), 0, st, q16, rows, kv, layer, scale, out, qtype, qo);
     }

@@ -47,6 +47,21 @@ __device__ __forceinline__ void unpack_row32(const uint4 (&u4)[4], float* out) {
     }
 }
 
+// four 16-byte chunks -> 16 words of packed f16 pairs, in order
+__device__ __forceinline__ void words16(const uint4 (&u4)[4], uint32_t (&w)[16]) {
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+        w[4 * c] = u4[c].x; w[4 * c + 1] = u4[c].y; w[4 * c + 2] = u4[c].z; w[4 * c + 3] = u4[c].w;
+    }
+}
+
+// 32 consecutive f16 values at p (16-byte aligned) as 16 packed pairs
+__device__ __forceinline__ void load_row32_h(const uint16_t* p, uint32_t (&w)[16]) {
+    const uint4* p4 = reinterpret_cast<const uint4*>(p);
+    const uint4 u[4] = {p4[0], p4[1], p4[2], p4[3]};
+    words16(u, w);
+}
+
 // 32 consecutive f16 values at p (16-byte aligned) -> f32
 __device__ __forceinline__ void load_row32(const uint16_t* p, float* out) {
     const uint4* p4 = reinterpret_cast<const uint4*>(p);

@@ -93,6 +93,32 @@ __device__ __forceinline__ float dot32(const float* q, const float* k) {
     return __fadd_rn(__fadd_rn(c[0], c[1]), __fadd_rn(c[2], c[3]));
 }
 
+// Two steps of an fma chain on packed f16 pairs: c = fma(a.lo, b.lo, c), then c = fma(a.hi, b.hi, c)
+// (element 2i in the low half of word i).  sm_100's mixed-precision fma takes the f16 operands as
+// they are (their conversion to f32 is exact) and rounds once, so each step is the same value as
+// __fmaf_rn(h2f(a), h2f(b), c), without the two conversions.
+__device__ __forceinline__ float fma_h2(uint32_t a2, uint32_t b2, float c) {
+    asm("{\n.reg .f16 al, ah, bl, bh;\nmov.b32 {al, ah}, %1;\nmov.b32 {bl, bh}, %2;\n"
+        "fma.rn.f32.f16 %0, al, bl, %0;\nfma.rn.f32.f16 %0, ah, bh, %0;\n}\n"
+        : "+f"(c)
+        : "r"(a2), "r"(b2));
+    return c;
+}
+
+// dot32 of a query and a key row held as 16 packed f16 pairs each: the same four sequential
+// 8-term chains, summed pairwise.
+__device__ __forceinline__ float dot32_h(const uint32_t (&q)[16], const uint32_t (&k)[16]) {
+    float c[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        float s = 0.0f;
+#pragma unroll
+        for (int w = 4 * j; w < 4 * j + 4; ++w) s = fma_h2(q[w], k[w], s);
+        c[j] = s;
+    }
+    return __fadd_rn(__fadd_rn(c[0], c[1]), __fadd_rn(c[2], c[3]));
+}
+
 }  // namespace t2sx
 
 namespace t2sx {
