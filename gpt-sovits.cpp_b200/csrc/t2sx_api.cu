@@ -840,20 +840,12 @@ static bool run_layers(t2sx_session* s, Work& w, int T, bool decode, int final_q
             e3.quant_in = true;   // the FFN rows' conversion (Q8_0: inside the down projection)
             matmul(L.down, act_for(w, w.h), T, L.down_b, 0, w.f, s->st, e3);
         } else {
-            const bool aux = pdl_aux();
             matmul(L.out, act_for(w, w.attn), T, L.out_b, 0, w.o, s->st);
-            {
-                PdlScope p1(aux);
-                residual_layernorm(T, w.x, w.o, L.ln1_w, L.ln1_b, 1e-5f, w.ln1, L.up.type, act_of(w), s->st);
-            }
+            residual_layernorm(T, w.x, w.o, L.ln1_w, L.ln1_b, 1e-5f, w.ln1, L.up.type, act_of(w), s->st);
             matmul(L.up, act_for(w, w.ln1), T, L.up_b, 1, w.h, s->st);
             ActQ a = act_of(w);
-            {
-                PdlScope p2(aux);
-                quantize_act(L.down.type, w.h, T, s->ff, a, s->st);
-            }
+            quantize_act(L.down.type, w.h, T, s->ff, a, s->st);
             matmul(L.down, act_for(w, w.h), T, L.down_b, 0, w.f, s->st);
-            PdlScope p3(aux);
             residual_layernorm(T, w.ln1, w.f, L.ln2_w, L.ln2_b, 1e-5f, w.x, next_q, act_of(w), s->st);
         }
     }

@@ -24,14 +24,6 @@ bool pdl_enabled() {
     return on || t_pdl_scope;
 }
 
-bool pdl_aux() {
-    static const bool v = [] {
-        const char* e = getenv("T2SX_PDL_AUX");
-        return e && e[0] == '1';
-    }();
-    return v;
-}
-
 PdlScope::PdlScope(bool on) : prev(t_pdl_scope) { t_pdl_scope = prev || on; }
 PdlScope::~PdlScope() { t_pdl_scope = prev; }
 
@@ -1436,7 +1428,6 @@ void attention_decode(int T, const uint16_t* q16, Rows rows, KVView kv, int laye
             launch_k((k_attn_decode<4, false, true>), dim3(T * (kHeads / 4)), dim3(128), 0, st, q16, rows, kv, layer, scale, out, -1, qo);
         else
             launch_k((k_attn_decode<4, false>), dim3(T * (kHeads / 4)), dim3(128), 0, st, q16, rows, kv, layer, scale, out, -1, qo);
-        PdlScope pdl(pdl_aux());
         quantize_act(W_Q4_K, out, T, kD, qo, st);
     } else if (T < pipe1_rows() && T <= kAttnLanes && attn_split()) {
         // very few rows: one head per CTA, four threads per position lane (at most 32 rows: the

@@ -13,9 +13,6 @@ namespace t2sx {
 // while its predecessor runs and waits for it before touching data it produced (see pdl_wait in
 // t2sx_math.cuh for what may be read before the wait).
 bool pdl_enabled();
-// T2SX_PDL_AUX=1: the short kernels between the many-row chain's matmuls and attention (residual +
-// LayerNorm, activation conversion) are launched programmatically (measurement switch).
-bool pdl_aux();
 // Launches made on this host thread while a PdlScope(true) lives carry the attribute as well.
 struct PdlScope {
     explicit PdlScope(bool on);
