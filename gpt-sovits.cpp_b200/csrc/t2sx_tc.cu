@@ -17,7 +17,8 @@
 //
 // Persistent CTAs (one per SM) walk 128-row x 64-row output tiles; 12 warps in 3 warpgroups:
 //   warp 0     : TMA producer (cp.async.bulk.tensor, 128-byte swizzle), 3-stage ring of half
-//                super-blocks (3 weight planes x 128 rows x 128 B + 64 activation rows x 128 B);
+//                super-blocks (3 weight planes x 128 rows x 128 B + 64 activation rows x 128 B); the
+//                first three stages' weight planes are requested before the programmatic wait;
 //   warps 1-3  : one thread each issues one weight plane's MMAs (4 per stage) and its tcgen05.commit
 //                arrivals (the barriers count the three issuers);
 //   warps 4-11 : fold -- warp w owns TMEM lanes 32*(w%4).. (weight rows) and 32 of the 64 columns,
@@ -250,6 +251,10 @@ k_mm_tc_q4k(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUt
     const int tiles_n = (N + BM - 1) / BM, tiles_m = (M + BN - 1) / BN;
     const int n_tiles = tiles_n * tiles_m;
 
+    // The first tile's first stages: their weight planes are constants, so the producer thread
+    // requests them here, before the programmatic wait; their activation tiles follow the wait.
+    const int pre = (blockIdx.x < n_tiles) ? (2 * nsb < NS ? 2 * nsb : NS) : 0;
+    const int n0_first = (blockIdx.x % tiles_n) * BM, m0_first = (blockIdx.x / tiles_n) * BN;
     if (tid == 0) {
         for (int i = 0; i < NS; ++i) { bar_init(full0 + 8 * i, 1); bar_init(empty0 + 8 * i, PLANES); }
         for (int i = 0; i < NBUF; ++i) { bar_init(tfull0 + 8 * i, PLANES); bar_init(tempty0 + 8 * i, EPI_WARPS); }
@@ -257,6 +262,13 @@ k_mm_tc_q4k(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUt
         bar_init(stall_bar, 1);   // no thread ever arrives on it
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+        for (int s = 0; s < pre; ++s) {
+            const uint32_t fb = full0 + 8 * s;
+            bar_expect_tx(fb, STAGE);   // the whole stage: these planes and, after the wait, the activations
+            const uint32_t st = smem_u32(smem + s * STAGE);
+#pragma unroll
+            for (int p = 0; p < PLANES; ++p) tma_load_2d(st + p * A_PLANE, &tmW, s * 128, p * W.tc_npad + n0_first, fb);
+        }
     }
     if (warp == 0) {
         __syncwarp();
@@ -290,10 +302,15 @@ k_mm_tc_q4k(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUt
         if (warp == 0) {
             // ---------------- TMA producer: stages of 128 K-elements, 2 per super-block ----------------
             if (lane == 0) {
+                // the activation tiles of the stages whose planes went out before the wait (always
+                // issued, so that those stages complete and the abort drain below ends)
+                for (int s = 0; s < pre; ++s)
+                    tma_load_2d(smem_u32(smem + s * STAGE) + PLANES * A_PLANE, &tmX, s * 128, m0_first, full0 + 8 * s);
                 int stg = 0;
                 for (int t = blockIdx.x; t < n_tiles && !aborted; t += gridDim.x) {
                     const int n0 = (t % tiles_n) * BM, m0 = (t / tiles_n) * BN;
                     for (int h = 0; h < 2 * nsb; ++h, ++stg) {
+                        if (stg < pre) continue;   // issued above
                         const int ss = stg % NS;
                         if (!bar_wait(empty0 + 8 * ss, ((stg / NS) & 1) ^ 1, abort_flag, spin)) { aborted = true; break; }
                         const uint32_t fb = full0 + 8 * ss;
