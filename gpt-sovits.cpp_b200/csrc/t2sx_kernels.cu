@@ -1015,8 +1015,9 @@ __device__ __forceinline__ void attn_finish(AttnState& st, int r, int hg, int wa
 // ends with the same state and lane d owns output dim d.  The output row is written in the
 // out-projection's dot type (a Q8_0 block is one head, a Q8_K block the CTA's eight heads), or
 // as f32 when qtype < 0.
-// F32DOT: the score chain on converted f32 values instead of the f16 pairs (the same value).
-template <int HPC, bool PIPE, bool F32DOT = false>
+// PF: each lane's next position's K/V rows are loaded while the current one is folded (a two-deep
+// register pipeline over the lane's positions, K and V held as packed f16 pairs).
+template <int HPC, bool PIPE, bool PF = false>
 __global__ void __launch_bounds__(32 * HPC) k_attn_decode(const uint16_t* __restrict__ q16, Rows rows, KVView kv, int layer,
                                                           float scale, float* __restrict__ out, int qtype, ActQ qo) {
     pdl_wait();
@@ -1036,15 +1037,20 @@ __global__ void __launch_bounds__(32 * HPC) k_attn_decode(const uint16_t* __rest
     AttnState st;
     st_empty(st);
     const int32_t* pt = kv.ptab + (size_t)s * kv.max_pages;
-    if (!PIPE && F32DOT) {
-        float qf[kHeadDim];
-        load_row32(q16 + (size_t)r * kD + h * kHeadDim, qf);
-        for (int i = lane; i < L; i += kAttnLanes) {
+    if (!PIPE && PF) {
+        uint32_t kc[kHeadDim / 2], vc[kHeadDim / 2];
+        auto load_pos = [&](int i, uint32_t (&kw)[kHeadDim / 2], uint32_t (&vw)[kHeadDim / 2]) {
             const int page = pt[i / kPage];
-            float k[kHeadDim], v[kHeadDim];
-            load_row32(kv.pool + kv_off(kv, page, layer, 0, h, i % kPage), k);
-            load_row32(kv.pool + kv_off(kv, page, layer, 1, h, i % kPage), v);
-            st_update(st, __fmul_rn(dot32(qf, k), scale), v);
+            load_row32_h(kv.pool + kv_off(kv, page, layer, 0, h, i % kPage), kw);
+            load_row32_h(kv.pool + kv_off(kv, page, layer, 1, h, i % kPage), vw);
+        };
+        if (lane < L) load_pos(lane, kc, vc);
+        for (int i = lane; i < L; i += kAttnLanes) {
+            uint32_t kn[kHeadDim / 2], vn[kHeadDim / 2];
+            if (i + kAttnLanes < L) load_pos(i + kAttnLanes, kn, vn);
+            st_update_h(st, __fmul_rn(dot32_h(q, kc), scale), vc);
+#pragma unroll
+            for (int w = 0; w < kHeadDim / 2; ++w) { kc[w] = kn[w]; vc[w] = vn[w]; }
         }
     } else if (!PIPE) {
         for (int i = lane; i < L; i += kAttnLanes) {
@@ -1393,13 +1399,13 @@ static bool attn_split() {
     return v;
 }
 
-// Rows up to which the many-row attention runs the score chain on converted f32 values rather than
-// on the f16 pairs (T2SX_ATTN_F32DOT_ROWS).  The f16-pair chain needs 96 instead of 114 registers,
-// so five CTAs fit an SM instead of four: at 512 and 2048 rows that is faster (72.6 vs 79.2 us,
-// 249.7 vs 261.6 us per launch), at 256 rows (6.9 CTAs per SM, two rounds either way) slower
-// (48.6 vs 44.1 us).
-static int attn_f32dot_rows() {
-    static const int v = [] { const char* e = getenv("T2SX_ATTN_F32DOT_ROWS"); return e ? atoi(e) : 384; }();
+// Rows up to which the many-row attention keeps each lane's next position in flight
+// (T2SX_ATTN_PF_ROWS, 0 = never).  The two-deep pipeline needs 118 registers (four CTAs per SM);
+// the one-deep kernel 96 (five).  At 256 rows, 6.9 CTAs per SM, the pipeline wins (42.5 against
+// 44.1 us for the best one-deep variant, the f32 score chain at four CTAs per SM); at 512 and 2048
+// rows the fifth CTA per SM wins (72.2 against 76.1 us, 248.8 against 248.9 us).
+static int attn_pf_rows() {
+    static const int v = [] { const char* e = getenv("T2SX_ATTN_PF_ROWS"); return e ? atoi(e) : 384; }();
     return v;
 }
 
@@ -1424,7 +1430,7 @@ void attention_decode(int T, const uint16_t* q16, Rows rows, KVView kv, int laye
         // many rows: four heads per CTA with an f32 row, then the Q8_K conversion as its own pass
         // (eight-head CTAs that convert in place wait on two CTA barriers per row: 8.65 -> 8.39 ms
         // for the 2048-row decode step)
-        if (T <= attn_f32dot_rows())
+        if (T <= attn_pf_rows())
             launch_k((k_attn_decode<4, false, true>), dim3(T * (kHeads / 4)), dim3(128), 0, st, q16, rows, kv, layer, scale, out, -1, qo);
         else
             launch_k((k_attn_decode<4, false>), dim3(T * (kHeads / 4)), dim3(128), 0, st, q16, rows, kv, layer, scale, out, -1, qo);
@@ -1454,7 +1460,7 @@ void attention_decode(int T, const uint16_t* q16, Rows rows, KVView kv, int laye
         launch_k((k_attn_decode<1, true>), dim3(T * kHeads), dim3(32), attn_pipe_smem<1>(kv), st, q16, rows, kv, layer, scale, out, qtype, qo);
     } else if (T < 64) {
         launch_k((k_attn_decode<2, true>), dim3(T * (kHeads / 2)), dim3(64), attn_pipe_smem<2>(kv), st, q16, rows, kv, layer, scale, out, qtype, qo);
-    } else if (T <= attn_f32dot_rows()) {
+    } else if (T <= attn_pf_rows()) {
         launch_k((k_attn_decode<4, false, true>), dim3(T * (kHeads / 4)), dim3(128), 0, st, q16, rows, kv, layer, scale, out, qtype, qo);
     } else {
         launch_k((k_attn_decode<4, false>), dim3(T * (kHeads / 4)), dim3(128), 0, st, q16, rows, kv, layer, scale, out, qtype, qo);

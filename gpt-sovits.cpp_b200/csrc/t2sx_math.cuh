@@ -69,6 +69,29 @@ __device__ __forceinline__ void st_update(AttnState& st, float s, const float* v
     }
 }
 
+// st_update with the value row as 16 packed f16 pairs, converted element by element inside the
+// update (the same values and operations as st_update on the converted row).
+__device__ __forceinline__ void st_update_h(AttnState& st, float s, const uint32_t (&vw)[kHeadDim / 2]) {
+    if (s > st.m) {
+        const float t = t2s_expf(__fsub_rn(st.m, s));
+        st.m = s;
+        st.l = __fmaf_rn(st.l, t, 1.0f);
+#pragma unroll
+        for (int w = 0; w < kHeadDim / 2; ++w) {
+            st.o[2 * w] = __fmaf_rn(st.o[2 * w], t, h2f((uint16_t)(vw[w] & 0xffffu)));
+            st.o[2 * w + 1] = __fmaf_rn(st.o[2 * w + 1], t, h2f((uint16_t)(vw[w] >> 16)));
+        }
+    } else {
+        const float t = t2s_expf(__fsub_rn(s, st.m));
+        st.l = __fadd_rn(st.l, t);
+#pragma unroll
+        for (int w = 0; w < kHeadDim / 2; ++w) {
+            st.o[2 * w] = __fmaf_rn(t, h2f((uint16_t)(vw[w] & 0xffffu)), st.o[2 * w]);
+            st.o[2 * w + 1] = __fmaf_rn(t, h2f((uint16_t)(vw[w] >> 16)), st.o[2 * w + 1]);
+        }
+    }
+}
+
 // Symmetric merge of two states: merge(A,B) == merge(B,A) bit for bit.
 __device__ __forceinline__ void st_merge_scalars(float mA, float lA, float mB, float lB, float& M, float& a,
                                                  float& b, float& l, bool& empty) {
@@ -77,20 +100,6 @@ __device__ __forceinline__ void st_merge_scalars(float mA, float lA, float mB, f
     a = empty ? 0.0f : t2s_expf(__fsub_rn(mA, M));
     b = empty ? 0.0f : t2s_expf(__fsub_rn(mB, M));
     l = empty ? 0.0f : __fadd_rn(__fmul_rn(lA, a), __fmul_rn(lB, b));
-}
-
-// 32-term dot of an f16-rounded query (as f32) with an f16 key row: four sequential fma
-// chains of 8 terms (the products of two f16 values are exact in f32), summed pairwise.
-__device__ __forceinline__ float dot32(const float* q, const float* k) {
-    float c[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        float s = 0.0f;
-#pragma unroll
-        for (int d = 8 * j; d < 8 * j + 8; ++d) s = __fmaf_rn(q[d], k[d], s);
-        c[j] = s;
-    }
-    return __fadd_rn(__fadd_rn(c[0], c[1]), __fadd_rn(c[2], c[3]));
 }
 
 // Two steps of an fma chain on packed f16 pairs: c = fma(a.lo, b.lo, c), then c = fma(a.hi, b.hi, c)
@@ -105,8 +114,9 @@ __device__ __forceinline__ float fma_h2(uint32_t a2, uint32_t b2, float c) {
     return c;
 }
 
-// dot32 of a query and a key row held as 16 packed f16 pairs each: the same four sequential
-// 8-term chains, summed pairwise.
+// 32-term dot of an f16 query with an f16 key row, both held as 16 packed f16 pairs: four
+// sequential fma chains of 8 terms (the products of two f16 values are exact in f32), summed
+// pairwise as (c0 + c1) + (c2 + c3).
 __device__ __forceinline__ float dot32_h(const uint32_t (&q)[16], const uint32_t (&k)[16]) {
     float c[4];
 #pragma unroll
