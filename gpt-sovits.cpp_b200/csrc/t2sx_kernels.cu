@@ -1409,6 +1409,14 @@ static int attn_pf_rows() {
     return v;
 }
 
+// Up to T2SX_ATTN_PF_ROWS rows with a Q4_K out-projection, eight heads per CTA (two-deep pipeline)
+// convert the row to Q8_K in place instead of a separate conversion launch (T2SX_ATTN_Q8K8=0: four
+// heads per CTA and the launch).  256 rows: step 1.924 -> 1.911 ms.
+static bool attn_q8k_inplace() {
+    static const bool v = [] { const char* e = getenv("T2SX_ATTN_Q8K8"); return !(e && e[0] == '0'); }();
+    return v;
+}
+
 // 4-32 rows (not Q4_K, whose Q8_K output spans eight heads): the four-threads-per-lane kernel as
 // well (T2SX_ATTN_SPLIT32=0: two heads per CTA, one warp per head).
 static bool attn_split32() {
@@ -1430,6 +1438,11 @@ void attention_decode(int T, const uint16_t* q16, Rows rows, KVView kv, int laye
         // many rows: four heads per CTA with an f32 row, then the Q8_K conversion as its own pass
         // (eight-head CTAs that convert in place wait on two CTA barriers per row: 8.65 -> 8.39 ms
         // for the 2048-row decode step)
+        if (T <= attn_pf_rows() && attn_q8k_inplace()) {
+            // eight heads per CTA write the row's Q8_K blocks in place (no conversion launch)
+            launch_k((k_attn_decode<8, false, true>), dim3(T * (kHeads / 8)), dim3(256), 0, st, q16, rows, kv, layer, scale, out, qtype, qo);
+            return;
+        }
         if (T <= attn_pf_rows())
             launch_k((k_attn_decode<4, false, true>), dim3(T * (kHeads / 4)), dim3(128), 0, st, q16, rows, kv, layer, scale, out, -1, qo);
         else
