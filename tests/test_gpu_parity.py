@@ -470,6 +470,20 @@ def test_decode_many_sessions_q4_k_bit_exact(t2sx_mod, orc):
     _run_pair(t2sx_mod, orc, path, lengths, steps=8)
 
 
+@pytest.mark.parametrize("n", [40, 100, 400])
+@pytest.mark.parametrize("fmt", ["q8_0", "q4_0", "q4_k"])
+def test_decode_between_paths_bit_exact(t2sx_mod, orc, fmt, n):
+    """33-63 rows (two-head attention CTAs with cp.async rings, mma.sync matmuls for Q8_0/Q4_0),
+    64-384 rows (the attention with each lane's next position in flight; Q4_K: eight-head CTAs
+    writing the Q8_K row in place) and above 384 rows (five one-deep CTAs per SM)."""
+    _need_gpu()
+    import synth
+    path = synth.ensure_gguf(fmt, 7, n_layer=2)
+    rng = np.random.default_rng(60 + n)
+    lengths = [(int(rng.integers(5, 40)), int(rng.integers(3, 30)), 700 + i) for i in range(n)]
+    _run_pair(t2sx_mod, orc, path, lengths, steps=6, check_kv=False)
+
+
 @pytest.mark.parametrize("fmt", ["q8_0", "f32"])
 def test_extract_latent_bit_exact(t2sx_mod, orc, fmt):
     """Prompt codes from HuBERT frames (Conv1d k=2 s=2 + nearest codebook entry), GPU against the
