@@ -835,6 +835,14 @@ static int fp_tile_min_rows() {
     return v;
 }
 
+static bool f16_sk_on() {
+    static const bool v = [] {
+        const char* e = getenv("T2SX_F16_SK");
+        return !(e && e[0] == '0');
+    }();
+    return v;
+}
+
 void matmul(const DevW& W, const ActQ& a_in, int M, const float* bias, int relu, float* y, cudaStream_t st, const Epi& e) {
     const bool quant = W.type == W_Q8_0 || W.type == W_Q4_0 || W.type == W_Q4_K;
     ActQ a = a_in;
@@ -846,6 +854,10 @@ void matmul(const DevW& W, const ActQ& a_in, int M, const float* bias, int relu,
     if (quant && M >= tc_min_rows() && matmul_tc(W, a, M, bias, relu, y, e.qkv, st)) return;
     if (quant && M > kSmallM && matmul_mma(W, a, M, bias, relu, y, e.qkv, st)) return;
     if (quant && M >= narrow_min_rows() && !(e.tail && M <= kSmallM) && matmul_mma_narrow(W, a, M, bias, relu, y, e.qkv, st))
+        return;
+    // F16 weights at 8-256 rows: split-K tiles (T2SX_F16_SK=0: the tiled kernel / per-row kernel)
+    if (W.type == W_F16 && M >= narrow_min_rows() && M <= 256 && !(e.tail && M <= kSmallM) && f16_sk_on() &&
+        matmul_f16_sk(W, a, M, bias, relu, y, e.qkv, st))
         return;
     QKVStore qkv{};
     if (e.qkv) qkv = *e.qkv;

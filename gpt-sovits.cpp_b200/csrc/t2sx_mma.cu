@@ -555,6 +555,105 @@ __global__ void __launch_bounds__(32 * NW) k_mm_sk(DevW W, ActQ A, int M, const 
     }
 }
 
+// ---------------------------------------------------------------------------------------------
+// F16 weights (f16 activations), 8-256 rows: split-K tiles of 16 weight rows x 16 activation rows.
+// The canonical F16 arithmetic -- per 32-element block an fma chain from 0 over the elements in
+// order, the block sums added in order from 0 -- lets the blocks' chains run in parallel: each of
+// the 8 warps stages its contiguous range of blocks for the 32 rows (weights before the
+// programmatic wait, activations after it), runs the 32-term chains of its blocks on the packed f16
+// pairs with the mixed-precision fma (the f16 operands convert exactly; one rounding per step, as
+// the f32 chain on converted operands), and stores the block sums; after one barrier each thread
+// adds its output's block sums in order.  A lane owns 4 weight rows x 2 activation rows.
+// ---------------------------------------------------------------------------------------------
+namespace fsk {
+constexpr int BN = 16, BM = 16, NW = 8;
+__host__ __device__ inline int row_h(int K) { return K + 8; }   // staged row: halves (16-byte pad)
+__host__ __device__ inline int smem_bytes(int K) { return 32 * row_h(K) * 2 + (K / 32) * BN * BM * 4; }
+}  // namespace fsk
+
+__global__ void __launch_bounds__(32 * fsk::NW) k_mm_f16_sk(DevW W, ActQ A, int M, const float* __restrict__ bias, int relu,
+                                                            float* __restrict__ y, QKVStore qkv, int use_qkv) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    const int N = W.N, K = W.K, nb = K / 32, rh = fsk::row_h(K);
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int n0 = blockIdx.x * fsk::BN, m0 = blockIdx.y * fsk::BM;
+    const int chunk = nb / fsk::NW, b0 = warp * chunk;   // this warp's blocks [b0, b0 + chunk)
+    uint16_t* sW = reinterpret_cast<uint16_t*>(smem);
+    uint16_t* sX = sW + fsk::BN * rh;
+    float* sS = reinterpret_cast<float*>(smem + 32 * rh * 2);   // [nb][BN * BM] block sums
+    const int cpr = chunk * 4;   // 16-byte pieces (8 halves) per row of the range
+    for (int i = lane; i < fsk::BN * cpr; i += 32) {
+        const int r = i / cpr, c = i % cpr, n = n0 + r;
+        const bool ok = n < N;
+        cp_async16(sW + r * rh + b0 * 32 + c * 8, ok ? (const void*)(W.h + (size_t)n * K + b0 * 32 + c * 8) : (const void*)W.h, ok);
+    }
+    pdl_wait();
+    pdl_trigger();
+    for (int i = lane; i < fsk::BM * cpr; i += 32) {
+        const int r = i / cpr, c = i % cpr, m = m0 + r;
+        const bool ok = m < M;
+        cp_async16(sX + r * rh + b0 * 32 + c * 8, ok ? (const void*)(A.h + (size_t)m * K + b0 * 32 + c * 8) : (const void*)A.h, ok);
+    }
+    cp_commit();
+    cp_wait<0>();
+    __syncwarp();
+    const int nq = (lane & 3) * 4, mq = (lane >> 2) * 2;
+    for (int b = b0; b < b0 + chunk; ++b) {
+        uint4 xv[2][4];
+#pragma unroll
+        for (int j = 0; j < 2; ++j)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) xv[j][c] = *reinterpret_cast<const uint4*>(sX + (mq + j) * rh + b * 32 + c * 8);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            uint4 wv[4];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) wv[c] = *reinterpret_cast<const uint4*>(sW + (nq + i) * rh + b * 32 + c * 8);
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                float sblk = 0.0f;
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    sblk = fma_h2(wv[c].x, xv[j][c].x, sblk);
+                    sblk = fma_h2(wv[c].y, xv[j][c].y, sblk);
+                    sblk = fma_h2(wv[c].z, xv[j][c].z, sblk);
+                    sblk = fma_h2(wv[c].w, xv[j][c].w, sblk);
+                }
+                sS[b * (fsk::BN * fsk::BM) + (nq + i) * fsk::BM + mq + j] = sblk;
+            }
+        }
+    }
+    __syncthreads();
+    const int nl = tid / fsk::BM, ml = tid % fsk::BM, n = n0 + nl, m = m0 + ml;
+    float acc = 0.0f;
+#pragma unroll 8
+    for (int b = 0; b < nb; ++b) acc = __fadd_rn(acc, sS[b * (fsk::BN * fsk::BM) + tid]);
+    if (n < N && m < M) {
+        float v = bias ? __fadd_rn(acc, bias[n]) : acc;
+        if (relu) v = (v > 0.0f) ? v : 0.0f;
+        if (use_qkv) qkv_store_m(qkv, m, n, v);
+        else y[(size_t)m * N + n] = v;
+    }
+}
+
+bool matmul_f16_sk(const DevW& W, const ActQ& a, int M, const float* bias, int relu, float* y, const QKVStore* qkv,
+                   cudaStream_t st) {
+    if (W.type != W_F16 || M < 1 || M > 256 || W.K % 256 || W.K > 2048 || !a.h ||
+        (((uintptr_t)a.h | (uintptr_t)W.h) & 15))
+        return false;
+    static PerDeviceOnce setup;   // the shared-memory limit for K = 2048, once per device
+    if (!setup.ensure([](int, int*) {
+            return cudaFuncSetAttribute(k_mm_f16_sk, cudaFuncAttributeMaxDynamicSharedMemorySize, fsk::smem_bytes(2048)) ==
+                   cudaSuccess;
+        }))
+        return false;
+    const dim3 grid((W.N + fsk::BN - 1) / fsk::BN, (M + fsk::BM - 1) / fsk::BM);
+    QKVStore q{};
+    if (qkv) q = *qkv;
+    launch_k(k_mm_f16_sk, grid, dim3(32 * fsk::NW), (size_t)fsk::smem_bytes(W.K), st, W, a, M, bias, relu, y, q, qkv ? 1 : 0);
+    return true;
+}
+
 // Split-K tiles for 8-32 rows (T2SX_SPLITK=0: the narrow ring kernel below instead).
 static bool splitk_on() {
     static const bool v = [] {

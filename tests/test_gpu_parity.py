@@ -132,9 +132,9 @@ def test_decode_small_model_bit_exact(t2sx_mod, orc, fmt):
 @pytest.mark.parametrize("n", [12, 24])
 @pytest.mark.parametrize("fmt", ["q8_0", "q5_0", "q4_0", "q4_k", "f16"])
 def test_decode_8_to_32_sessions_bit_exact(t2sx_mod, orc, fmt, n):
-    """8-32 rows per step: split-K matmul tiles (16 activation rows per tile, partly filled), the
-    four-threads-per-lane attention, programmatic launches, and for Q8_0/Q4_0 FFN weights the up
-    projection's Q8_0 epilogue feeding the down projection."""
+    """8-32 rows per step: split-K matmul tiles (16 activation rows per tile, partly filled; the
+    int8 tiles for the quantised formats, the f16-pair tiles for F16), the four-threads-per-lane
+    attention and programmatic launches."""
     _need_gpu()
     import synth
     path = synth.ensure_gguf(fmt, 7, n_layer=2)
@@ -471,11 +471,12 @@ def test_decode_many_sessions_q4_k_bit_exact(t2sx_mod, orc):
 
 
 @pytest.mark.parametrize("n", [40, 100, 400])
-@pytest.mark.parametrize("fmt", ["q8_0", "q4_0", "q4_k"])
+@pytest.mark.parametrize("fmt", ["q8_0", "q4_0", "q4_k", "f16"])
 def test_decode_between_paths_bit_exact(t2sx_mod, orc, fmt, n):
     """33-63 rows (two-head attention CTAs with cp.async rings, mma.sync matmuls for Q8_0/Q4_0),
     64-384 rows (the attention with each lane's next position in flight; Q4_K: eight-head CTAs
-    writing the Q8_K row in place) and above 384 rows (five one-deep CTAs per SM)."""
+    writing the Q8_K row in place) and above 384 rows (five one-deep CTAs per SM); F16 weights:
+    split-K tiles up to 256 rows, the tiled kernel above."""
     _need_gpu()
     import synth
     path = synth.ensure_gguf(fmt, 7, n_layer=2)
