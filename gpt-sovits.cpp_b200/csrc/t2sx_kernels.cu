@@ -852,6 +852,7 @@ void matmul(const DevW& W, const ActQ& a_in, int M, const float* bias, int relu,
                     (M < narrow_min_rows() || e.tail) && M < tc_min_rows() && (((uintptr_t)a.f) & 15) == 0;
     if (e.quant_in && !fq) quantize_act(W.type, a.f, M, W.K, a, st);
     if (quant && M >= tc_min_rows() && matmul_tc(W, a, M, bias, relu, y, e.qkv, st)) return;
+    if (quant && M > kSmallM && matmul_sk_mid(W, a, M, bias, relu, y, e.qkv, st)) return;
     if (quant && M > kSmallM && matmul_mma(W, a, M, bias, relu, y, e.qkv, st)) return;
     if (quant && M >= narrow_min_rows() && !(e.tail && M <= kSmallM) && matmul_mma_narrow(W, a, M, bias, relu, y, e.qkv, st))
         return;

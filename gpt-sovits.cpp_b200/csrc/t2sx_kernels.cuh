@@ -211,6 +211,9 @@ int tc_min_rows();
 // mma.sync path with 32-weight-row tiles for M <= 32 (enough CTAs when there are few rows).
 bool matmul_mma_narrow(const DevW& W, const ActQ& a, int M, const float* bias, int relu, float* y, const QKVStore* qkv,
                        cudaStream_t st);
+// Quantised weights, 33 to T2SX_SK_MAX_ROWS rows: split-K tiles; false: nothing launched.
+bool matmul_sk_mid(const DevW& W, const ActQ& a, int M, const float* bias, int relu, float* y, const QKVStore* qkv,
+                   cudaStream_t st);
 // F16 weights, 1-256 rows, K a multiple of 256 up to 2048: split-K tiles; false: nothing launched.
 bool matmul_f16_sk(const DevW& W, const ActQ& a, int M, const float* bias, int relu, float* y, const QKVStore* qkv,
                    cudaStream_t st);

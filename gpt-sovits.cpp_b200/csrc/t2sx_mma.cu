@@ -683,7 +683,7 @@ static bool launch_sk(const DevW& W, const ActQ& a, int M, const float* bias, in
 static bool matmul_sk(const DevW& W, const ActQ& a, int M, const float* bias, int relu, float* y, const QKVStore* qkv,
                       cudaStream_t st) {
     const int nb = W.K / 32;
-    if (W.K % 128 || W.K > 2048 || M > 32) return false;
+    if (W.K % 128 || W.K > 2048 || M > 256) return false;
     const int nw = (nb % 32 == 0) ? 8 : (nb % 16 == 0 ? 4 : 0);   // chunk = nb / nw, a multiple of 4
     if (!nw) return false;
     const int smem = sk::layout(W.type, W.K).bytes;
@@ -695,9 +695,29 @@ static bool matmul_sk(const DevW& W, const ActQ& a, int M, const float* bias, in
     return false;
 }
 
+// Rows up to which the split-K tiles also take Q8_0/Q4_0 (and Q4_K below the tcgen05 threshold)
+// matmuls above 32 rows instead of the mma.sync ring kernel: 64 rows, 160 for K = 2048, or
+// T2SX_SK_MAX_ROWS for every K (at most 256).  Isolated calls: K = 2048 at 40-64 rows 22.6 ->
+// 12.3 us, at 130 rows 22.6 -> 16.4 us; K = 512 at 40-64 rows 12.3 -> 10.3 us; at 256 rows the
+// ring kernel's 128-row weight tiles are as fast or faster.
+static int sk_env_rows() {
+    static const int v = [] {
+        const char* e = getenv("T2SX_SK_MAX_ROWS");
+        const int r = e ? atoi(e) : 0;
+        return r <= 0 ? 0 : (r < 32 ? 32 : (r > 256 ? 256 : r));
+    }();
+    return v;
+}
+
+bool matmul_sk_mid(const DevW& W, const ActQ& a, int M, const float* bias, int relu, float* y, const QKVStore* qkv,
+                   cudaStream_t st) {
+    const int lim = sk_env_rows() ? sk_env_rows() : (W.K >= 2048 ? 160 : 64);
+    return M > 32 && M <= lim && splitk_on() && matmul_sk(W, a, M, bias, relu, y, qkv, st);
+}
+
 bool matmul_mma_narrow(const DevW& W, const ActQ& a, int M, const float* bias, int relu, float* y, const QKVStore* qkv,
                        cudaStream_t st) {
-    if (splitk_on() && matmul_sk(W, a, M, bias, relu, y, qkv, st)) return true;
+    if (M <= 32 && splitk_on() && matmul_sk(W, a, M, bias, relu, y, qkv, st)) return true;
     if (W.K % (32 * KB) || M > 32) return false;
     switch (W.type) {
         case W_Q8_0: narrow16() ? launch_mma<W_Q8_0, 1, 1, 6, 1>(W, a, M, bias, relu, y, qkv, st) : launch_mma<W_Q8_0, 1, 1, 6>(W, a, M, bias, relu, y, qkv, st); return true;
