@@ -93,10 +93,25 @@ def _should_quantize(name, arr, block):
     return name not in EMBEDDING_NAMES and arr.ndim == 2 and arr.shape[1] % block == 0
 
 
+def tensor_values(seed: int, n_layer: int = 24, d=512, ff=2048, vocab=1025, phone_vocab=732):
+    """(name, f32 array in PyTorch layout) in converter order, before any conversion: LayerNorm
+    gamma and the position alphas 1, LayerNorm beta 0, every other tensor N(0, 0.02) drawn from
+    numpy.random.default_rng(seed) in this order."""
+    rng = np.random.default_rng(seed)
+    for name, shape in tensor_specs(d, ff, n_layer, vocab, phone_vocab):
+        base = name.split(".")[-1]
+        if base in ("ln1_w", "ln2_w") or name.endswith("pos_alpha"):
+            arr = np.ones(shape, dtype=np.float32)
+        elif base in ("ln1_b", "ln2_b"):
+            arr = np.zeros(shape, dtype=np.float32)
+        else:
+            arr = (rng.standard_normal(size=shape, dtype=np.float32) * np.float32(0.02)).astype(np.float32)
+        yield name, arr
+
+
 def write_gguf(path: str, wtype: int, seed: int, n_layer: int = 24, d=512, ff=2048, n_head=16,
                vocab=1025, phone_vocab=732, eos=1024) -> str:
     import gguf
-    rng = np.random.default_rng(seed)
     # one temporary name per process: several ranks may generate the same file at once; the
     # final rename is atomic and any of the identical results may win
     tmp = f"{path}.tmp.{os.getpid()}"
@@ -108,14 +123,7 @@ def write_gguf(path: str, wtype: int, seed: int, n_layer: int = 24, d=512, ff=20
         writer.add_uint32(k, v)
     qt = gguf.GGMLQuantizationType
     is_quant = wtype in BLOCK
-    for name, shape in tensor_specs(d, ff, n_layer, vocab, phone_vocab):
-        base = name.split(".")[-1]
-        if base in ("ln1_w", "ln2_w") or name.endswith("pos_alpha"):
-            arr = np.ones(shape, dtype=np.float32)
-        elif base in ("ln1_b", "ln2_b"):
-            arr = np.zeros(shape, dtype=np.float32)
-        else:
-            arr = (rng.standard_normal(size=shape, dtype=np.float32) * np.float32(0.02)).astype(np.float32)
+    for name, arr in tensor_values(seed, n_layer, d, ff, vocab, phone_vocab):
         if is_quant and _should_quantize(name, arr, BLOCK[wtype]):
             if wtype == GGML_Q4_K:
                 writer.add_tensor(name, quantize_q4_k(arr), raw_dtype=qt.Q4_K)
