@@ -1138,6 +1138,7 @@ __global__ void __launch_bounds__(32 * HPC) k_attn_decode(const uint16_t* __rest
 // warps, through shared memory) and the merge formula, so the row equals the one-warp kernel's.
 constexpr int kQD = 16;   // positions per lane in flight (fewer than 4 rows)
 constexpr int kQD32 = 8;  // 4-32 rows: 32 KB rings, so that all (row, head) CTAs are resident at once
+                          // (32-session steps of one build: 8 deep 1.157 ms, 10 deep 1.154, 12 deep 1.165, 16 deep 1.289)
 
 __device__ __forceinline__ void st_update8(float& m, float& l, float (&o)[8], float s, const float (&v)[8]) {
     if (s > m) {
@@ -1440,6 +1441,19 @@ static bool attn_split32() {
     return v;
 }
 
+// The four-threads-per-lane kernel with QD positions per lane in flight (QD x 4 KB of rings).
+template <int QD>
+static void launch_split(int T, const uint16_t* q16, Rows rows, KVView kv, int layer, float scale, float* out,
+                         int qtype, ActQ qo, cudaStream_t st) {
+    static PerDeviceOnce setup;
+    setup.ensure([](int, int*) {
+        return cudaFuncSetAttribute(k_attn_decode_split<QD>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) ==
+               cudaSuccess;
+    });
+    const size_t smem = (size_t)QD * 2 * 128 * 16 + (10 * 128 + 32) * 4 + (size_t)kv.max_pages * 4;
+    launch_k(k_attn_decode_split<QD>, dim3(T * kHeads), dim3(128), smem, st, q16, rows, kv, layer, scale, out, qtype, qo);
+}
+
 void attention_decode(int T, const uint16_t* q16, Rows rows, KVView kv, int layer, float scale, float* out, int qtype,
                       ActQ qo, cudaStream_t st) {
     if (T <= 0) return;
@@ -1465,22 +1479,10 @@ void attention_decode(int T, const uint16_t* q16, Rows rows, KVView kv, int laye
         // very few rows: one head per CTA, four threads per position lane (at most 32 rows: the
         // positions of a pass are then at most one per position lane, which the kernel's early
         // K/V fetch relies on)
-        static PerDeviceOnce setup;
-        setup.ensure([](int, int*) {
-            return cudaFuncSetAttribute(k_attn_decode_split<kQD>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) ==
-                   cudaSuccess;
-        });
-        const size_t smem = (size_t)kQD * 2 * 128 * 16 + (10 * 128 + 32) * 4 + (size_t)kv.max_pages * 4;
-        launch_k(k_attn_decode_split<kQD>, dim3(T * kHeads), dim3(128), smem, st, q16, rows, kv, layer, scale, out, qtype, qo);
+        launch_split<kQD>(T, q16, rows, kv, layer, scale, out, qtype, qo, st);
     } else if (T >= pipe1_rows() && T <= kAttnLanes && attn_split32()) {
         // 4-32 rows: the same kernel with 8 positions per lane in flight
-        static PerDeviceOnce setup;
-        setup.ensure([](int, int*) {
-            return cudaFuncSetAttribute(k_attn_decode_split<kQD32>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024) ==
-                   cudaSuccess;
-        });
-        const size_t smem = (size_t)kQD32 * 2 * 128 * 16 + (10 * 128 + 32) * 4 + (size_t)kv.max_pages * 4;
-        launch_k(k_attn_decode_split<kQD32>, dim3(T * kHeads), dim3(128), smem, st, q16, rows, kv, layer, scale, out, qtype, qo);
+        launch_split<kQD32>(T, q16, rows, kv, layer, scale, out, qtype, qo, st);
     } else if (T < pipe1_rows()) {
         // very few rows: one head per CTA, 16 positions per lane in flight
         launch_k((k_attn_decode<1, true>), dim3(T * kHeads), dim3(32), attn_pipe_smem<1>(kv), st, q16, rows, kv, layer, scale, out, qtype, qo);
