@@ -1140,18 +1140,29 @@ constexpr int kQD = 16;   // positions per lane in flight (fewer than 4 rows)
 constexpr int kQD32 = 8;  // 4-32 rows: 32 KB rings, so that all (row, head) CTAs are resident at once
                           // (32-session steps of one build: 8 deep 1.157 ms, 10 deep 1.154, 12 deep 1.165, 16 deep 1.289)
 
-__device__ __forceinline__ void st_update8(float& m, float& l, float (&o)[8], float s, const float (&v)[8]) {
-    if (s > m) {
-        const float t = t2s_expf(__fsub_rn(m, s));
-        m = s;
-        l = __fmaf_rn(l, t, 1.0f);
+// The online-softmax step of a position lane (8 of its dims) for positions k and k + 1 (the second
+// only if has1).  A position with score s against the running maximum m: a new maximum (s > m)
+// takes t = e^(m - s), m = s, l = fma(l, t, 1), o = fma(o, t, v); otherwise t = e^(s - m),
+// l = l + t, o = fma(t, v, o).  The running maximum does not depend on the weights, so both
+// weights e^(-|s - m|) (fsub(m, s) = -fsub(s, m) exactly) are formed side by side from the maxima,
+// and the updates use selects instead of branches that the lanes of a warp would take apart:
+// fma(v, t, o) = fma(t, v, o), and fma(1, t, l) = l + t.
+__device__ __forceinline__ void st_update8_pair(float& m, float& l, float (&o)[8], float s0, const float (&v0)[8],
+                                                float s1, const float (&v1)[8], bool has1) {
+    const bool g0 = s0 > m;
+    const float m1 = g0 ? s0 : m;
+    const bool g1 = has1 && s1 > m1;
+    const float t0 = t2s_expf(-fabsf(__fsub_rn(s0, m)));
+    const float t1 = t2s_expf(-fabsf(__fsub_rn(s1, m1)));
+    l = __fmaf_rn(g0 ? l : 1.0f, t0, g0 ? 1.0f : l);
 #pragma unroll
-        for (int d = 0; d < 8; ++d) o[d] = __fmaf_rn(o[d], t, v[d]);
-    } else {
-        const float t = t2s_expf(__fsub_rn(s, m));
-        l = __fadd_rn(l, t);
+    for (int d = 0; d < 8; ++d) o[d] = __fmaf_rn(g0 ? o[d] : v0[d], t0, g0 ? v0[d] : o[d]);
+    m = m1;
+    if (has1) {
+        l = __fmaf_rn(g1 ? l : 1.0f, t1, g1 ? 1.0f : l);
 #pragma unroll
-        for (int d = 0; d < 8; ++d) o[d] = __fmaf_rn(t, v[d], o[d]);
+        for (int d = 0; d < 8; ++d) o[d] = __fmaf_rn(g1 ? o[d] : v1[d], t1, g1 ? v1[d] : o[d]);
+        m = g1 ? s1 : m1;
     }
 }
 
@@ -1249,13 +1260,10 @@ __global__ void __launch_bounds__(128) k_attn_decode_split(const uint16_t* __res
         const float a1 = __fadd_rn(c1, __shfl_xor_sync(gmask, c1, 1));
         const float dot0 = __fadd_rn(a0, __shfl_xor_sync(gmask, a0, 2));
         const float dot1 = __fadd_rn(a1, __shfl_xor_sync(gmask, a1, 2));
-        float vf[8];
-        unpack8(*reinterpret_cast<const uint4*>(src0 + 128 * 16), vf);
-        st_update8(m, l, o, __fmul_rn(dot0, scale), vf);
-        if (k + 1 < nk) {   // (the same for the lane's four threads)
-            unpack8(*reinterpret_cast<const uint4*>(src1 + 128 * 16), vf);
-            st_update8(m, l, o, __fmul_rn(dot1, scale), vf);
-        }
+        float v0[8], v1[8];
+        unpack8(*reinterpret_cast<const uint4*>(src0 + 128 * 16), v0);
+        unpack8(*reinterpret_cast<const uint4*>(src1 + 128 * 16), v1);
+        st_update8_pair(m, l, o, __fmul_rn(dot0, scale), v0, __fmul_rn(dot1, scale), v1, k + 1 < nk);
     }
     cp_wait<0>();
     // butterfly rounds 16 and 8: partner thread tid ^ 64, then tid ^ 32

@@ -55,14 +55,15 @@ __device__ __forceinline__ void st_empty(AttnState& s) {
 
 // Fold one key position (score s, value row v as f32) into the state.
 __device__ __forceinline__ void st_update(AttnState& st, float s, const float* v) {
+    // the weight before the branch (fsub(m, s) = -fsub(s, m) exactly): lanes that take the two
+    // sides apart share the exponential
+    const float t = t2s_expf(-fabsf(__fsub_rn(s, st.m)));
     if (s > st.m) {
-        const float t = t2s_expf(__fsub_rn(st.m, s));
         st.m = s;
         st.l = __fmaf_rn(st.l, t, 1.0f);
 #pragma unroll
         for (int d = 0; d < kHeadDim; ++d) st.o[d] = __fmaf_rn(st.o[d], t, v[d]);
     } else {
-        const float t = t2s_expf(__fsub_rn(s, st.m));
         st.l = __fadd_rn(st.l, t);
 #pragma unroll
         for (int d = 0; d < kHeadDim; ++d) st.o[d] = __fmaf_rn(t, v[d], st.o[d]);
@@ -72,8 +73,8 @@ __device__ __forceinline__ void st_update(AttnState& st, float s, const float* v
 // st_update with the value row as 16 packed f16 pairs, converted element by element inside the
 // update (the same values and operations as st_update on the converted row).
 __device__ __forceinline__ void st_update_h(AttnState& st, float s, const uint32_t (&vw)[kHeadDim / 2]) {
+    const float t = t2s_expf(-fabsf(__fsub_rn(s, st.m)));
     if (s > st.m) {
-        const float t = t2s_expf(__fsub_rn(st.m, s));
         st.m = s;
         st.l = __fmaf_rn(st.l, t, 1.0f);
 #pragma unroll
@@ -82,7 +83,6 @@ __device__ __forceinline__ void st_update_h(AttnState& st, float s, const uint32
             st.o[2 * w + 1] = __fmaf_rn(st.o[2 * w + 1], t, h2f((uint16_t)(vw[w] >> 16)));
         }
     } else {
-        const float t = t2s_expf(__fsub_rn(s, st.m));
         st.l = __fadd_rn(st.l, t);
 #pragma unroll
         for (int w = 0; w < kHeadDim / 2; ++w) {
