@@ -77,4 +77,36 @@ __device__ __forceinline__ void load_row32(const uint16_t* p, float* out) {
     }
 }
 
+// QKV projection output element (row m, column n) -> Q as f16 for attention, K / V as f16 into
+// the row's cache page (ggml_set_rows into an F16 cache, block.cpp:557-573).
+__device__ __forceinline__ void qkv_store(const QKVStore& e, int m, int n, float v) {
+    const uint16_t h = f2h(v);
+    if (n < kD) { e.q16[(size_t)m * kD + n] = h; return; }
+    const int pos = e.rows.pos[m];
+    const int s = e.rows.slot[m];
+    if (pos < 0 || pos >= e.rows.cap[s]) return;
+    const int page = e.kv.ptab[(size_t)s * e.kv.max_pages + pos / kPage];
+    const int which = (n - kD) / kD, j = (n - kD) % kD;
+    e.kv.pool[kv_off(e.kv, page, e.layer, which, j / kHeadDim, pos % kPage) + (j % kHeadDim)] = h;
+}
+
+// qkv_store in two steps, for kernels that look the destination up ahead of the dot products:
+// qkv_dest gives row m's cache page and position ((-1, 0): no K/V store, as qkv_store skips a
+// position outside the slot's capacity).  Its capacity and page-table loads are independent
+// (the page-table index is clamped), so they cost one round trip after the position and slot.
+__device__ __forceinline__ int2 qkv_dest(const QKVStore& e, int pos, int s) {
+    const int pg = min(max(pos, 0) / kPage, e.kv.max_pages - 1);
+    const int cap = e.rows.cap[s];
+    const int page = e.kv.ptab[(size_t)s * e.kv.max_pages + pg];
+    return (pos < 0 || pos >= cap) ? make_int2(-1, 0) : make_int2(page, pos);
+}
+
+__device__ __forceinline__ void qkv_store_at(const QKVStore& e, int m, int n, float v, int2 dst) {
+    const uint16_t h = f2h(v);
+    if (n < kD) { e.q16[(size_t)m * kD + n] = h; return; }
+    if (dst.x < 0) return;
+    const int which = (n - kD) / kD, j = (n - kD) % kD;
+    e.kv.pool[kv_off(e.kv, dst.x, e.layer, which, j / kHeadDim, dst.y % kPage) + (j % kHeadDim)] = h;
+}
+
 }  // namespace t2sx

@@ -53,18 +53,6 @@ struct Cfg {
     static constexpr int SMEM = NSTG * STAGE;
 };
 
-// QKV projection output element -> Q as f16, K / V as f16 into the row's cache page.
-__device__ __forceinline__ void qkv_store_m(const QKVStore& e, int m, int n, float v) {
-    const uint16_t h = f2h(v);
-    if (n < kD) { e.q16[(size_t)m * kD + n] = h; return; }
-    const int pos = e.rows.pos[m];
-    const int s = e.rows.slot[m];
-    if (pos < 0 || pos >= e.rows.cap[s]) return;
-    const int page = e.kv.ptab[(size_t)s * e.kv.max_pages + pos / kPage];
-    const int which = (n - kD) / kD, j = (n - kD) % kD;
-    e.kv.pool[kv_off(e.kv, page, e.layer, which, j / kHeadDim, pos % kPage) + (j % kHeadDim)] = h;
-}
-
 template <int WT, int MT_, int WN_, int NSTG_, int IT_>
 __global__ void __launch_bounds__(64 * WN_) k_mm_mma(DevW W, ActQ A, int M, const float* __restrict__ bias, int relu,
                                                 float* __restrict__ y, QKVStore qkv, int use_qkv) {
@@ -295,7 +283,7 @@ __global__ void __launch_bounds__(64 * WN_) k_mm_mma(DevW W, ActQ A, int M, cons
                     float v = (WT == W_Q4_K) ? __fadd_rn(acc[i][j][e], accm[i][j][e]) : acc[i][j][e];
                     if (bias) v = __fadd_rn(v, bias[n]);
                     if (relu) v = (v > 0.0f) ? v : 0.0f;
-                    if (use_qkv) qkv_store_m(qkv, m, n, v);
+                    if (use_qkv) qkv_store(qkv, m, n, v);
                     else y[(size_t)m * N + n] = v;
                 }
             }
@@ -442,8 +430,35 @@ __global__ void __launch_bounds__(32 * NW) k_mm_sk(DevW W, ActQ A, int M, const 
                 }
         }
     }
+    // ---- cache destinations of this thread's K/V outputs (QKV projection): above layer 0 the rows'
+    // positions, slots and pages were written two or more launches back, so they are read before
+    // the wait; layer 0 follows the embedding that writes them, so it reads them just after ----
+    static_assert(sk::OUT % NT == 0, "whole outputs per thread");
+    constexpr int NO = sk::OUT / NT;   // outputs per thread
+    int2 dst[NO];
+    auto out_row = [&](int o) {
+        const int je = o >> 5, l = o & 31, j = je >> 2, e = je & 3;
+        return m0 + j * 8 + 2 * (l & 3) + (e & 1);
+    };
+    auto out_col = [&](int o) {
+        const int je = o >> 5, l = o & 31, e = je & 3;
+        return n0 + (l >> 2) + ((e >> 1) << 3);
+    };
+    auto dest_of = [&](int o) {
+        const int m = out_row(o);
+        return (m < M && out_col(o) >= kD) ? qkv_dest(qkv, qkv.rows.pos[m], qkv.rows.slot[m]) : make_int2(-1, 0);
+    };
+    const bool early_dst = use_qkv && qkv.layer > 0;
+    if (early_dst) {
+#pragma unroll
+        for (int i = 0; i < NO; ++i) dst[i] = dest_of(tid + i * NT);
+    }
     pdl_wait();
     pdl_trigger();
+    if (use_qkv && !early_dst) {
+#pragma unroll
+        for (int i = 0; i < NO; ++i) dst[i] = dest_of(tid + i * NT);
+    }
     // ---- activation slices ----
     {
         const int cpr = chunk * 2;   // 32 int8 per block
@@ -513,7 +528,9 @@ __global__ void __launch_bounds__(32 * NW) k_mm_sk(DevW W, ActQ A, int M, const 
     __syncthreads();
 
     // ---- ordered fold, one output per thread (two with 4 warps) ----
-    for (int o = tid; o < sk::OUT; o += NT) {
+#pragma unroll
+    for (int i = 0; i < NO; ++i) {
+        const int o = tid + i * NT;
         const int je = o >> 5, l = o & 31;
         const int j = je >> 2, e = je & 3;
         const int nl = (l >> 2) + ((e >> 1) << 3), ml = j * 8 + 2 * (l & 3) + (e & 1);
@@ -549,7 +566,7 @@ __global__ void __launch_bounds__(32 * NW) k_mm_sk(DevW W, ActQ A, int M, const 
         if (n < N && m < M) {
             if (bias) v = __fadd_rn(v, bias[n]);
             if (relu) v = (v > 0.0f) ? v : 0.0f;
-            if (use_qkv) qkv_store_m(qkv, m, n, v);
+            if (use_qkv) qkv_store_at(qkv, m, n, v, dst[i]);
             else y[(size_t)m * N + n] = v;
         }
     }
@@ -631,7 +648,7 @@ __global__ void __launch_bounds__(32 * fsk::NW) k_mm_f16_sk(DevW W, ActQ A, int 
     if (n < N && m < M) {
         float v = bias ? __fadd_rn(acc, bias[n]) : acc;
         if (relu) v = (v > 0.0f) ? v : 0.0f;
-        if (use_qkv) qkv_store_m(qkv, m, n, v);
+        if (use_qkv) qkv_store(qkv, m, n, v);
         else y[(size_t)m * N + n] = v;
     }
 }
