@@ -453,6 +453,12 @@ __global__ void __launch_bounds__(32 * NW) k_mm_sk(DevW W, ActQ A, int M, const 
 #pragma unroll
         for (int i = 0; i < NO; ++i) dst[i] = dest_of(tid + i * NT);
     }
+    float bv[NO];   // the outputs' biases (constants)
+#pragma unroll
+    for (int i = 0; i < NO; ++i) {
+        const int n = out_col(tid + i * NT);
+        bv[i] = (bias && n < N) ? bias[n] : 0.0f;
+    }
     pdl_wait();
     pdl_trigger();
     if (use_qkv && !early_dst) {
@@ -564,7 +570,7 @@ __global__ void __launch_bounds__(32 * NW) k_mm_sk(DevW W, ActQ A, int M, const 
             v = acc;
         }
         if (n < N && m < M) {
-            if (bias) v = __fadd_rn(v, bias[n]);
+            if (bias) v = __fadd_rn(v, bv[i]);
             if (relu) v = (v > 0.0f) ? v : 0.0f;
             if (use_qkv) qkv_store_at(qkv, m, n, v, dst[i]);
             else y[(size_t)m * N + n] = v;
@@ -604,6 +610,8 @@ __global__ void __launch_bounds__(32 * fsk::NW) k_mm_f16_sk(DevW W, ActQ A, int 
         const bool ok = n < N;
         cp_async16(sW + r * rh + b0 * 32 + c * 8, ok ? (const void*)(W.h + (size_t)n * K + b0 * 32 + c * 8) : (const void*)W.h, ok);
     }
+    const int n_out = n0 + tid / fsk::BM;
+    const float b_out = (bias && n_out < N) ? bias[n_out] : 0.0f;   // this thread's output's bias (a constant)
     pdl_wait();
     pdl_trigger();
     for (int i = lane; i < fsk::BM * cpr; i += 32) {
@@ -646,7 +654,7 @@ __global__ void __launch_bounds__(32 * fsk::NW) k_mm_f16_sk(DevW W, ActQ A, int 
 #pragma unroll 8
     for (int b = 0; b < nb; ++b) acc = __fadd_rn(acc, sS[b * (fsk::BN * fsk::BM) + tid]);
     if (n < N && m < M) {
-        float v = bias ? __fadd_rn(acc, bias[n]) : acc;
+        float v = bias ? __fadd_rn(acc, b_out) : acc;
         if (relu) v = (v > 0.0f) ? v : 0.0f;
         if (use_qkv) qkv_store(qkv, m, n, v);
         else y[(size_t)m * N + n] = v;

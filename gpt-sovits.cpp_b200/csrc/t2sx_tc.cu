@@ -383,6 +383,20 @@ k_mm_tc_q4k(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUt
             for (int c = 0; c < 16; ++c) { acc[c] = make_float2(0.0f, 0.0f); accm[c] = make_float2(0.0f, 0.0f); }
             float wd = nok ? W.d[(size_t)n * nsb] : 0.0f, wm = nok ? W.dmin[(size_t)n * nsb] : 0.0f;
             float xd = mok ? A.d[(size_t)mt * nsb] : 0.0f;
+            // for the epilogue, requested now so that the loads overlap the fold: this lane's bias
+            // and (QKV projection) the K/V cache offset of (page, layer, K, head 0, pos, dim 0) of
+            // tile row m0 + et, or -1
+            const float bn = (bias && nok) ? bias[n] : 0.0f;
+            const int et = tid - 32 * EPI_WARP0;   // 0..255
+            long long kv_row = -1;
+            if (use_qkv && et < BN && m0 + et < M) {
+                const int m = m0 + et;
+                const int pos = qkv.rows.pos[m], sl = qkv.rows.slot[m];
+                const int pg = min(max(pos, 0) / kPage, qkv.kv.max_pages - 1);
+                const int cap = qkv.rows.cap[sl];
+                const int page = qkv.kv.ptab[(size_t)sl * qkv.kv.max_pages + pg];
+                if (pos >= 0 && pos < cap) kv_row = (long long)kv_off(qkv.kv, page, qkv.layer, 0, 0, pos % kPage);
+            }
             for (int sb = 0; sb < nsb; ++sb, ++gsb) {
                 const float2 d2 = make_float2(wd, wd), ndm2 = make_float2(-wm, -wm);
                 __syncwarp();
@@ -440,7 +454,6 @@ k_mm_tc_q4k(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUt
             // read the tile before the tile is written again); K/V tiles go to each row's page
             // slot with 16-byte stores.  Every epilogue warp takes the same abort decision at the
             // first barrier.
-            const int et = tid - 32 * EPI_WARP0;   // 0..255
             if (tstore && et == 0) bulk_wait_read();
             aborted = epi_sync_or(aborted || *abort_flag);
             const float nan_v = __int_as_float(0x7FC00000);
@@ -448,7 +461,6 @@ k_mm_tc_q4k(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUt
             {
                 // acc + accm is never -0 (both chains start at +0), so adding a zero bias changes no value
                 const int col = quarter * 32 + lane;
-                const float bn = (bias && nok) ? bias[n] : 0.0f;
                 const float2 bn2 = make_float2(bn, bn);
                 float2 v2[16];
 #pragma unroll
@@ -472,19 +484,7 @@ k_mm_tc_q4k(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUt
                     }
                 }
             }
-            if (use_qkv && et < BN) {
-                // K/V cache element offset of (page, layer, K, head 0, pos, dim 0) for this row, or -1
-                long long off = -1;
-                const int m = m0 + et;
-                if (m < M) {
-                    const int pos = qkv.rows.pos[m], sl = qkv.rows.slot[m];
-                    if (pos >= 0 && pos < qkv.rows.cap[sl]) {
-                        const int page = qkv.kv.ptab[(size_t)sl * qkv.kv.max_pages + pos / kPage];
-                        off = (long long)kv_off(qkv.kv, page, qkv.layer, 0, 0, pos % kPage);
-                    }
-                }
-                kvb[et] = off;
-            }
+            if (use_qkv && et < BN) kvb[et] = kv_row;
             if (tstore) fence_proxy_async_smem();
             epi_sync();
             if (use_qkv && n0 >= kD) {
