@@ -240,21 +240,18 @@ constexpr int kSmallM = 32;
 
 // y = LN(a + b) * g + beta for one row held by one warp (ggml_norm + mul + add,
 // block.cpp:615-619 / :630-634): lane l sums elements l, l+32, ... in double, the lanes combine
-// by an xor butterfly.  `b_l2` reads b through L2 (written by other CTAs of the same kernel).
-__device__ void ln_row_warp(const float* __restrict__ a, const float* __restrict__ b, bool b_l2,
-                            const float* __restrict__ g, const float* __restrict__ beta, float eps, int lane,
+// by an xor butterfly.  This form takes the lane's elements of a, g and beta already loaded (av,
+// gv, bv: element lane + 32 t at t); `b_l2` reads b through L2 (written by other CTAs of the same
+// kernel).
+__device__ void ln_row_vals(const float (&av)[kD / 32], const float* __restrict__ b, bool b_l2,
+                            const float (&gv)[kD / 32], const float (&bv)[kD / 32], float eps, int lane,
                             float (&out)[kD / 32]) {
-    float v[kD / 32], gv[kD / 32], bv[kD / 32];
-#pragma unroll
-    for (int t = 0; t < kD / 32; ++t) {   // loaded with the row: one round trip, not one after the sums
-        gv[t] = g[lane + 32 * t];
-        bv[t] = beta[lane + 32 * t];
-    }
+    float v[kD / 32];
     double s = 0.0;
 #pragma unroll
     for (int t = 0; t < kD / 32; ++t) {
         const int i = lane + 32 * t;
-        v[t] = __fadd_rn(a[i], b_l2 ? __ldcg(b + i) : b[i]);
+        v[t] = __fadd_rn(av[t], b_l2 ? __ldcg(b + i) : b[i]);
         s = __dadd_rn(s, (double)v[t]);
     }
 #pragma unroll
@@ -274,6 +271,23 @@ __device__ void ln_row_warp(const float* __restrict__ a, const float* __restrict
     const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
 #pragma unroll
     for (int t = 0; t < kD / 32; ++t) out[t] = __fadd_rn(__fmul_rn(__fmul_rn(v[t], scale), gv[t]), bv[t]);
+}
+
+// The lane's elements of a 512-wide row.
+__device__ __forceinline__ void load_row_lane(const float* __restrict__ x, int lane, float (&v)[kD / 32]) {
+#pragma unroll
+    for (int t = 0; t < kD / 32; ++t) v[t] = x[lane + 32 * t];
+}
+
+// ln_row_vals with a, g and beta loaded here, with the row: one round trip, not one after the sums.
+__device__ void ln_row_warp(const float* __restrict__ a, const float* __restrict__ b, bool b_l2,
+                            const float* __restrict__ g, const float* __restrict__ beta, float eps, int lane,
+                            float (&out)[kD / 32]) {
+    float av[kD / 32], gv[kD / 32], bv[kD / 32];
+    load_row_lane(g, lane, gv);
+    load_row_lane(beta, lane, bv);
+    load_row_lane(a, lane, av);
+    ln_row_vals(av, b, b_l2, gv, bv, eps, lane, out);
 }
 
 // Work of the last CTA of a small-M matmul, once every CTA's output is written: residual +
@@ -626,16 +640,26 @@ __global__ void __launch_bounds__(128) k_mm_ln(DevW W, LnIn ln, int M, const flo
     }
     const bool own = row && lane < M;
     const float bv = (bias && own) ? bias[n] : 0.0f;
-    // weights and bias are constants: with a programmatic launch they are in flight while the
-    // preceding matmul finishes; everything below reads data of earlier kernels
+    // the norm's g, beta and residual row a (written two or more launches back), and the K/V
+    // cache slot of row `lane` (QKV projection above layer 0: rows placed two or more launches back)
+    float ag[kD / 32], gg[kD / 32], bg[kD / 32];
+    if (warp < M) {
+        load_row_lane(ln.g, lane, gg);
+        load_row_lane(ln.beta, lane, bg);
+        load_row_lane(ln.a + (size_t)warp * kD, lane, ag);
+    }
+    const bool kvcol = use_qkv && own && n >= kD;
+    const bool early_dst = kvcol && qkv.layer > 0;
+    int2 kdst = make_int2(-1, 0);
+    if (early_dst) kdst = qkv_dest(qkv, qkv.rows.pos[lane], qkv.rows.slot[lane]);
+    // weights, bias and those are in flight while the preceding matmul finishes (programmatic
+    // launch); below, the preceding kernel's output
     pdl_wait();
     pdl_trigger();
-    const bool kvcol = use_qkv && own && n >= kD;
-    int kpos = 0, kslot = 0;
-    if (kvcol) { kpos = qkv.rows.pos[lane]; kslot = qkv.rows.slot[lane]; }
+    if (kvcol && !early_dst) kdst = qkv_dest(qkv, qkv.rows.pos[lane], qkv.rows.slot[lane]);
     if (warp < M) {
         float o[kD / 32];
-        ln_row_warp(ln.a + (size_t)warp * kD, ln.b + (size_t)warp * kD, true, ln.g, ln.beta, ln.eps, lane, o);
+        ln_row_vals(ag, ln.b + (size_t)warp * kD, true, gg, bg, ln.eps, lane, o);
         if (blockIdx.x == 0) {
 #pragma unroll
             for (int t = 0; t < kD / 32; ++t) ln.y_out[(size_t)warp * kD + lane + 32 * t] = o[t];
@@ -661,7 +685,7 @@ __global__ void __launch_bounds__(128) k_mm_ln(DevW W, LnIn ln, int M, const flo
 #pragma unroll
         for (int b = 0; b < nb; ++b) acc = __fmaf_rn(s_dd[warp][m][b], (float)s_a[warp][m][b], acc);
         const float v_ = epi_v(acc, bias != nullptr, bv, relu);
-        if (use_qkv) qkv_store_at(qkv, m, n, v_, kvcol ? qkv_dest(qkv, kpos, kslot) : make_int2(-1, 0));
+        if (use_qkv) qkv_store_at(qkv, m, n, v_, kdst);
         else y[(size_t)m * W.N + n] = v_;
     }
 }
@@ -1471,18 +1495,28 @@ void attention_decode(int T, const uint16_t* q16, Rows rows, KVView kv, int laye
     }
 }
 
-// y = LN(a + b) * g + beta, one warp per row (ln_row_warp); the row is also written in the next
-// matmul's dot type when qtype >= 0.
+// y = LN(a + b) * g + beta, one warp per row (ln_row_vals); the row is also written in the next
+// matmul's dot type when qtype >= 0.  a must have been written two or more launches back: it is
+// read before the programmatic wait.
 __global__ void k_residual_ln(int T, const float* __restrict__ a, const float* __restrict__ b,
                               const float* __restrict__ g, const float* __restrict__ beta, float eps,
                               float* __restrict__ y, int qtype, ActQ qo) {
-    pdl_wait();
-    pdl_trigger();
     const int lane = threadIdx.x & 31;
     const int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-    if (r >= T) return;
+    // before the wait: g, beta and the residual rows a (callers' residuals are written two or
+    // more launches back; b is the preceding matmul's output)
+    float av[kD / 32], gv[kD / 32], bv[kD / 32];
+    const bool live = r < T;
+    if (live) {
+        load_row_lane(g, lane, gv);
+        load_row_lane(beta, lane, bv);
+        load_row_lane(a + (size_t)r * kD, lane, av);
+    }
+    pdl_wait();
+    pdl_trigger();
+    if (!live) return;
     float out[kD / 32];
-    ln_row_warp(a + (size_t)r * kD, b + (size_t)r * kD, false, g, beta, eps, lane, out);
+    ln_row_vals(av, b + (size_t)r * kD, false, gv, bv, eps, lane, out);
 #pragma unroll
     for (int t = 0; t < kD / 32; ++t) y[(size_t)r * kD + lane + 32 * t] = out[t];
     quant_row512_strided(out, lane, qtype, qo, (size_t)r);

@@ -230,6 +230,8 @@ void attention_decode(int T, const uint16_t* q16, Rows rows, KVView kv, int laye
                       ActQ qo, cudaStream_t st);
 void attention_rows(int T, int row0, const int2* groups, int n_groups, const uint16_t* q16, Rows rows, KVView kv, int layer,
                     float scale, float* out, int qtype, ActQ qo, cudaStream_t st);
+// y = LN(a + b) * g + beta over T rows of kD (and y in dot type qtype into qo).  With a programmatic
+// launch a is read before the wait: it must have been written two or more launches back.
 void residual_layernorm(int T, const float* a, const float* b, const float* g, const float* beta, float eps,
                         float* y, int qtype, ActQ qo, cudaStream_t st);
 // Logit given to EOS when EOS is masked (finite, so the masked-lerp filters stay finite).
