@@ -1025,8 +1025,6 @@ __device__ __forceinline__ void attn_finish(AttnState& st, int r, int hg, int wa
 template <int HPC, bool PIPE, bool PF = false>
 __global__ void __launch_bounds__(32 * HPC) k_attn_decode(const uint16_t* __restrict__ q16, Rows rows, KVView kv, int layer,
                                                           float scale, float* __restrict__ out, int qtype, ActQ qo) {
-    pdl_wait();
-    pdl_trigger();
     __shared__ AbsMax s_am[8];
     __shared__ float s_is;
     // CTAs in (row, head group) order, head group fastest: the CTAs of one row run together and
@@ -1035,8 +1033,11 @@ __global__ void __launch_bounds__(32 * HPC) k_attn_decode(const uint16_t* __rest
     const int warp = threadIdx.x >> 5;
     const int h = hg * HPC + warp;
     const int lane = threadIdx.x & 31;
+    // the row's slot and length were written two or more launches back (read before the wait)
     const int s = rows.slot[r];
     const int L = rows.L[r];
+    pdl_wait();
+    pdl_trigger();
     uint32_t q[kHeadDim / 2];   // the f16 query as packed pairs (the score's mixed-precision fma chain)
     load_row32_h(q16 + (size_t)r * kD + h * kHeadDim, q);
     AttnState st;
