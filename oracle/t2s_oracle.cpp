@@ -680,7 +680,7 @@ void orc_attn_decode(const float* q, const uint16_t* k, const uint16_t* v, int L
     attn_decode_head(qh, k, v, L, 32, out);
 }
 // Batched attention rows (the per-head functions above, positions strided by 16 heads x 32 dims).
-// Used for batched-attention shapes (SURVEY config 3: attention over a paged f16 cache).
+// Used for batched-attention shapes (many sessions attending over a paged f16 cache).
 void orc_attn_rows(int n, const int* seqs, const int* lens, const uint16_t* q16, const uint16_t* k,
                    const uint16_t* v, int max_len, float* out) {
 #pragma omp parallel for schedule(dynamic, 4)

@@ -3,7 +3,7 @@ CPU operator definitions (the oracle's ggml-order mode: generic vec_dot folds, s
 LayerNorm sums, per-query flash attention with an f16 V accumulator, libm expf), on the 24-layer
 model with the one-session workload's prompt, teacher-forced (both fed the canonical tokens).
 
-* F16 weights (convert_t2s_to_gguf.py's default output type): logits agree within the north-star
+* F16 weights (convert_t2s_to_gguf.py's default output type): logits agree within the stated
   tolerance, |a - b| <= 1e-2 + 1e-3 |b|, with an F16 and with an F32 KV cache, and every greedy
   token agrees.
 * Q8_0 weights: activations are quantised to Q8_0 before every matmul, so a one-ulp change of an
@@ -29,7 +29,7 @@ def _gap(path, steps):
     return gap_report.measure(path, lengths, steps, free_running=False), gap_report.ulp_sensitivity(path, lengths)
 
 
-def test_f16_weights_within_north_star_tolerance(orc):
+def test_f16_weights_within_logit_tolerance(orc):
     import synth
     r, _ = _gap(synth.ensure_gguf("f16", 0, n_layer=24), STEPS)
     for mode in ("ggml16", "ggml32"):
