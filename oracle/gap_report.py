@@ -3,11 +3,11 @@ from ggml's CPU operator definitions -- TEST INFRASTRUCTURE ONLY.
 
 Three oracle sessions run the same prompts:
   canon  : the canonical order (GPU == canon, bit for bit, checked by the -m gpu tests);
-  ggml16 : ggml's CPU operator definitions with an F16 KV cache (the north-star cache type);
+  ggml16 : ggml's CPU operator definitions with an F16 KV cache (the cache type this path keeps);
   ggml32 : the same with an F32 KV cache (the reference's default kv_cache_type).
 Teacher-forced: every session is fed canon's greedy tokens, so each step compares logits of the
 same inputs: the max abs difference, the largest |a - b| / (1e-2 + 1e-3 |b|) (at most 1 when the
-north-star tolerance of 1e-2 absolute plus 1e-3 relative holds), argmax agreement with EOS
+logit tolerance of 1e-2 absolute plus 1e-3 relative holds), argmax agreement with EOS
 masked, and at each disagreement the top1 - top2 margin of canon's logits.  Free-running: ggml16
 decodes its own greedy tokens; the first step where its stream leaves canon's is reported.
 Sensitivity: canon itself is run again on inputs with a one-ulp change in 1% of the prefill

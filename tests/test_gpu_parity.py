@@ -1,7 +1,7 @@
 """GPU parity: libt2sx (through its C ABI) against the CPU oracle, bit for bit.
 
 Every kernel reproduces the oracle's evaluation order, so the comparisons below are exact
-(array_equal on the raw bits), well inside the north-star tolerance for logits (1e-2 abs /
+(array_equal on the raw bits), well inside the logit tolerance (1e-2 abs /
 1e-3 rel), and greedy token streams must be identical.
 """
 import os

@@ -11,7 +11,7 @@ The CPU test builds the binaries into tests/cpp/_ref_bin (only where the referen
 present; nothing is copied from them).  The GPU test runs those binaries on synthetic GGUF files
 of the reference's model shapes: every loader test passes, and in the infer suite the three
 F16-KV configurations pass (prefill, 200 stochastic decode steps, token checks) while the nine
-others fail at t2s_session_init, which refuses KV types other than F16 (the north star fixes an
+others fail at t2s_session_init, which refuses KV types other than F16 (this path keeps an
 f16 cache).
 """
 import os
